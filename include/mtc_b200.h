@@ -1,0 +1,177 @@
+/*
+ * mtc_b200.h -- C ABI of the B200 (sm_100a) packed-quadtree MTC GEMM library.
+ *
+ * The reference (Sharexi/TensorPack, "MTC") is a Python + Numba package; its
+ * hot path is the packed GEMM `mtc.kernels.gemm.mtc_gemm` over an `MTCMatrix`
+ * (mtc/kernels/gemm.py:217-574).  This header is the native boundary a
+ * Python caller binds with ctypes: plain pointers, sizes
+ * and a CUDA stream handle passed as `void*`; no C++ or torch types.
+ *
+ * Conventions
+ *  - Every entry point returns MTC_OK (0) or a negative MTC_ERR_* code and
+ *    never exits or aborts.  `mtc_last_error()` returns the message of the
+ *    most recent failure on the calling thread.
+ *  - All array arguments are device pointers unless noted "host".
+ *  - W is the K x N weight (in_features x out_features, reduction along the
+ *    rows, mtc/core/allocation.py:8-10).  The device stream stores the
+ *    PERMUTED matrix Wp = W[row_perm][:, col_perm] (mtc/core/permutation.py:
+ *    15-21); row_perm / col_perm may be NULL for an unpermuted matrix.
+ *  - Calls enqueue work on `stream` and do not synchronise, except
+ *    mtc_repack_plan which reads back one 8-byte total.
+ *  - The library holds no global mutable state: concurrent calls on
+ *    different streams with different buffers are independent.
+ */
+#ifndef MTC_B200_H
+#define MTC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MTC_API __attribute__((visibility("default")))
+#else
+#define MTC_API
+#endif
+
+#define MTC_ABI_VERSION 1
+
+enum {
+  MTC_OK = 0,
+  MTC_ERR_INVALID = -1,     /* bad argument (shape, pointer, alignment, size)  */
+  MTC_ERR_CUDA = -2,        /* a CUDA runtime call failed                      */
+  MTC_ERR_WORKSPACE = -3,   /* caller-provided workspace too small             */
+  MTC_ERR_UNSUPPORTED = -4  /* valid request this build does not handle        */
+};
+
+/* Device status word bits (written by kernels, read by the host after sync). */
+enum {
+  MTC_STATUS_TIMEOUT = 1u,       /* a bounded pipeline wait gave up           */
+  MTC_STATUS_X_RANGE = 2u,       /* |x| beyond the fp16 range of the tensor path */
+  MTC_STATUS_BAD_STREAM = 4u     /* a tile record failed a bounds check       */
+};
+
+/* One quadtree leaf as handed to the GPU repack (host builds, device reads).
+ * Leaves are grouped by 32x32 tile (tile-major, grid order kt*tn+nt) and
+ * sorted by Z-order inside each tile; `z0` is the Z index of the leaf's first
+ * 4x4 micro-block inside its tile (0..63), `size` its edge (4, 8, 16 or 32).
+ * `arena_off` is the byte offset of the leaf payload in the reference-layout
+ * arena: m*size*size/8 bytes, codes row-major in the leaf, LSB-first m-bit
+ * two's-complement fields (mtc/kernels/gemm.py:457-478).  P0 leaves carry no
+ * payload.  `scale_bits` holds the raw fp32 bits of the (signed) leaf scale;
+ * quadtree allocations use bf16-exact scales (mtc/core/allocation.py:97-103,
+ * mtc/core/quadtree.py:84), fixed-block ones may use any fp32 scale
+ * (allocation.py:197). */
+typedef struct mtc_leaf_in {
+  uint32_t arena_off;
+  uint32_t scale_bits;
+  uint8_t mode;   /* 0, 2, 3, 4, 5, 6, 8 or 16 */
+  uint8_t z0;
+  uint8_t size;
+  uint8_t pad_;
+} mtc_leaf_in;
+
+/* 16-byte tile descriptor of the device stream, one per 32x32 tile, indexed
+ * kt*tn + nt.  The tile record at `record_off` is
+ *   [leaf table: n_leaves x scale_words u32, padded to 16 B]
+ *   [primary code planes: prim_bytes, padded to 16 B]
+ *   [secondary code planes, padded to 16 B]
+ * Leaf-table entry: bits 0-4 mode, 8-11 primary bytes per micro-block / 4,
+ * 12-13 secondary bytes per micro-block / 2, 14 fp32-conversion flag,
+ * 16-31 bf16 scale bits; with scale_words == 2 a second word holds the fp32
+ * scale (matrices whose scales are not all bf16-exact).  `leaf_start` has
+ * bit z set when a leaf starts at
+ * micro-block z (Z order), so popc(leaf_start & ((2<<z)-1)) - 1 is the leaf
+ * of micro-block z. */
+typedef struct mtc_tile_desc {
+  uint32_t record_off;
+  uint16_t n_leaves;
+  uint16_t prim_bytes;
+  uint64_t leaf_start;
+} mtc_tile_desc;
+
+/* Device-resident tile stream of one packed matrix (all pointers device). */
+typedef struct mtc_stream_desc {
+  const uint8_t* records;        /* tile records, band-major: [band][kt][tile in band] */
+  const mtc_tile_desc* tiles;    /* [tk * tn] */
+  const uint32_t* row_off;       /* [n_bands * (tk + 1)] byte offset of each k-tile row of a band */
+  int32_t K, N;                  /* logical shape of W */
+  int32_t tk, tn;                /* 32x32 tiles along K and N (padded up) */
+  int32_t band_tiles;            /* tiles per column band (8 = 256 output features) */
+  int32_t exp2;                  /* fp16 tensor path computes with W * 2^exp2 */
+  uint64_t record_bytes;         /* total bytes of `records` */
+  uint32_t max_row_bytes;        /* largest k-tile row of any band */
+  int32_t scale_words;           /* 1: bf16 scale in the entry, 2: extra fp32 scale word */
+} mtc_stream_desc;
+
+MTC_API int mtc_abi_version(void);
+MTC_API const char* mtc_last_error(void);
+MTC_API int mtc_device_sm_count(int device);
+
+/* Repack step 1 (replaces the per-block offset computation of
+ * MTCMatrix.from_allocation, mtc/kernels/gemm.py:449-454): measures every
+ * tile record, lays the records out band-major, fills `tiles`
+ * (all fields) and `row_off`, and writes out_host[0] = total record bytes and
+ * out_host[1] = the largest k-tile row of any band (host array of two;
+ * synchronises `stream`).  `tile_leaf_begin` is the [tk*tn + 1] CSR of
+ * `leaves`; `scratch_u32` is device scratch of at least tk*tn + 6 words.
+ * Fails with MTC_ERR_INVALID when the leaves of a tile do not cover its 64
+ * micro-blocks exactly once in Z order. */
+MTC_API int mtc_repack_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf_begin, int32_t tk,
+                    int32_t tn, int32_t band_tiles, int32_t scale_words, mtc_tile_desc* tiles,
+                    uint32_t* row_off, uint32_t* scratch_u32, uint64_t* out_host, void* stream);
+
+/* Repack step 2: transcodes every leaf's reference-layout codes
+ * (mtc/kernels/gemm.py:457-478) from `arena` into the tile records
+ * (4x4 micro-blocks in Z order, bit-plane split, fragment order).
+ * `s` must carry the tiles / row_off filled by mtc_repack_plan and the
+ * chosen exp2; `scratch_u32` is one device word.  Synchronises `stream`. */
+MTC_API int mtc_repack_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc_leaf_in* leaves,
+                    const uint32_t* tile_leaf_begin, const mtc_stream_desc* s, uint8_t* records,
+                    uint32_t* scratch_u32, void* stream);
+
+/* Exact dequantisation (replaces MTCMatrix.to_array, gemm.py:510-538, and
+ * qt_dequant / permuted_qt_dequant, quadtree.py:157-171, permutation.py:
+ * 76-79): out = q * scale in fp32 (__fmul_rn), bit-identical to the
+ * reference.  With row_perm/col_perm non-NULL, element (k, n) of the stored
+ * matrix lands at out[row_perm[k]][col_perm[n]] (original order).  `ldo` is
+ * the row stride of `out` in elements. */
+MTC_API int mtc_dequant(const mtc_stream_desc* s, const int32_t* row_perm, const int32_t* col_perm,
+                float* out, int64_t ldo, void* stream);
+
+/* Split-K streaming GEMM for M <= 16 (decode): Y[:, col_perm] =
+ * X[:, row_perm] @ Wp (replaces mtc_gemm, gemm.py:541-574, and the
+ * gather/GEMM/scatter of permutation.py:15-21).  X is M x K fp32 (row
+ * stride ldx), Y is M x N fp32 (row stride ldy).  fp16 operands on the
+ * tensor cores, fp32 accumulation.  `ws` / `ws_bytes` is scratch for the
+ * split-K partial sums (size from mtc_gemv_workspace_bytes); `counters`
+ * points at n_bands u32 that are zero before the first call and are left
+ * zero by every successful call.  `status` (nullable) receives MTC_STATUS_*
+ * bits. */
+MTC_API size_t mtc_gemv_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t rows_per_unit);
+MTC_API int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+             const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
+             int32_t rows_per_unit, void* ws, size_t ws_bytes, uint32_t* counters,
+             uint32_t* status, void* stream);
+
+/* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
+ * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,
+ * gemm.py:541-574, and permutation.py:15-21).  Takes the INVERSE column
+ * permutation (col_perm_inv[col_perm[n]] = n, NULL when unpermuted).  fp16
+ * operands, fp32 TMEM accumulation.  `ws` (256-byte aligned) holds the fp16
+ * gathered activations and, for permuted matrices, the permuted output; its
+ * size comes from mtc_prefill_workspace_bytes(s, M, col_perm_inv != NULL).
+ * Requires K, N <= 51200. */
+MTC_API size_t mtc_prefill_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t permuted);
+MTC_API int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                             const int32_t* row_perm, const int32_t* col_perm_inv, float* Y,
+                             int64_t ldy, void* ws, size_t ws_bytes, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MTC_B200_H */

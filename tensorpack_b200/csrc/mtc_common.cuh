@@ -1,0 +1,422 @@
+// Device-side helpers shared by the MTC kernels: the tile-stream format,
+// micro-block decoders, and thin PTX wrappers (mbarrier, bulk copies, mma).
+//
+// Tile stream format (all kernels agree on it; the repack writes it):
+//   * W (stored permuted, K x N) is cut into 32x32 tiles, each tile into an
+//     8x8 grid of 4x4 micro-blocks (mb).  Micro-blocks are numbered in Z
+//     order: z = i2 j2 i1 j1 i0 j0 (i = mb row, j = mb column, bit 2 first),
+//     so every quadtree leaf (edge 4..32, aligned) is a contiguous z range.
+//   * Codes are stored biased, u = q + 2^(m-1), split into a primary plane of
+//     width wp and a secondary plane of width ws:  P2 (2,0) P3 (2,1)
+//     P4 (4,0) P5 (4,1) P6 (4,2) P8 (8,0); P16 keeps signed int16 codes.
+//   * An mb is read as two halves h = 0, 1 (mb columns 2h and 2h+1); a half
+//     holds four code pairs j = 0..3: pair j = (column 2h + (j>>1),
+//     rows 2(j&1) and 2(j&1)+1) as (lo, hi).  Plane layouts per mb:
+//       width 1 (2 B):  code (h, j, lo/hi) at bit 4h + j + 8*hi
+//       width 2 (4 B):  code (h, j, lo/hi) at bit 8h + 2j + 16*hi
+//       width 4 (8 B):  word h, code (j, lo/hi) at bit 4(j&1) + 8(j>>1) + 16*hi
+//       width 8 (16 B): half h = 2 words, word j>>1, byte (j&1) + 2*hi
+//       P16   (32 B):   half h = 4 words, word j = lo16 | hi16 << 16 (signed)
+//     These positions let one LOP3 against 0x6400 (fp16 1024.0) produce two
+//     fp16 values (1024 + 2^p u) that one HFMA2 turns into exact codes.
+//   * Primary planes of the tile's mbs are concatenated in z order, then the
+//     secondary planes; offsets are prefix sums over z (computed in-kernel).
+//     Primary offsets are multiples of 4 bytes, secondary offsets multiples
+//     of 2, so secondary planes are read in 16-bit units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mtc_b200.h"
+
+namespace mtc {
+
+constexpr int kTile = 32;
+constexpr int kMbPerTile = 64;
+constexpr uint32_t kMagic = 0x64006400u;  // two fp16 1024.0
+
+__host__ __device__ constexpr int pad16(int x) { return (x + 15) & ~15; }
+
+// Primary / secondary plane bytes per micro-block for each mode.
+__host__ __device__ inline int mb_prim_bytes(int m) {
+  switch (m) {
+    case 2: case 3: return 4;
+    case 4: case 5: case 6: return 8;
+    case 8: return 16;
+    case 16: return 32;
+    default: return 0;
+  }
+}
+__host__ __device__ inline int mb_sec_bytes(int m) {
+  switch (m) {
+    case 3: case 5: return 2;
+    case 6: return 4;
+    default: return 0;
+  }
+}
+__host__ __device__ inline int prim_width(int m) {
+  switch (m) {
+    case 2: case 3: return 2;
+    case 4: case 5: case 6: return 4;
+    case 8: return 8;
+    case 16: return 16;
+    default: return 0;
+  }
+}
+
+// Leaf-table entry fields.
+__device__ __forceinline__ int lt_mode(uint32_t e) { return e & 31u; }
+__device__ __forceinline__ int lt_prim(uint32_t e) { return ((e >> 8) & 15u) * 4; }
+__device__ __forceinline__ int lt_sec(uint32_t e) { return ((e >> 12) & 3u) * 2; }
+__device__ __forceinline__ bool lt_slow(uint32_t e) { return (e >> 14) & 1u; }
+__device__ __forceinline__ float lt_scale(uint32_t e) { return __uint_as_float(e & 0xffff0000u); }
+// Leaf-table entry and scale of leaf L (sw = scale words per leaf, 1 or 2).
+__device__ __forceinline__ uint32_t lt_entry(const uint32_t* ltab, int L, int sw) { return ltab[L * sw]; }
+__device__ __forceinline__ float lt_scale_of(const uint32_t* ltab, int L, int sw) {
+  return sw == 2 ? __uint_as_float(ltab[2 * L + 1]) : lt_scale(ltab[L]);
+}
+
+// Z order <-> (mb row, mb column) inside a tile.
+__host__ __device__ inline int z_of(int i, int j) {
+  return ((i >> 2) & 1) << 5 | ((j >> 2) & 1) << 4 | ((i >> 1) & 1) << 3 | ((j >> 1) & 1) << 2 |
+         (i & 1) << 1 | (j & 1);
+}
+__host__ __device__ inline int z_row(int z) {
+  return ((z >> 5) & 1) << 2 | ((z >> 3) & 1) << 1 | ((z >> 1) & 1);
+}
+__host__ __device__ inline int z_col(int z) {
+  return ((z >> 4) & 1) << 2 | ((z >> 2) & 1) << 1 | (z & 1);
+}
+
+// Leaf index of micro-block z given the tile's leaf-start mask.
+__device__ __forceinline__ int leaf_of(uint64_t start, int z) {
+  uint64_t m = (z >= 63) ? ~0ull : ((2ull << z) - 1ull);
+  return __popcll(start & m) - 1;
+}
+
+// ---------------------------------------------------------------------------
+// Code extraction helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t lop_or(uint32_t x, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(x), "r"(mask), "r"(kMagic));
+  return r;
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__host__ __device__ constexpr uint32_t h2const(uint16_t bits) {
+  return (uint32_t)bits | ((uint32_t)bits << 16);
+}
+
+// fp16 bit pattern of an exactly representable normal (or zero) value,
+// evaluated at compile time for the decoder constants.
+__host__ __device__ constexpr uint16_t f16_bits(double v) {
+  uint16_t sign = v < 0 ? 0x8000u : 0u;
+  double a = v < 0 ? -v : v;
+  if (a == 0.0) return sign;
+  int e = 0;
+  while (a >= 2.0) { a /= 2.0; ++e; }
+  while (a < 1.0) { a *= 2.0; --e; }
+  return (uint16_t)(sign | (uint16_t)((e + 15) << 10) | (uint16_t)((a - 1.0) * 1024.0));
+}
+__host__ __device__ constexpr uint32_t k2(double v) { return h2const(f16_bits(v)); }
+
+// Load helpers (generic pointers into shared or global memory).
+__device__ __forceinline__ uint32_t ld32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t ld16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// Pair decoders: each returns two exact fp16 codes (lo row, hi row).
+// A field of a p-bit position inside each 16-bit half, OR-ed into 1024.0,
+// reads 1024 + 2^p u; scaling by 2^-p and subtracting 1024 2^-p + bias is
+// exact because every intermediate is a small integer.
+template <int J>
+__device__ __forceinline__ uint32_t pair_p2(uint32_t v) {  // v = plane word >> 8h
+  constexpr double c = 1.0 / double(1 << (2 * J));
+  return hfma2u(lop_or(v, 0x00030003u << (2 * J)), k2(c), k2(-1024.0 * c - 2.0));
+}
+template <int J>
+__device__ __forceinline__ uint32_t nib_field(uint32_t w) {  // P4-style nibble plane word
+  return lop_or((J >> 1) ? (w >> 8) : w, (J & 1) ? 0x00F000F0u : 0x000F000Fu);
+}
+template <int J>
+__device__ __forceinline__ uint32_t pair_p4(uint32_t w) {
+  constexpr double c = (J & 1) ? 1.0 / 16.0 : 1.0;
+  return hfma2u(nib_field<J>(w), k2(c), k2(-1024.0 * c - 8.0));
+}
+template <int J>
+__device__ __forceinline__ uint32_t pair_p8(uint32_t w0, uint32_t w1) {
+  uint32_t w = (J >> 1) ? w1 : w0;
+  return hfma2u(lop_or((J & 1) ? (w >> 8) : w, 0x00FF00FFu), k2(1.0), k2(-1152.0));
+}
+// P3: primary crumb plane (u & 3) + bit plane (u >> 2); v1 = bit plane >> 4h.
+template <int J>
+__device__ __forceinline__ uint32_t pair_p3(uint32_t v, uint32_t v1) {
+  constexpr double c2 = 1.0 / double(1 << (2 * J));
+  constexpr double c1 = 4.0 / double(1 << J);
+  uint32_t inner = hfma2u(lop_or(v1, 0x00010001u << J), k2(c1), k2(-1024.0 * c1 - 4.0 - 1024.0 * c2));
+  return hfma2u(lop_or(v, 0x00030003u << (2 * J)), k2(c2), inner);
+}
+// P5: nibble plane + bit plane (u >> 4); P6: nibble plane + crumb plane (u >> 4).
+template <int MODE, int J>
+__device__ __forceinline__ uint32_t pair_p56(uint32_t w, uint32_t vs) {
+  constexpr double c4 = (J & 1) ? 1.0 / 16.0 : 1.0;
+  constexpr double bias = (MODE == 5) ? 16.0 : 32.0;
+  constexpr double cs = (MODE == 5) ? 16.0 / double(1 << J) : 16.0 / double(1 << (2 * J));
+  constexpr uint32_t mask = (MODE == 5) ? (0x00010001u << J) : (0x00030003u << (2 * J));
+  uint32_t inner = hfma2u(lop_or(vs, mask), k2(cs), k2(-1024.0 * cs - bias - 1024.0 * c4));
+  return hfma2u(nib_field<J>(w), k2(c4), inner);
+}
+
+// Decode one half micro-block into four fp16x2 registers holding the exact
+// codes q (pairs j = 0..3), for every mode except P16 and P0.
+// prim/sec point at this mb's primary / secondary plane bytes.
+__device__ __forceinline__ void decode_half_codes(int mode, const uint8_t* prim, const uint8_t* sec,
+                                                  int h, uint32_t q[4]) {
+  switch (mode) {
+    case 2: {
+      uint32_t v = ld32(prim) >> (8 * h);
+      q[0] = pair_p2<0>(v); q[1] = pair_p2<1>(v); q[2] = pair_p2<2>(v); q[3] = pair_p2<3>(v);
+      break;
+    }
+    case 4: {
+      uint32_t w = ld32(prim + 4 * h);
+      q[0] = pair_p4<0>(w); q[1] = pair_p4<1>(w); q[2] = pair_p4<2>(w); q[3] = pair_p4<3>(w);
+      break;
+    }
+    case 8: {
+      uint32_t w0 = ld32(prim + 8 * h), w1 = ld32(prim + 8 * h + 4);
+      q[0] = pair_p8<0>(w0, w1); q[1] = pair_p8<1>(w0, w1);
+      q[2] = pair_p8<2>(w0, w1); q[3] = pair_p8<3>(w0, w1);
+      break;
+    }
+    case 3: {
+      uint32_t v = ld32(prim) >> (8 * h);
+      uint32_t v1 = __byte_perm(ld16(sec), 0u, 0x4140) >> (4 * h);
+      q[0] = pair_p3<0>(v, v1); q[1] = pair_p3<1>(v, v1);
+      q[2] = pair_p3<2>(v, v1); q[3] = pair_p3<3>(v, v1);
+      break;
+    }
+    case 5: {
+      uint32_t w = ld32(prim + 4 * h);
+      uint32_t vs = __byte_perm(ld16(sec), 0u, 0x4140) >> (4 * h);
+      q[0] = pair_p56<5, 0>(w, vs); q[1] = pair_p56<5, 1>(w, vs);
+      q[2] = pair_p56<5, 2>(w, vs); q[3] = pair_p56<5, 3>(w, vs);
+      break;
+    }
+    case 6: {
+      uint32_t w = ld32(prim + 4 * h);
+      uint32_t vs = (ld16(sec) | (ld16(sec + 2) << 16)) >> (8 * h);
+      q[0] = pair_p56<6, 0>(w, vs); q[1] = pair_p56<6, 1>(w, vs);
+      q[2] = pair_p56<6, 2>(w, vs); q[3] = pair_p56<6, 3>(w, vs);
+      break;
+    }
+    default:
+      q[0] = q[1] = q[2] = q[3] = 0u;
+  }
+}
+
+// Integer codes of one half micro-block (exact path used by the dequant
+// kernel and the repack self-check): code[2j + hi].
+__device__ __forceinline__ void decode_half_int(int mode, const uint8_t* prim, const uint8_t* sec,
+                                                int h, int code[8]) {
+  if (mode == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) code[i] = 0;
+    return;
+  }
+  if (mode == 16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w = ld32(prim + 16 * h + 4 * j);
+      code[2 * j] = (int)(int16_t)(w & 0xffffu);
+      code[2 * j + 1] = (int)(int16_t)(w >> 16);
+    }
+    return;
+  }
+  const int wp = prim_width(mode);
+  const int bias = 1 << (mode - 1);
+  uint32_t pw0 = 0, pw1 = 0, sv = 0;
+  if (wp == 2) pw0 = ld32(prim);
+  if (wp == 4) pw0 = ld32(prim + 4 * h);
+  if (wp == 8) { pw0 = ld32(prim + 8 * h); pw1 = ld32(prim + 8 * h + 4); }
+  if (mode == 3 || mode == 5) sv = ld16(sec);
+  if (mode == 6) sv = ld16(sec) | (ld16(sec + 2) << 16);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+      uint32_t u = 0;
+      if (wp == 2) u = (pw0 >> (8 * h + 2 * j + 16 * hi)) & 3u;
+      if (wp == 4) u = (pw0 >> (4 * (j & 1) + 8 * (j >> 1) + 16 * hi)) & 15u;
+      if (wp == 8) u = (((j >> 1) ? pw1 : pw0) >> (8 * ((j & 1) + 2 * hi))) & 255u;
+      if (mode == 3) u |= ((sv >> (4 * h + j + 8 * hi)) & 1u) << 2;
+      if (mode == 5) u |= ((sv >> (4 * h + j + 8 * hi)) & 1u) << 4;
+      if (mode == 6) u |= ((sv >> (8 * h + 2 * j + 16 * hi)) & 3u) << 4;
+      code[2 * j + hi] = (int)u - bias;
+    }
+  }
+}
+
+// fp16 weights W*2^e of one half micro-block as four f16x2 registers:
+// pair j = (row lo, row hi) of column 2h + (j>>1).
+__device__ __forceinline__ void decode_half_w16(uint32_t entry, float scale, const uint8_t* prim,
+                                                const uint8_t* sec, int h, float pow2e, uint32_t r[4]) {
+  const int mode = lt_mode(entry);
+  if (mode == 0) {
+    r[0] = r[1] = r[2] = r[3] = 0u;
+    return;
+  }
+  if (mode == 16 || lt_slow(entry)) {
+    int code[8];
+    decode_half_int(mode, prim, sec, h, code);
+    const float s = scale * pow2e;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 v = __floats2half2_rn(__fmul_rn((float)code[2 * j], s), __fmul_rn((float)code[2 * j + 1], s));
+      r[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return;
+  }
+  uint32_t q[4];
+  decode_half_codes(mode, prim, sec, h, q);
+  __half s16 = __float2half_rn(scale * pow2e);
+  const uint32_t s2 = h2const(*reinterpret_cast<uint16_t*>(&s16));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r[j] = hmul2u(q[j], s2);
+}
+
+// Decode, for one tile record, the aligned 2x2 micro-block group owned by
+// this lane into fp16 (W * 2^e) pairs.  All 32 lanes of the warp must call
+// it together (it scans group sizes with shuffles).  Lane (g, t) =
+// (lane >> 2, lane & 3) owns group (t, jj = g >> 1) and column half h = g & 1;
+// R[k] (k = 2 di + dj) is micro-block (2t + di, 2jj + dj), pairs j = 0..3 as
+// in decode_half_w16.
+__device__ __forceinline__ int group_of_lane(int lane) {
+  const int t = lane & 3, jj = lane >> 3;
+  return ((t >> 1) << 3) | ((jj >> 1) << 2) | ((t & 1) << 1) | (jj & 1);
+}
+
+__device__ __forceinline__ void decode_group_w16(const uint8_t* rec, uint16_t n_leaves, uint16_t prim_bytes,
+                                                 uint64_t leaf_start, int sw, int lane, float pow2e,
+                                                 uint32_t R[4][4]) {
+  const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
+  const uint8_t* prim_base = rec + pad16(4 * sw * n_leaves);
+  const uint8_t* sec_base = prim_base + pad16(prim_bytes);
+  const int G = group_of_lane(lane);
+  const int z0 = 4 * G;
+  const int h = (lane >> 2) & 1;
+  uint32_t e[4];
+  float sc[4];
+  const int l0 = leaf_of(leaf_start, z0);
+  if (((leaf_start >> (z0 + 1)) & 7ull) == 0ull) {
+    e[0] = e[1] = e[2] = e[3] = lt_entry(ltab, l0, sw);
+    sc[0] = sc[1] = sc[2] = sc[3] = lt_scale_of(ltab, l0, sw);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      e[k] = lt_entry(ltab, l0 + k, sw);
+      sc[k] = lt_scale_of(ltab, l0 + k, sw);
+    }
+  }
+  uint32_t v = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v += (uint32_t)lt_prim(e[k]) | ((uint32_t)lt_sec(e[k]) << 16);
+  // exclusive scan of group sizes over the 16 groups in Z order; the group
+  // G' is held (with h = 0) by lane 8 * jj' + t'.
+  uint32_t incl = v;
+#pragma unroll
+  for (int dl = 1; dl < 16; dl <<= 1) {
+    const int Gs = G - dl;
+    const int ts = ((Gs >> 3) & 1) << 1 | ((Gs >> 1) & 1);
+    const int js = ((Gs >> 2) & 1) << 1 | (Gs & 1);
+    const int src = (Gs >= 0) ? (8 * js + ts) : lane;
+    const uint32_t u = __shfl_sync(0xffffffffu, incl, src);
+    if (Gs >= 0) incl += u;
+  }
+  uint32_t po = (incl - v) & 0xffffu, so = (incl - v) >> 16;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    decode_half_w16(e[k], sc[k], prim_base + po, sec_base + so, h, pow2e, R[k]);
+    po += lt_prim(e[k]);
+    so += lt_sec(e[k]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy / mma wrappers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: returns false (and the caller aborts) after `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+}  // namespace mtc

@@ -1,0 +1,456 @@
+// Fused dequant + tcgen05 GEMM for prefill-sized M: Y[:, pc] = X[:, pr] @ Wp.
+//
+// Replaces the reference's packed GEMM (mtc/kernels/gemm.py:124-210, 541-574)
+// and the MTC-QT-P gather / scatter (mtc/core/permutation.py:15-21) for
+// large M.  Three kernels on one stream:
+//
+//  1. gather_x:   Xp[m][k] = fp16(X[m][pr[k]]) (zero for k >= K); one CTA per
+//                 row stages the row in shared memory so both the read and
+//                 the write are coalesced.
+//  2. prefill:    persistent, one CTA per SM, output tile 256 tokens x 256
+//                 features, K step 64.  Warp roles:
+//                   warps 0-3  epilogue: TMEM -> registers -> global
+//                   warp  4    producer: TMA of the Xp tile (SWIZZLE_128B) and
+//                              cp.async.bulk of the band's packed k-tile rows
+//                   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
+//                   warps 6-13 dequant: packed codes -> fp16 W tile in the
+//                              K-major SWIZZLE_128B layout the MMA reads
+//                 Two 128x256 fp32 accumulators (all 512 TMEM columns) share
+//                 each dequantised W tile, so every weight is decoded once
+//                 per 256 tokens.  mbarriers link the stages; every wait is
+//                 bounded.
+//  3. permute_y:  Y[m][j] = Yp[m][ipc[j]] for MTC-QT-P matrices (row staged in
+//                 shared memory, coalesced in and out).
+#include "mtc_common.cuh"
+#include "mtc_internal.h"
+#include "mtc_tc.cuh"
+
+namespace mtc {
+namespace {
+
+constexpr int BM = 256;   // tokens per CTA tile (two M=128 MMAs)
+constexpr int BN = 256;   // features per CTA tile (one column band)
+constexpr int BK = 64;    // K per pipeline stage (two k-tile rows)
+constexpr int kEpiWarps = 4;
+constexpr int kProdWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kDeqWarp0 = 6;
+constexpr int kDeqWarps = 8;
+constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;
+constexpr uint32_t kABytes = BM * BK * 2;
+constexpr uint32_t kBBytes = BN * BK * 2;
+constexpr int kMaxS = 4;
+constexpr int kMaxP = 4;
+
+struct PrefillParams {
+  mtc_stream_desc s;
+  int M;
+  float* Y;           // Y (no column permutation) or Yp (permuted columns)
+  long long ldy;
+  uint32_t* status;
+  int n_bands, n_tiles, nkb;
+  int S, P;
+  uint32_t pslot;
+  float pow2e, inv_pow2e;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
+  if (st) atomicOr(st, bits);
+}
+
+// byte offset of element (row n, k) in a K-major SWIZZLE_128B tile of 64 fp16 per row
+__device__ __forceinline__ uint32_t sw128_off(int n, int k) {
+  return (uint32_t)n * 128u + ((((uint32_t)k >> 3) ^ ((uint32_t)n & 7u)) << 4) + (((uint32_t)k & 7u) << 1);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + p.S * kABytes;
+  uint8_t* sP = sB + p.S * kBBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.P * p.pslot);
+  uint64_t* full_ab = bars;              // [S]
+  uint64_t* empty_ab = full_ab + kMaxS;  // [S]
+  uint64_t* pfull = empty_ab + kMaxS;    // [P]
+  uint64_t* pempty = pfull + kMaxP;      // [P]
+  uint64_t* acc_full = pempty + kMaxP;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_empty + 1;
+  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort
+  uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
+
+  const mtc_stream_desc& s = p.s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.S; ++i) {
+      mbar_init(&full_ab[i], 1 + kDeqWarps);
+      mbar_init(&empty_ab[i], 1);
+    }
+    for (int i = 0; i < p.P; ++i) {
+      mbar_init(&pfull[i], 1);
+      mbar_init(&pempty[i], kDeqWarps);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kEpiWarps);
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    fence_barrier_init();
+  }
+  if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, 512);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProdWarp) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
+        const int mblk = tile / p.n_bands, band = tile % p.n_bands;
+        const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+          const int st = it % p.S, pst = it % p.P;
+          if (it >= (uint32_t)p.S && !mbar_wait(&empty_ab[st], ((it / p.S) & 1) ^ 1, p.timeout_ns)) {
+            flags[0] = 1;
+            break;
+          }
+          mbar_expect_tx(&full_ab[st], kABytes);
+          tc::tma_load_2d(sA + st * kABytes, &tmap_x, kb * BK, mblk * BM, &full_ab[st]);
+          if (it >= (uint32_t)p.P && !mbar_wait(&pempty[pst], ((it / p.P) & 1) ^ 1, p.timeout_ns)) {
+            flags[0] = 1;
+            break;
+          }
+          const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
+          const uint32_t off = row_off[r0];
+          const uint32_t bytes = row_off[r1] - off;
+          if (bytes > p.pslot || (off & 15u) || (bytes & 15u)) {
+            flag(p.status, MTC_STATUS_BAD_STREAM);
+            flags[0] = 1;
+            break;
+          }
+          mbar_expect_tx(&pfull[pst], bytes);
+          bulk_g2s(sP + pst * p.pslot, s.records + off, bytes, &pfull[pst]);
+        }
+      }
+      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16_f32(128, BN);
+      uint32_t it = 0, tcount = 0;
+      for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x, ++tcount) {
+        if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        tc::fence_after();
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+          const int st = it % p.S;
+          if (!mbar_wait(&full_ab[st], (it / p.S) & 1, p.timeout_ns)) {
+            flags[0] = 1;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t a0 = smem_u32(sA + st * kABytes);
+          const uint32_t b0 = smem_u32(sB + st * kBBytes);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            const uint64_t bd = tc::smem_desc_k_sw128(b0 + 32 * j);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            tc::mma_f16_ss(tmem, tc::smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
+            tc::mma_f16_ss(tmem + 256, tc::smem_desc_k_sw128(a0 + 128 * 128 + 32 * j), bd, idesc, acc);
+          }
+          tc::commit(&empty_ab[st]);
+        }
+        if (flags[0]) break;
+        tc::commit(acc_full);
+      }
+      // make sure no MMA is still reading shared memory or writing TMEM
+      tc::commit(drain);
+      (void)mbar_wait(drain, 0, 100000000ull);
+      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+    }
+  } else if (warp >= kDeqWarp0) {
+    // ---------------------------------------------------------------- dequant
+    const int dw = warp - kDeqWarp0;  // tile column inside the band
+    const int g = lane >> 2, t = lane & 3;
+    const int jj = g >> 1, h = g & 1;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
+      const int band = tile % p.n_bands;
+      const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
+      const int nt = band * s.band_tiles + dw;
+      for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        const int st = it % p.S, pst = it % p.P;
+        if (!mbar_wait(&pfull[pst], (it / p.P) & 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        if (it >= (uint32_t)p.S && !mbar_wait(&empty_ab[st], ((it / p.S) & 1) ^ 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        uint8_t* Bt = sB + st * kBBytes;
+        const uint32_t base_off = row_off[2 * kb];
+#pragma unroll 1
+        for (int r = 0; r < 2; ++r) {
+          const int kt = 2 * kb + r;
+          uint32_t R[4][4];
+          if (kt < s.tk && nt < s.tn) {
+            const mtc_tile_desc d = s.tiles[(size_t)kt * s.tn + nt];
+            const uint8_t* rec = sP + pst * p.pslot + (d.record_off - base_off);
+            decode_group_w16(rec, d.n_leaves, d.prim_bytes, d.leaf_start, s.scale_words, lane, p.pow2e, R);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int di = k >> 1, dj = k & 1;
+            const int f0 = 32 * dw + 4 * (2 * jj + dj) + 2 * h;   // feature row of the B tile
+            const int k0 = 32 * r + 4 * (2 * t + di);             // k column inside the stage
+            *reinterpret_cast<uint2*>(Bt + sw128_off(f0, k0)) = make_uint2(R[k][0], R[k][1]);
+            *reinterpret_cast<uint2*>(Bt + sw128_off(f0 + 1, k0)) = make_uint2(R[k][2], R[k][3]);
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full_ab[st]);
+          mbar_arrive(&pempty[pst]);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x, ++tcount) {
+      const int mblk = tile / p.n_bands, band = tile % p.n_bands;
+      if (!mbar_wait(acc_full, tcount & 1, p.timeout_ns)) {
+        flags[0] = 1;
+        break;
+      }
+      tc::fence_after();
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int m = mblk * BM + half * 128 + 32 * warp + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + half * 256 + c, v);
+          const int n0 = band * BN + c;
+          if (m < p.M) {
+            float* y = p.Y + (long long)m * p.ldy + n0;
+            if (n0 + 32 <= s.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                *reinterpret_cast<float4*>(y + j) =
+                    make_float4(__uint_as_float(v[j]) * p.inv_pow2e, __uint_as_float(v[j + 1]) * p.inv_pow2e,
+                                __uint_as_float(v[j + 2]) * p.inv_pow2e, __uint_as_float(v[j + 3]) * p.inv_pow2e);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < s.N) y[j] = __uint_as_float(v[j]) * p.inv_pow2e;
+            }
+          }
+        }
+      }
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+    if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+  }
+
+  tc::fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// Xp[m][k] = fp16(X[m][pr[k]]), k < K; zero up to Kp.  One CTA per row.
+__global__ void __launch_bounds__(256) gather_x_kernel(const float* __restrict__ X, long long ldx, int K, int Kp,
+                                                       const int32_t* __restrict__ pr, __half* __restrict__ Xp,
+                                                       uint32_t* status) {
+  extern __shared__ float row[];
+  const int m = blockIdx.x;
+  const float* x = X + (long long)m * ldx;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) row[k] = x[k];
+  __syncthreads();
+  uint32_t bad = 0;
+  __half* out = Xp + (long long)m * Kp;
+  for (int k = 2 * threadIdx.x; k < Kp; k += 2 * blockDim.x) {
+    float a = 0.f, b = 0.f;
+    if (k < K) a = row[pr ? pr[k] : k];
+    if (k + 1 < K) b = row[pr ? pr[k + 1] : k + 1];
+    if (!(fabsf(a) <= 65504.0f) || !(fabsf(b) <= 65504.0f)) bad = 1;
+    *reinterpret_cast<__half2*>(out + k) = __floats2half2_rn(a, b);
+  }
+  if (bad) flag(status, MTC_STATUS_X_RANGE);
+}
+
+// Y[m][j] = Yp[m][ipc[j]]  (Y[:, pc] = Yp).  One CTA per row.
+__global__ void __launch_bounds__(512) permute_y_kernel(const float* __restrict__ Yp, long long ldp,
+                                                        const int32_t* __restrict__ ipc, int N,
+                                                        float* __restrict__ Y, long long ldy) {
+  extern __shared__ float row[];
+  const int m = blockIdx.x;
+  const float* src = Yp + (long long)m * ldp;
+  for (int n = threadIdx.x; n < N; n += blockDim.x) row[n] = src[n];
+  __syncthreads();
+  float* dst = Y + (long long)m * ldy;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = row[ipc[j]];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+struct PrefillPlan {
+  int Kp, Np, nkb, n_mblk, n_bands, n_tiles, S, P;
+  uint32_t pslot;
+  size_t smem, xp_bytes, yp_bytes;
+};
+
+bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* pl) {
+  pl->Kp = s->tk * kTile;
+  pl->Np = s->tn * kTile;
+  pl->nkb = (s->tk + 1) / 2;
+  pl->n_mblk = (M + BM - 1) / BM;
+  pl->n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
+  pl->n_tiles = pl->n_mblk * pl->n_bands;
+  pl->pslot = (2 * s->max_row_bytes + 127u) & ~127u;
+  const size_t cap = 227 * 1024;
+  const size_t fixed = 1024 /*align*/ + 256 /*barriers*/;
+  int S = kMaxS, P = 2;
+  while (S >= 2 && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)P * pl->pslot > cap) --S;
+  if (S < 2) return false;
+  while (P < kMaxP && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)(P + 1) * pl->pslot <= cap) ++P;
+  pl->S = S;
+  pl->P = P;
+  pl->smem = fixed + (size_t)S * (kABytes + kBBytes) + (size_t)P * pl->pslot;
+  pl->xp_bytes = ((size_t)M * pl->Kp * 2 + 255) & ~(size_t)255;
+  pl->yp_bytes = permuted ? (size_t)M * pl->Np * 4 : 0;
+  return true;
+}
+
+}  // namespace
+}  // namespace mtc
+
+using namespace mtc;
+
+extern "C" size_t mtc_prefill_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t permuted) {
+  PrefillPlan pl;
+  if (!s || M <= 0 || !plan_prefill(s, M, permuted != 0, &pl)) return 0;
+  return pl.xp_bytes + pl.yp_bytes;
+}
+
+extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                                const int32_t* row_perm, const int32_t* col_perm_inv, float* Y, int64_t ldy,
+                                void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
+  clear_error();
+  MTC_REQUIRE(s && X && Y && ws && s->records && s->tiles && s->row_off, "mtc_gemm_prefill: null pointer argument");
+  MTC_REQUIRE(M >= 1, "mtc_gemm_prefill: M=%d", M);
+  MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_gemm_prefill: bad leading dimensions");
+  MTC_REQUIRE(s->band_tiles * kTile == BN, "mtc_gemm_prefill: stream band width %d tiles, kernel needs %d",
+              s->band_tiles, BN / kTile);
+  MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "mtc_gemm_prefill: workspace not 256-byte aligned");
+  PrefillPlan pl;
+  MTC_REQUIRE(plan_prefill(s, M, col_perm_inv != nullptr, &pl),
+              "mtc_gemm_prefill: a k-tile row of %u bytes does not fit shared memory", s->max_row_bytes);
+  if (ws_bytes < pl.xp_bytes + pl.yp_bytes) {
+    set_error("mtc_gemm_prefill: workspace %zu bytes, need %zu", ws_bytes, pl.xp_bytes + pl.yp_bytes);
+    return MTC_ERR_WORKSPACE;
+  }
+  MTC_REQUIRE((size_t)s->K * 4 <= 200 * 1024 && (size_t)s->N * 4 <= 200 * 1024,
+              "mtc_gemm_prefill: K=%d / N=%d above the 51200 supported by the row-staged gather/permute", s->K,
+              s->N);
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) {
+    set_error("mtc_gemm_prefill: cuTensorMapEncodeTiled unavailable from the driver");
+    return MTC_ERR_CUDA;
+  }
+  cudaStream_t st = as_stream(stream);
+  __half* Xp = static_cast<__half*>(ws);
+  float* Yp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.xp_bytes);
+
+  // 1. gather + fp16 cast of the activations
+  {
+    const size_t sm = (size_t)s->K * 4;
+    if (sm > 48 * 1024)
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                     "mtc_gemm_prefill: gather smem");
+    gather_x_kernel<<<M, 256, sm, st>>>(X, ldx, s->K, pl.Kp, row_perm, Xp, status);
+    MTC_CHECK_LAUNCH("mtc_gemm_prefill: gather_x");
+  }
+  // 2. TMA descriptor of Xp: fp16 [M][Kp], box 64 (k) x 256 (rows), 128-byte swizzle
+  CUtensorMap tmap;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)pl.Kp, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)pl.Kp * 2};
+    cuuint32_t box[2] = {BK, BM};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Xp, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("mtc_gemm_prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+      return MTC_ERR_CUDA;
+    }
+  }
+  // 3. fused dequant + tcgen05 GEMM
+  PrefillParams p;
+  p.s = *s;
+  p.M = M;
+  p.Y = col_perm_inv ? Yp : Y;
+  p.ldy = col_perm_inv ? pl.Np : ldy;
+  p.status = status;
+  p.n_bands = pl.n_bands;
+  p.n_tiles = pl.n_tiles;
+  p.nkb = pl.nkb;
+  p.S = pl.S;
+  p.P = pl.P;
+  p.pslot = pl.pslot;
+  p.pow2e = ldexpf(1.0f, s->exp2);
+  p.inv_pow2e = ldexpf(1.0f, -s->exp2);
+  p.timeout_ns = 2000000000ull;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  MTC_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
+                 "mtc_gemm_prefill: smem attribute");
+  const int grid = pl.n_tiles < sms ? pl.n_tiles : sms;
+  prefill_kernel<<<grid, kThreads, pl.smem, st>>>(tmap, p);
+  MTC_CHECK_LAUNCH("mtc_gemm_prefill: prefill");
+  // 4. output column permutation
+  if (col_perm_inv) {
+    const size_t sm = (size_t)s->N * 4;
+    if (sm > 48 * 1024)
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                     "mtc_gemm_prefill: permute smem");
+    permute_y_kernel<<<M, 512, sm, st>>>(Yp, pl.Np, col_perm_inv, s->N, Y, ldy);
+    MTC_CHECK_LAUNCH("mtc_gemm_prefill: permute_y");
+  }
+  return MTC_OK;
+}

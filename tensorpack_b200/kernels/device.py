@@ -1,0 +1,164 @@
+"""Device-resident tile stream of a packed MTC matrix and the kernel launchers.
+
+``DeviceStream`` owns the GPU copy of one matrix (tile records, 16-byte tile
+descriptors, per-band row offsets, permutations) as torch tensors and calls
+the C ABI with their device pointers on the current torch stream.  torch is
+only the allocator / stream provider here; every byte of the stream is
+produced and consumed by the CUDA kernels in ``csrc/``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..core import layout
+
+BAND_TILES = 8  # tiles per column band = 256 output features (one per consumer warp)
+DECODE_MAX_M = 16  # largest M served by the split-K decode kernel
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class DeviceStream:
+    """GPU tile stream of one MTCMatrix on one device (built by the GPU repack)."""
+
+    def __init__(self, mat, device):
+        if not torch.cuda.is_available():
+            raise RuntimeError("the MTC GEMM path needs a CUDA device (B200, sm_100a); none is available")
+        lib = _lib.load()
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError(f"DeviceStream needs a CUDA device, got {self.device}")
+        K, N = mat.shape
+        self.K, self.N = int(K), int(N)
+        ls = mat.leaf_set
+        leaves, begin, tk, tn = layout.device_leaf_list(ls, self.K, self.N)
+        self.tk, self.tn = tk, tn
+        self.n_bands = -(-tn // BAND_TILES)
+        self.exp2 = layout.choose_exp2(ls)
+        self.scale_words = 1 if layout.bf16_exact(ls.scale) else 2
+        dev = self.device
+        arena = np.ascontiguousarray(mat.arena.raw_buffer[:max(mat.total_bytes_allocated, 1)])
+        with torch.cuda.device(dev):
+            d_arena = torch.from_numpy(arena).to(dev)
+            d_leaves = torch.from_numpy(leaves.view(np.uint8).copy()).to(dev)
+            d_begin = torch.from_numpy(begin.view(np.int32).copy()).to(dev)
+            T = tk * tn
+            self.tiles = torch.empty(T * 16, dtype=torch.uint8, device=dev)
+            self.row_off = torch.empty(self.n_bands * (tk + 1), dtype=torch.int32, device=dev)
+            scratch = torch.empty(T + 8, dtype=torch.int32, device=dev)
+            out = (ctypes.c_uint64 * 2)()
+            st = _stream(dev)
+            _lib.check(lib.mtc_repack_plan(d_leaves.data_ptr(), d_begin.data_ptr(), tk, tn, BAND_TILES,
+                                           self.scale_words, self.tiles.data_ptr(), self.row_off.data_ptr(),
+                                           scratch.data_ptr(), out, st), "repack plan")
+            self.record_bytes = int(out[0])
+            self.max_row_bytes = int(out[1])
+            self.records = torch.empty(max(self.record_bytes, 16), dtype=torch.uint8, device=dev)
+            self.desc = _lib.StreamDesc(
+                records=self.records.data_ptr(), tiles=self.tiles.data_ptr(), row_off=self.row_off.data_ptr(),
+                K=self.K, N=self.N, tk=tk, tn=tn, band_tiles=BAND_TILES, exp2=self.exp2,
+                record_bytes=self.record_bytes, max_row_bytes=self.max_row_bytes, scale_words=self.scale_words)
+            _lib.check(lib.mtc_repack_fill(d_arena.data_ptr(), arena.nbytes, d_leaves.data_ptr(),
+                                           d_begin.data_ptr(), ctypes.byref(self.desc), self.records.data_ptr(),
+                                           scratch.data_ptr(), st), "repack fill")
+            self.row_perm = None if mat.row_perm is None else torch.from_numpy(
+                np.asarray(mat.row_perm, dtype=np.int32)).to(dev)
+            self.col_perm = None if mat.col_perm is None else torch.from_numpy(
+                np.asarray(mat.col_perm, dtype=np.int32)).to(dev)
+            self.col_perm_inv = None
+            if mat.col_perm is not None:
+                inv = np.empty(self.N, dtype=np.int32)
+                inv[np.asarray(mat.col_perm)] = np.arange(self.N, dtype=np.int32)
+                self.col_perm_inv = torch.from_numpy(inv).to(dev)
+            self.counters = torch.zeros(self.n_bands, dtype=torch.int32, device=dev)
+            self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._ws = {}
+        self.n_leaves = len(ls)
+
+    # ------------------------------------------------------------------
+    @property
+    def device_bytes(self) -> int:
+        """Bytes of the device format (records + descriptors + row offsets)."""
+        return self.record_bytes + self.tiles.numel() + 4 * self.row_off.numel()
+
+    def dequant(self, original_order: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Exact fp32 reconstruction (bit-identical to the reference dequant)."""
+        lib = _lib.load()
+        if out is None:
+            out = torch.empty(self.K, self.N, dtype=torch.float32, device=self.device)
+        assert out.shape == (self.K, self.N) and out.dtype == torch.float32 and out.stride(1) == 1
+        pr = self.row_perm if original_order else None
+        pc = self.col_perm if original_order else None
+        _lib.check(lib.mtc_dequant(ctypes.byref(self.desc), _ptr(pr), _ptr(pc), out.data_ptr(), out.stride(0),
+                                   _stream(self.device)), "dequant")
+        return out
+
+    def _workspace(self, M: int, rows_per_unit: int) -> torch.Tensor:
+        lib = _lib.load()
+        need = int(lib.mtc_gemv_workspace_bytes(ctypes.byref(self.desc), M, rows_per_unit))
+        key = (M > 8, rows_per_unit)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.empty(max(need // 4, 1), dtype=torch.float32, device=self.device)
+            self._ws[key] = ws
+        return ws
+
+    def gemv(self, X: torch.Tensor, Y: torch.Tensor, rows_per_unit: int = 0) -> torch.Tensor:
+        """Y[:M] = X @ W for M <= 16 (split-K streaming kernel)."""
+        lib = _lib.load()
+        M = X.shape[0]
+        ws = self._workspace(M, rows_per_unit)
+        _lib.check(lib.mtc_gemv(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
+                                _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), rows_per_unit, ws.data_ptr(),
+                                ws.numel() * 4, self.counters.data_ptr(), self.status.data_ptr(),
+                                _stream(self.device)), "gemv")
+        return Y
+
+    def prefill(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
+        """Y = X @ W for any M (fused dequant + tcgen05 kernel; used for M > 16)."""
+        lib = _lib.load()
+        M = X.shape[0]
+        permuted = 1 if self.col_perm_inv is not None else 0
+        need = int(lib.mtc_prefill_workspace_bytes(ctypes.byref(self.desc), M, permuted))
+        ws = self._ws.get("prefill")
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+            self._ws["prefill"] = ws
+        _lib.check(lib.mtc_gemm_prefill(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
+                                        _ptr(self.col_perm_inv), Y.data_ptr(), Y.stride(0), ws.data_ptr(),
+                                        ws.numel(), self.status.data_ptr(), _stream(self.device)), "prefill")
+        return Y
+
+    def matmul(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
+        """Y = X @ W, picking the decode kernel for M <= 16 and the tensor-core
+        prefill kernel above."""
+        if X.shape[0] <= DECODE_MAX_M:
+            return self.gemv(X, Y)
+        return self.prefill(X, Y)
+
+    def check_status(self):
+        """Raise if a kernel reported a runtime problem (synchronises)."""
+        v = int(self.status.item())
+        if v:
+            self.status.zero_()
+            self.counters.zero_()
+            bits = []
+            if v & _lib.STATUS_TIMEOUT:
+                bits.append("pipeline wait timed out")
+            if v & _lib.STATUS_X_RANGE:
+                bits.append("|X| exceeds the fp16 range (65504) of the tensor-core path")
+            if v & _lib.STATUS_BAD_STREAM:
+                bits.append("tile stream failed a bounds check")
+            raise RuntimeError("MTC kernel status: " + "; ".join(bits))

@@ -1,0 +1,63 @@
+"""Quantized linear layer running the packed MTC GEMM on the GPU.
+
+Drop-in for ``mtc.nn.layers.LinearMTCAdaptive`` (mtc/nn/layers.py:115-151):
+same constructor signature, the same seeded fp32 weights (LinearFP32,
+layers.py:78-85) packed with ``MTCMatrix.from_numpy`` and the same
+``weight_bytes``.  The reference's forward multiplies by a cached dequantised
+copy on the CPU; here ``forward`` runs the packed GEMM kernels, so the
+packed bytes are what the GPU reads.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import numpy as np
+import torch
+
+from ..core.arena import MemoryArena
+from ..kernels.gemm import MTCMatrix, mtc_gemm
+
+
+class LinearMTCAdaptive(torch.nn.Module):
+    def __init__(self, in_features: int, out_features: int, block_size: int = 16, epsilon: float = 0.05,
+                 seed: int = 42, *, W_mtc: Optional[MTCMatrix] = None, bias: Optional[np.ndarray] = None):
+        super().__init__()
+        self.block_size = block_size
+        self.in_features = in_features
+        self.out_features = out_features
+        if W_mtc is None:
+            rng = np.random.RandomState(seed)
+            std = 1.0 / np.sqrt(in_features)
+            W = rng.uniform(-std, std, size=(in_features, out_features)).astype(np.float32)
+            self.arena = MemoryArena(capacity_bytes=in_features * out_features * 2)
+            W_mtc = MTCMatrix.from_numpy(W, block_size=block_size, epsilon=epsilon, arena=self.arena,
+                                         use_pointer_hierarchy=False)
+        else:
+            if W_mtc.shape != (in_features, out_features):
+                raise ValueError(f"W_mtc shape {W_mtc.shape} != ({in_features}, {out_features})")
+            self.arena = W_mtc.arena
+        self.W_mtc = W_mtc
+        self.b = np.zeros(out_features, dtype=np.float32) if bias is None else np.asarray(bias, np.float32)
+        self._bias_dev = {}
+
+    @classmethod
+    def from_mtc(cls, W_mtc: MTCMatrix, bias: Optional[np.ndarray] = None) -> "LinearMTCAdaptive":
+        """Wrap an already packed matrix (e.g. from ``MTCMatrix.from_qt_allocation``)."""
+        K, N = W_mtc.shape
+        return cls(K, N, block_size=W_mtc.block_size, W_mtc=W_mtc, bias=bias)
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.W_mtc.total_bytes_allocated + self.b.nbytes
+
+    def forward(self, X):
+        if isinstance(X, np.ndarray):
+            return mtc_gemm(X, self.W_mtc) + self.b
+        Y = mtc_gemm(X, self.W_mtc)
+        key = str(Y.device)
+        bd = self._bias_dev.get(key)
+        if bd is None:
+            bd = torch.from_numpy(self.b).to(Y.device)
+            self._bias_dev[key] = bd
+        return Y.add_(bd)

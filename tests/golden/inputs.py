@@ -79,3 +79,57 @@ def fixed_pair(seed=5):
     A[:, :32] *= 1e-4
     B[32:64] *= 20.0
     return A, B
+
+
+def linear_fp32_weight(in_features, out_features, seed=42):
+    """Weights of the reference's LinearFP32 (mtc/nn/layers.py:78-83):
+    uniform(-1/sqrt(in), 1/sqrt(in)) from RandomState(seed)."""
+    rng = np.random.RandomState(seed)
+    std = 1.0 / np.sqrt(in_features)
+    return rng.uniform(-std, std, size=(in_features, out_features)).astype(np.float32)
+
+
+def heavy_tailed(K, N, seed=9):
+    """Student-t(2) weights with a few very large entries (reaches P8/P16)."""
+    rng = np.random.default_rng(seed)
+    W = rng.standard_t(2, (K, N)).astype(np.float32)
+    W[rng.random((K, N)) < 0.002] *= 1e4
+    return W
+
+
+def forced_mode_allocation(K, N, seed=0, sizes=(32, 16, 8, 4), p_split=0.6):
+    """Random quadtree tiling whose leaves draw their mode uniformly from all
+    eight precisions (P0..P16) at every level, with signed bf16 scales of
+    amax/qmax times U(0.6, 1).  The reference allocator never produces this
+    mix on its benchmark inputs, so it is the coverage fixture for every
+    (edge, mode) pair.  Returns (W, sizes, leaf, modes, scales) with the
+    QTAllocation field layout (mtc/core/quadtree.py:55-61)."""
+    rng = np.random.default_rng(seed)
+    sig = np.exp(rng.uniform(np.log(1e-2), np.log(1e1), (K // 32, N // 32)))
+    W = (rng.standard_normal((K, N)) * np.kron(sig, np.ones((32, 32)))).astype(np.float32)
+    modes_all = np.array([0, 2, 3, 4, 5, 6, 8, 16], dtype=np.uint8)
+    leaf = {s: np.zeros((K // s, N // s), bool) for s in sizes}
+    modes = {s: np.zeros((K // s, N // s), np.uint8) for s in sizes}
+    scales = {s: np.zeros((K // s, N // s), np.float32) for s in sizes}
+
+    def visit(level, i, j):
+        s = sizes[level]
+        if level + 1 < len(sizes) and rng.random() < p_split:
+            for di in (0, 1):
+                for dj in (0, 1):
+                    visit(level + 1, 2 * i + di, 2 * j + dj)
+            return
+        m = int(modes_all[rng.integers(0, 8)])
+        leaf[s][i, j] = True
+        modes[s][i, j] = m
+        if m:
+            amax = float(np.abs(W[i * s:(i + 1) * s, j * s:(j + 1) * s]).max())
+            qmax = float(2 ** (m - 1) - 1) if m > 2 else 1.0
+            sc = np.float32(amax / qmax * rng.uniform(0.6, 1.0) * rng.choice([-1.0, 1.0]))
+            scales[s][i, j] = (np.array([sc], np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)[0]
+
+    root = sizes[0]
+    for i in range(K // root):
+        for j in range(N // root):
+            visit(0, i, j)
+    return W, tuple(sizes), leaf, modes, scales

@@ -131,6 +131,20 @@ def main():
          payload_bits=np.array(al.payload_bits), meta_bits=np.array(al.meta_bits),
          cand_D=c.D, cand_S=c.S)
 
+    # 8. Legacy adaptive per-block packing (MTCMatrix.from_numpy) as used by
+    #    LinearMTCAdaptive, on the layer's own seeded weights and on a
+    #    heavy-tailed matrix that reaches the P8 / P16 escape modes.
+    out = {}
+    for tag, W in (("layer", inputs.linear_fp32_weight(32, 16, seed=42)),
+                   ("heavy", inputs.heavy_tailed(64, 64, seed=9))):
+        mm = MTCMatrix.from_numpy(W, block_size=16, epsilon=0.05, use_pointer_hierarchy=False)
+        out[tag + "_arena"] = mm.arena.raw_buffer[: mm.total_bytes_allocated].copy()
+        out[tag + "_offsets"] = mm.offsets
+        out[tag + "_precisions"] = mm.precisions
+        out[tag + "_scales"] = mm.scales
+        out[tag + "_dequant"] = mm.to_array()
+    save("legacy_from_numpy.npz", **out)
+
 
 if __name__ == "__main__":
     main()
