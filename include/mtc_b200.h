@@ -105,6 +105,11 @@ typedef struct mtc_stream_desc {
   uint64_t record_bytes;         /* total bytes of `records` */
   uint32_t max_row_bytes;        /* largest k-tile row of any band */
   int32_t scale_words;           /* 1: bf16 scale in the entry, 2: extra fp32 scale word */
+  /* Prefill work lists (NULL until mtc_repack_stage_lists builds them): for
+   * every (band, stage of two k-tile rows), up to 256 8x8-group entries
+   * sorted by decode class, and their count. */
+  const uint64_t* stage_lists;   /* [n_bands * n_stages * 256] */
+  const uint32_t* stage_counts;  /* [n_bands * n_stages] */
 } mtc_stream_desc;
 
 MTC_API int mtc_abi_version(void);
@@ -132,6 +137,18 @@ MTC_API int mtc_repack_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf
 MTC_API int mtc_repack_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc_leaf_in* leaves,
                     const uint32_t* tile_leaf_begin, const mtc_stream_desc* s, uint8_t* records,
                     uint32_t* scratch_u32, void* stream);
+
+/* Repack step 3 (prefill only): for every stage (band, pair of k-tile rows)
+ * write the stage's 8x8 groups as 64-bit entries sorted by decode class
+ * (P0, P2, P3, P4, P5, P6, P8, then groups needing the generic per-block
+ * path), so prefill dequant warps take mode-uniform batches.  Entry bits:
+ * 0-15 primary-plane offset and 16-31 secondary-plane offset (bytes from the
+ * stage's first record), 32-47 fp16 bits of scale * 2^exp2, 48-51 class,
+ * 52-55 tile within the stage (row * 8 + column), 56-59 group (Z order).
+ * `lists` holds n_bands * n_stages * 256 entries, `counts` one word per
+ * stage (n_stages = ceil(tk / 2)).  Uses s->tiles, s->row_off, s->records. */
+MTC_API int mtc_repack_stage_lists(const mtc_stream_desc* s, uint64_t* lists, uint32_t* counts,
+                                   void* stream);
 
 /* Exact dequantisation (replaces MTCMatrix.to_array, gemm.py:510-538, and
  * qt_dequant / permuted_qt_dequant, quadtree.py:157-171, permutation.py:

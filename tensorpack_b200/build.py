@@ -53,15 +53,16 @@ def needs_build() -> bool:
     return any(os.path.getmtime(p) > t for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB, build_dir: str = BUILD) -> str:
+    """Compile every csrc/*.cu and link ``out``; ``defines`` are extra -D flags."""
+    if out == LIB and not defines and not force and not needs_build():
         return LIB
-    os.makedirs(BUILD, exist_ok=True)
+    os.makedirs(build_dir, exist_ok=True)
     cc = nvcc()
 
     def compile_one(src):
-        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-        cmd = [cc, *ARCH, *FLAGS, "-c", src, "-o", obj]
+        obj = os.path.join(build_dir, os.path.basename(src)[:-3] + ".o")
+        cmd = [cc, *ARCH, *FLAGS, *("-D" + d for d in defines), "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -73,13 +74,13 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, sources()))
-    tmp = LIB + ".tmp"
+    tmp = out + ".tmp"
     cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, out)
+    return out
 
 
 def main():

@@ -32,6 +32,13 @@
 
 #include "../../include/mtc_b200.h"
 
+// Decoder used when the lanes of a warp hold groups of different modes:
+// 1 = one table-driven instruction sequence for all modes, 0 = per-mode
+// specialised code (lanes of other modes idle while each path runs).
+#ifndef MTC_MIXED_TABLE_DECODE
+#define MTC_MIXED_TABLE_DECODE 0
+#endif
+
 namespace mtc {
 
 constexpr int kTile = 32;
@@ -308,49 +315,229 @@ __device__ __forceinline__ int group_of_lane(int lane) {
   return ((t >> 1) << 3) | ((jj >> 1) << 2) | ((t & 1) << 1) | (jj & 1);
 }
 
+// Per-lane constants of the group decode, computed once per kernel.
+struct GroupLane {
+  int z0;       // first micro-block (Z order) of this lane's group
+  int h;        // column half
+  int src[4];   // scan partner lane for distance 1, 2, 4, 8 (own lane if none)
+  uint32_t live;  // bit i set when the partner for distance 2^i exists
+};
+
+__device__ __forceinline__ GroupLane make_group_lane(int lane) {
+  GroupLane c;
+  const int G = group_of_lane(lane);
+  c.z0 = 4 * G;
+  c.h = (lane >> 2) & 1;
+  c.live = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int Gs = G - (1 << i);
+    const int ts = ((Gs >> 3) & 1) << 1 | ((Gs >> 1) & 1);
+    const int js = ((Gs >> 2) & 1) << 1 | (Gs & 1);
+    c.src[i] = (Gs >= 0) ? (8 * js + ts) : lane;
+    if (Gs >= 0) c.live |= 1u << i;
+  }
+  return c;
+}
+
+// Four micro-blocks of one mode, consecutive in the plane regions: the
+// group of a leaf of edge >= 8.  pb / sb = plane bytes per micro-block.
+template <int MODE>
+__device__ __forceinline__ void decode_run4(const uint8_t* prim, const uint8_t* sec, int h, uint32_t s2,
+                                            uint32_t R[4][4]) {
+  constexpr int pb = (MODE == 2 || MODE == 3) ? 4 : (MODE == 8 ? 16 : 8);
+  constexpr int sb = (MODE == 3 || MODE == 5) ? 2 : (MODE == 6 ? 4 : 0);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t q[4];
+    decode_half_codes(MODE, prim + k * pb, sec + k * sb, h, q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) R[k][j] = hmul2u(q[j], s2);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Mode-uniform ("two-plane") decoder used when the lanes of a warp hold
+// groups of different modes: one instruction sequence for P2..P8 driven by a
+// per-mode parameter table, so no lane waits on another lane's branch.
+//   q = fma(prim_field, c, fma(sec_field, cs, K))
+// prim_field = (x_j & pmask_j) | 1024.0, sec_field likewise with smask_j
+// (zero mask for single-plane modes: the field then reads 1024 exactly and K
+// cancels it).  All intermediate values are small integers, so exact.
+// ---------------------------------------------------------------------------
+struct DecRow {  // 20 words per mode: pmask[4] smask[4] c[4] cs[4] K[4]
+  uint32_t w[20];
+};
+
+__host__ __device__ constexpr DecRow make_dec_row(int mode) {
+  DecRow r{};
+  const int wp = (mode == 2 || mode == 3) ? 2 : (mode == 8 ? 8 : 4);
+  const int ws = (mode == 3 || mode == 5) ? 1 : (mode == 6 ? 2 : 0);
+  const double bias = double(1 << (mode - 1));
+  for (int j = 0; j < 4; ++j) {
+    uint32_t pm = 0;
+    int pos = 0;
+    if (wp == 2) { pm = 0x00030003u << (2 * j); pos = 2 * j; }
+    if (wp == 4) { pm = (j & 1) ? 0x00F000F0u : 0x000F000Fu; pos = (j & 1) ? 4 : 0; }
+    if (wp == 8) { pm = 0x00FF00FFu; pos = 0; }
+    uint32_t sm = 0;
+    double cs = 0.0;
+    if (ws == 1) { sm = 0x00010001u << j; cs = double(1 << wp) / double(1 << j); }
+    if (ws == 2) { sm = 0x00030003u << (2 * j); cs = double(1 << wp) / double(1 << (2 * j)); }
+    const double c = 1.0 / double(1 << pos);
+    r.w[j] = pm;
+    r.w[4 + j] = sm;
+    r.w[8 + j] = k2(c);
+    r.w[12 + j] = k2(cs);
+    r.w[16 + j] = k2(-1024.0 * cs - bias - 1024.0 * c);
+  }
+  return r;
+}
+
+// mode -> row of the parameter table (2,3,4,5,6,8 -> 0..5)
+__device__ __forceinline__ int dec_row_index(int mode) { return (0x5F43210u >> (4 * (mode - 2))) & 15u; }
+
+// The table, built at compile time (rows for modes 2, 3, 4, 5, 6, 8).
+static __constant__ DecRow kDecTable[6] = {make_dec_row(2), make_dec_row(3), make_dec_row(4),
+                                           make_dec_row(5), make_dec_row(6), make_dec_row(8)};
+
+// Copy the table (6 rows x 20 words) into shared memory; call by one warp.
+__device__ __forceinline__ void load_dec_table(uint32_t* dst, int lane) {
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(kDecTable);
+  for (int i = lane; i < 120; i += 32) dst[i] = src[i];
+}
+
+// One micro-block half with the table row `tab` (P2..P8).
+__device__ __forceinline__ void decode_half_uniform(const uint32_t* tab, int mode, const uint8_t* prim,
+                                                    const uint8_t* sec, int h, uint32_t s2, uint32_t r[4]) {
+  const int wp = (mode == 2 || mode == 3) ? 2 : (mode == 8 ? 8 : 4);
+  const int ws = (mode == 3 || mode == 5) ? 1 : (mode == 6 ? 2 : 0);
+  const int offA = (wp == 2) ? 0 : (wp == 4 ? 4 * h : 8 * h);
+  const int offB = (wp == 8) ? 8 * h + 4 : offA;
+  const uint32_t A = ld32(prim + offA) >> ((wp == 2) ? 8 * h : 0);
+  const uint32_t B = ld32(prim + offB) >> ((wp == 2) ? 8 * h : 0);
+  const uint32_t x[4] = {A, A >> (wp == 8 ? 8 : 0), B >> (wp == 4 ? 8 : 0), B >> (wp == 2 ? 0 : 8)};
+  uint32_t S = 0;
+  if (ws == 1) S = __byte_perm(ld16(sec), 0u, 0x4140) >> (4 * h);
+  if (ws == 2) S = (ld16(sec) | (ld16(sec + 2) << 16)) >> (8 * h);
+  const uint4 pm = *reinterpret_cast<const uint4*>(tab);
+  const uint4 sm = *reinterpret_cast<const uint4*>(tab + 4);
+  const uint4 c = *reinterpret_cast<const uint4*>(tab + 8);
+  const uint4 cs = *reinterpret_cast<const uint4*>(tab + 12);
+  const uint4 K = *reinterpret_cast<const uint4*>(tab + 16);
+  r[0] = hmul2u(hfma2u(lop_or(x[0], pm.x), c.x, hfma2u(lop_or(S, sm.x), cs.x, K.x)), s2);
+  r[1] = hmul2u(hfma2u(lop_or(x[1], pm.y), c.y, hfma2u(lop_or(S, sm.y), cs.y, K.y)), s2);
+  r[2] = hmul2u(hfma2u(lop_or(x[2], pm.z), c.z, hfma2u(lop_or(S, sm.z), cs.z, K.z)), s2);
+  r[3] = hmul2u(hfma2u(lop_or(x[3], pm.w), c.w, hfma2u(lop_or(S, sm.w), cs.w, K.w)), s2);
+}
+
+// Any group through the per-micro-block path (four 4x4 leaves of possibly
+// different modes, P16, inexact fp16 scales).  prim / sec = group base.
+__device__ __forceinline__ void decode_group_generic(const uint32_t* ltab, uint64_t leaf_start, int G,
+                                                     const uint8_t* prim, const uint8_t* sec, int sw, int h,
+                                                     float pow2e, uint32_t R[4][4]) {
+  const int z0 = 4 * G;
+  const int l0 = leaf_of(leaf_start, z0);
+  const bool single = ((leaf_start >> (z0 + 1)) & 7ull) == 0ull;
+  uint32_t po = 0, so = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int L = single ? l0 : l0 + k;
+    const uint32_t e = lt_entry(ltab, L, sw);
+    decode_half_w16(e, lt_scale_of(ltab, L, sw), prim + po, sec + so, h, pow2e, R[k]);
+    po += lt_prim(e);
+    so += lt_sec(e);
+  }
+}
+
+__device__ __forceinline__ uint32_t half2_bits(float v) {
+  __half x = __float2half_rn(v);
+  return h2const(*reinterpret_cast<uint16_t*>(&x));
+}
+
 __device__ __forceinline__ void decode_group_w16(const uint8_t* rec, uint16_t n_leaves, uint16_t prim_bytes,
-                                                 uint64_t leaf_start, int sw, int lane, float pow2e,
-                                                 uint32_t R[4][4]) {
+                                                 uint64_t leaf_start, int sw, const GroupLane& c, float pow2e,
+                                                 const uint32_t* dtab, uint32_t R[4][4]) {
   const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
   const uint8_t* prim_base = rec + pad16(4 * sw * n_leaves);
   const uint8_t* sec_base = prim_base + pad16(prim_bytes);
-  const int G = group_of_lane(lane);
-  const int z0 = 4 * G;
-  const int h = (lane >> 2) & 1;
-  uint32_t e[4];
-  float sc[4];
-  const int l0 = leaf_of(leaf_start, z0);
-  if (((leaf_start >> (z0 + 1)) & 7ull) == 0ull) {
-    e[0] = e[1] = e[2] = e[3] = lt_entry(ltab, l0, sw);
-    sc[0] = sc[1] = sc[2] = sc[3] = lt_scale_of(ltab, l0, sw);
+  const int l0 = leaf_of(leaf_start, c.z0);
+  const bool single = ((leaf_start >> (c.z0 + 1)) & 7ull) == 0ull;
+  const uint32_t e0 = lt_entry(ltab, l0, sw);
+  uint32_t v;
+  if (single) {
+    v = 4u * ((uint32_t)lt_prim(e0) | ((uint32_t)lt_sec(e0) << 16));
   } else {
+    v = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      e[k] = lt_entry(ltab, l0 + k, sw);
-      sc[k] = lt_scale_of(ltab, l0 + k, sw);
+      const uint32_t e = lt_entry(ltab, l0 + k, sw);
+      v += (uint32_t)lt_prim(e) | ((uint32_t)lt_sec(e) << 16);
     }
   }
-  uint32_t v = 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) v += (uint32_t)lt_prim(e[k]) | ((uint32_t)lt_sec(e[k]) << 16);
-  // exclusive scan of group sizes over the 16 groups in Z order; the group
-  // G' is held (with h = 0) by lane 8 * jj' + t'.
+  // exclusive scan of group sizes over the 16 groups in Z order
   uint32_t incl = v;
 #pragma unroll
-  for (int dl = 1; dl < 16; dl <<= 1) {
-    const int Gs = G - dl;
-    const int ts = ((Gs >> 3) & 1) << 1 | ((Gs >> 1) & 1);
-    const int js = ((Gs >> 2) & 1) << 1 | (Gs & 1);
-    const int src = (Gs >= 0) ? (8 * js + ts) : lane;
-    const uint32_t u = __shfl_sync(0xffffffffu, incl, src);
-    if (Gs >= 0) incl += u;
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t u = __shfl_sync(0xffffffffu, incl, c.src[i]);
+    if (c.live & (1u << i)) incl += u;
   }
-  uint32_t po = (incl - v) & 0xffffu, so = (incl - v) >> 16;
+  const uint32_t ex = incl - v;
+  const uint8_t* prim = prim_base + (ex & 0xffffu);
+  const uint8_t* sec = sec_base + (ex >> 16);
+  const int mode0 = lt_mode(e0);
+  const bool fast = single && mode0 != 16 && !lt_slow(e0);
+  const int mode_l0 = __shfl_sync(0xffffffffu, mode0, 0);
+  if (__all_sync(0xffffffffu, fast && mode0 == mode_l0)) {
+    // every lane holds a single-leaf group of the same mode: specialised path
+    const uint32_t s2 = half2_bits(lt_scale_of(ltab, l0, sw) * pow2e);
+    switch (mode_l0) {
+      case 2: decode_run4<2>(prim, sec, c.h, s2, R); return;
+      case 3: decode_run4<3>(prim, sec, c.h, s2, R); return;
+      case 4: decode_run4<4>(prim, sec, c.h, s2, R); return;
+      case 5: decode_run4<5>(prim, sec, c.h, s2, R); return;
+      case 6: decode_run4<6>(prim, sec, c.h, s2, R); return;
+      case 8: decode_run4<8>(prim, sec, c.h, s2, R); return;
+      default:
+#pragma unroll
+        for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
+        return;
+    }
+  }
+#if MTC_MIXED_TABLE_DECODE == 0
+  if (fast) {
+    const uint32_t s2 = half2_bits(lt_scale_of(ltab, l0, sw) * pow2e);
+    switch (mode0) {
+      case 2: decode_run4<2>(prim, sec, c.h, s2, R); return;
+      case 3: decode_run4<3>(prim, sec, c.h, s2, R); return;
+      case 4: decode_run4<4>(prim, sec, c.h, s2, R); return;
+      case 5: decode_run4<5>(prim, sec, c.h, s2, R); return;
+      case 6: decode_run4<6>(prim, sec, c.h, s2, R); return;
+      case 8: decode_run4<8>(prim, sec, c.h, s2, R); return;
+      default:
+#pragma unroll
+        for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
+        return;
+    }
+  }
+#endif
+  // mixed modes across the warp: one table-driven sequence for P2..P8,
+  // branches only for P0 / P16 / inexact-scale micro-blocks
+  uint32_t po = 0, so = 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    decode_half_w16(e[k], sc[k], prim_base + po, sec_base + so, h, pow2e, R[k]);
-    po += lt_prim(e[k]);
-    so += lt_sec(e[k]);
+    const int L = single ? l0 : l0 + k;
+    const uint32_t e = lt_entry(ltab, L, sw);
+    const int m = lt_mode(e);
+    const float scl = lt_scale_of(ltab, L, sw);
+    if (MTC_MIXED_TABLE_DECODE && m >= 2 && m != 16 && !lt_slow(e)) {
+      decode_half_uniform(dtab + 20 * dec_row_index(m), m, prim + po, sec + so, c.h, half2_bits(scl * pow2e),
+                          R[k]);
+    } else {
+      decode_half_w16(e, scl, prim + po, sec + so, c.h, pow2e, R[k]);
+    }
+    po += lt_prim(e);
+    so += lt_sec(e);
   }
 }
 
@@ -377,14 +564,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or ~20 us pass) instead of re-issuing the test, so idle roles do
+// not take issue slots from the working warps.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0;
 }
@@ -397,9 +587,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.

@@ -28,6 +28,8 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 8;
+constexpr uint32_t kDescBytes = 128;  // tile descriptors at the head of each stage slot
+constexpr int kHeadBytes = 1024;      // barriers, flags, decoder table
 
 struct GemvParams {
   mtc_stream_desc s;
@@ -61,9 +63,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(empty + kMaxStages);  // [0] abort, [1] last
-  __half* xs = reinterpret_cast<__half*>(smem + 256);
+  uint32_t* dtab = reinterpret_cast<uint32_t*>(smem + 256);  // two-plane decoder table (480 B)
+  __half* xs = reinterpret_cast<__half*>(smem + kHeadBytes);
   const int xs_bytes = TG * 8 * p.x_stride * 2;
-  uint8_t* slots = smem + 256 + ((xs_bytes + 127) & ~127);
+  uint8_t* slots = smem + kHeadBytes + ((xs_bytes + 127) & ~127);
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -83,6 +86,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     flags[1] = 0;
     fence_barrier_init();
   }
+  if (warp == 0) load_dec_table(dtab, lane);
   __syncthreads();
 
   if (warp == kConsumerWarps) {
@@ -99,14 +103,17 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         if (flags[0]) break;
         const uint32_t off = row_off[r0 + i];
         const uint32_t bytes = row_off[r0 + i + 1] - off;
-        if (bytes > p.slot_bytes || (off & 15u) || (bytes & 15u)) {
+        if (bytes + kDescBytes > p.slot_bytes || (off & 15u) || (bytes & 15u)) {
           flags[0] = 1;
           flag_status(p.status, MTC_STATUS_BAD_STREAM);
           break;
         }
         uint8_t* dst = slots + (size_t)slot * p.slot_bytes;
-        mbar_expect_tx(&full[slot], bytes);
-        bulk_g2s(dst, s.records + off, bytes, &full[slot]);
+        // the 16-byte descriptors of the band's tiles in this row, then the records
+        const int width = min(s.band_tiles, s.tn - b * s.band_tiles);
+        mbar_expect_tx(&full[slot], bytes + 16u * width);
+        bulk_g2s(dst, s.tiles + (size_t)(r0 + i) * s.tn + b * s.band_tiles, 16u * width, &full[slot]);
+        bulk_g2s(dst + kDescBytes, s.records + off, bytes, &full[slot]);
         ++issued;
       }
       if (flags[0]) {
@@ -143,6 +150,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     const int nt = b * s.band_tiles + warp;
     const bool active = (warp < s.band_tiles) && (nt < s.tn);
     const int g = lane >> 2, t = lane & 3;
+    const GroupLane gl = make_group_lane(lane);
     const int jj = g >> 1, h = g & 1;
     float acc[2][TG][4];
 #pragma unroll
@@ -162,10 +170,12 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
       if (active) {
         const int kt = r0 + i;
-        const mtc_tile_desc d = s.tiles[(size_t)kt * s.tn + nt];
-        const uint8_t* rec = slots + (size_t)slot * p.slot_bytes + (d.record_off - row_off[kt]);
+        const uint8_t* sl = slots + (size_t)slot * p.slot_bytes;
+        const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[warp];
+        const uint32_t base = reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off;
+        const uint8_t* rec = sl + kDescBytes + (d.record_off - base);
         uint32_t R[4][4];
-        decode_group_w16(rec, d.n_leaves, d.prim_bytes, d.leaf_start, s.scale_words, lane, p.pow2e, R);
+        decode_group_w16(rec, d.n_leaves, d.prim_bytes, d.leaf_start, s.scale_words, gl, p.pow2e, dtab, R);
 #pragma unroll
         for (int di = 0; di < 2; ++di) {
           const int kl = i * kTile + 4 * (2 * t + di);
@@ -251,15 +261,15 @@ bool make_plan(const mtc_stream_desc* s, int M, int rows_per_unit, Plan* pl) {
   pl->rpu = rpu;
   pl->upb = (s->tk + rpu - 1) / rpu;
   pl->units = nb * pl->upb;
-  pl->slot_bytes = (s->max_row_bytes + 127u) & ~127u;
+  pl->slot_bytes = (kDescBytes + s->max_row_bytes + 127u) & ~127u;
   pl->x_stride = rpu * kTile + 8;
   const size_t xs = ((size_t)pl->tg * 8 * pl->x_stride * 2 + 127) & ~(size_t)127;
   const size_t budget = 96 * 1024;  // leaves room for two CTAs per SM
   const size_t slot = pl->slot_bytes ? pl->slot_bytes : 1;
-  int nst = (int)((budget > xs + 256 ? budget - xs - 256 : 0) / slot);
+  int nst = (int)((budget > xs + kHeadBytes ? budget - xs - kHeadBytes : 0) / slot);
   nst = max(2, min(nst, kMaxStages));
   pl->nst = nst;
-  pl->smem = 256 + xs + (size_t)nst * pl->slot_bytes;
+  pl->smem = kHeadBytes + xs + (size_t)nst * pl->slot_bytes;
   pl->ws_bytes = (size_t)pl->units * pl->tg * 8 * s->band_tiles * kTile * sizeof(float);
   return true;
 }

@@ -13,8 +13,9 @@
 //                   warp  4    producer: TMA of the Xp tile (SWIZZLE_128B) and
 //                              cp.async.bulk of the band's packed k-tile rows
 //                   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
-//                   warps 6-13 dequant: packed codes -> fp16 W tile in the
-//                              K-major SWIZZLE_128B layout the MMA reads
+//                   warps 6-21 dequant: one 32x32 tile each per stage,
+//                              packed codes -> fp16 W tile in the K-major
+//                              SWIZZLE_128B layout the MMA reads
 //                 Two 128x256 fp32 accumulators (all 512 TMEM columns) share
 //                 each dequantised W tile, so every weight is decoded once
 //                 per 256 tokens.  mbarriers link the stages; every wait is
@@ -35,12 +36,19 @@ constexpr int kEpiWarps = 4;
 constexpr int kProdWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kDeqWarp0 = 6;
-constexpr int kDeqWarps = 8;
+constexpr int kDeqWarps = 16;
 constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;
 constexpr uint32_t kABytes = BM * BK * 2;
 constexpr uint32_t kBBytes = BN * BK * 2;
 constexpr int kMaxS = 4;
 constexpr int kMaxP = 4;
+// Packed slot layout: [0, 256) tile descriptors of the stage's 2 k rows,
+// [256, 2304) class-sorted group list, [2304, 2320) entry count, then records.
+constexpr int kMaxGroups = 256;
+constexpr uint32_t kListOff = 256;
+constexpr uint32_t kCountOff = kListOff + 8 * kMaxGroups;
+constexpr uint32_t kHeadBytes = kCountOff + 16;
+constexpr int kClassGeneric = 7;
 
 struct PrefillParams {
   mtc_stream_desc s;
@@ -67,7 +75,9 @@ __device__ __forceinline__ uint32_t sw128_off(int n, int k) {
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base for the SWIZZLE_128B atoms; pointer arithmetic on
+  // the __shared__ array keeps the shared address space visible to the compiler
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = sA + p.S * kABytes;
   uint8_t* sP = sB + p.S * kBBytes;
@@ -81,6 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 1;
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
+  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // decoder table
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -100,6 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     flags[0] = 0;
     fence_barrier_init();
   }
+  if (warp == 0) load_dec_table(dtab, lane);
   if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, 512);
   tc::fence_before();
   __syncthreads();
@@ -128,13 +140,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
           const uint32_t off = row_off[r0];
           const uint32_t bytes = row_off[r1] - off;
-          if (bytes > p.pslot || (off & 15u) || (bytes & 15u)) {
+          const size_t stage = (size_t)band * p.nkb + kb;
+          const uint32_t count = s.stage_counts[stage];
+          if (bytes + kHeadBytes > p.pslot || (off & 15u) || (bytes & 15u) || count > (uint32_t)kMaxGroups) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
           }
-          mbar_expect_tx(&pfull[pst], bytes);
-          bulk_g2s(sP + pst * p.pslot, s.records + off, bytes, &pfull[pst]);
+          // slot: tile descriptors of both k rows | sorted group list | count | records
+          const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
+          uint8_t* dst = sP + pst * p.pslot;
+          const uint32_t lbytes = 16u * ((count + 1u) / 2u);
+          *reinterpret_cast<uint32_t*>(dst + kCountOff) = count;
+          mbar_expect_tx(&pfull[pst], bytes + 16u * width * (r1 - r0) + lbytes);
+          for (int r = r0; r < r1; ++r)
+            bulk_g2s(dst + 128 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles, 16u * width,
+                     &pfull[pst]);
+          if (lbytes) bulk_g2s(dst + kListOff, s.stage_lists + stage * kMaxGroups, lbytes, &pfull[pst]);
+          bulk_g2s(dst + kHeadBytes, s.records + off, bytes, &pfull[pst]);
         }
       }
       if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
@@ -178,14 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kDeqWarp0) {
     // ---------------------------------------------------------------- dequant
-    const int dw = warp - kDeqWarp0;  // tile column inside the band
-    const int g = lane >> 2, t = lane & 3;
-    const int jj = g >> 1, h = g & 1;
+    // Each warp takes 16 entries of the stage's class-sorted group list; lane
+    // pair (2e, 2e + 1) decodes the two column halves of entry e.  Sorted
+    // entries make most warps mode-uniform, so they run one specialised path.
+    const int dw = warp - kDeqWarp0;
+    const int h = lane & 1;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
-      const int band = tile % p.n_bands;
-      const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
-      const int nt = band * s.band_tiles + dw;
       for (int kb = 0; kb < p.nkb; ++kb, ++it) {
         const int st = it % p.S, pst = it % p.P;
         if (!mbar_wait(&pfull[pst], (it / p.P) & 1, p.timeout_ns)) {
@@ -197,26 +219,72 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         uint8_t* Bt = sB + st * kBBytes;
-        const uint32_t base_off = row_off[2 * kb];
-#pragma unroll 1
-        for (int r = 0; r < 2; ++r) {
-          const int kt = 2 * kb + r;
-          uint32_t R[4][4];
-          if (kt < s.tk && nt < s.tn) {
-            const mtc_tile_desc d = s.tiles[(size_t)kt * s.tn + nt];
-            const uint8_t* rec = sP + pst * p.pslot + (d.record_off - base_off);
-            decode_group_w16(rec, d.n_leaves, d.prim_bytes, d.leaf_start, s.scale_words, lane, p.pow2e, R);
-          } else {
+        const uint8_t* sl = sP + pst * p.pslot;
+        const uint32_t count = reinterpret_cast<const uint32_t*>(sl + kListOff)[kMaxGroups * 2];
+        const uint8_t* payload = sl + kHeadBytes;
+        const int idx = 16 * dw + (lane >> 1);
+        const bool valid = idx < (int)count;
+        const uint64_t ent = valid ? reinterpret_cast<const uint64_t*>(sl + kListOff)[idx] : 0ull;
+        const int cls = valid ? (int)((ent >> 48) & 15u) : -1;
+        const int cls0 = __shfl_sync(0xffffffffu, cls, 0);
+        const uint8_t* prim = payload + (uint32_t)(ent & 0xffffu);
+        const uint8_t* sec = payload + (uint32_t)((ent >> 16) & 0xffffu);
+        const uint32_t s2 = h2const((uint16_t)((ent >> 32) & 0xffffu));
+        const int ti = (int)((ent >> 52) & 15u), G = (int)((ent >> 56) & 15u);
+        uint32_t R[4][4];
+        if (__all_sync(0xffffffffu, !valid || cls == cls0) && cls0 != kClassGeneric) {
+          switch (cls0) {  // warp-uniform branch
+            case 1: decode_run4<2>(prim, sec, h, s2, R); break;
+            case 2: decode_run4<3>(prim, sec, h, s2, R); break;
+            case 3: decode_run4<4>(prim, sec, h, s2, R); break;
+            case 4: decode_run4<5>(prim, sec, h, s2, R); break;
+            case 5: decode_run4<6>(prim, sec, h, s2, R); break;
+            case 6: decode_run4<8>(prim, sec, h, s2, R); break;
+            default:
 #pragma unroll
-            for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
+              for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
           }
+        } else {
+          switch (cls) {  // class boundary inside the warp, or generic groups
+            case 1: decode_run4<2>(prim, sec, h, s2, R); break;
+            case 2: decode_run4<3>(prim, sec, h, s2, R); break;
+            case 3: decode_run4<4>(prim, sec, h, s2, R); break;
+            case 4: decode_run4<5>(prim, sec, h, s2, R); break;
+            case 5: decode_run4<6>(prim, sec, h, s2, R); break;
+            case 6: decode_run4<8>(prim, sec, h, s2, R); break;
+            case kClassGeneric: {
+              const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
+              const uint8_t* rec = payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
+              decode_group_generic(reinterpret_cast<const uint32_t*>(rec), d.leaf_start, G, prim, sec,
+                                   s.scale_words, h, p.pow2e, R);
+              break;
+            }
+            default:
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int di = k >> 1, dj = k & 1;
-            const int f0 = 32 * dw + 4 * (2 * jj + dj) + 2 * h;   // feature row of the B tile
-            const int k0 = 32 * r + 4 * (2 * t + di);             // k column inside the stage
-            *reinterpret_cast<uint2*>(Bt + sw128_off(f0, k0)) = make_uint2(R[k][0], R[k][1]);
-            *reinterpret_cast<uint2*>(Bt + sw128_off(f0 + 1, k0)) = make_uint2(R[k][2], R[k][3]);
+              for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
+          }
+        }
+        if (valid) {
+          // R[2 di + dj] = micro-block (2t + di, 2jj + dj) of group G: pairs 0,1
+          // feature 2h (k rows 0..3), pairs 2,3 feature 2h + 1; di selects k 0..3 / 4..7
+          const int r = ti >> 3, col = ti & 7;
+          const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
+          const int jj = ((G >> 2) & 1) << 1 | (G & 1);
+#pragma unroll
+          for (int dj = 0; dj < 2; ++dj) {
+            const int f = 32 * col + 4 * (2 * jj + dj) + 2 * h;
+            *reinterpret_cast<uint4*>(Bt + sw128_off(f, 32 * r + 8 * t)) =
+                make_uint4(R[dj][0], R[dj][1], R[2 + dj][0], R[2 + dj][1]);
+            *reinterpret_cast<uint4*>(Bt + sw128_off(f + 1, 32 * r + 8 * t)) =
+                make_uint4(R[dj][2], R[dj][3], R[2 + dj][2], R[2 + dj][3]);
+          }
+        }
+        if (2 * kb + 1 >= s.tk) {
+          // odd number of k-tile rows: the stage's second row is zero padding
+          const int tid_d = tid - kDeqWarp0 * 32;
+          for (int c = tid_d; c < BN * 4; c += kDeqWarps * 32) {
+            const int f = c >> 2, ch = 4 + (c & 3);
+            *reinterpret_cast<uint4*>(Bt + f * 128 + ((ch ^ (f & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
           }
         }
         fence_proxy_async();
@@ -340,10 +408,13 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
   pl->n_mblk = (M + BM - 1) / BM;
   pl->n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
   pl->n_tiles = pl->n_mblk * pl->n_bands;
-  pl->pslot = (2 * s->max_row_bytes + 127u) & ~127u;
+  pl->pslot = (kHeadBytes + 2 * s->max_row_bytes + 127u) & ~127u;
   const size_t cap = 227 * 1024;
-  const size_t fixed = 1024 /*align*/ + 256 /*barriers*/;
-  int S = kMaxS, P = 2;
+  const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/;
+  // Three A/B stages let dequant run two stages ahead of the MMA (absorbing
+  // the varying cost of mode mixes); packed-weight slots take what is left.
+  // (Measured: S=3/P=2 beats S=2/P=4 by 15% on a 4096x14336 layer.)
+  int S = 3, P = 2;
   while (S >= 2 && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)P * pl->pslot > cap) --S;
   if (S < 2) return false;
   while (P < kMaxP && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)(P + 1) * pl->pslot <= cap) ++P;
@@ -372,6 +443,8 @@ extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_
   clear_error();
   MTC_REQUIRE(s && X && Y && ws && s->records && s->tiles && s->row_off, "mtc_gemm_prefill: null pointer argument");
   MTC_REQUIRE(M >= 1, "mtc_gemm_prefill: M=%d", M);
+  MTC_REQUIRE(s->stage_lists && s->stage_counts,
+              "mtc_gemm_prefill: stage work lists missing (run mtc_repack_stage_lists first)");
   MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_gemm_prefill: bad leading dimensions");
   MTC_REQUIRE(s->band_tiles * kTile == BN, "mtc_gemm_prefill: stream band width %d tiles, kernel needs %d",
               s->band_tiles, BN / kTile);

@@ -263,10 +263,120 @@ __global__ void __launch_bounds__(256) fill_tiles(const uint8_t* __restrict__ ar
   }
 }
 
+// Classes of the prefill work lists: decode path of an 8x8 group.
+constexpr int kClassZero = 0;     // P0 leaf: writes zeros
+constexpr int kClassGeneric = 7;  // four 4x4 leaves, P16 or inexact fp16 scale
+
+__device__ __forceinline__ int class_of_mode(int m) {
+  switch (m) {
+    case 0: return kClassZero;
+    case 2: return 1;
+    case 3: return 2;
+    case 4: return 3;
+    case 5: return 4;
+    case 6: return 5;
+    case 8: return 6;
+    default: return kClassGeneric;
+  }
+}
+
+// One CTA of 256 threads per stage (band, k-tile rows 2kb and 2kb + 1);
+// thread i owns group G = i & 15 of tile (row i >> 7, column (i >> 4) & 7).
+__global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int nkb, uint64_t* __restrict__ lists,
+                                                          uint32_t* __restrict__ counts) {
+  __shared__ uint32_t cnt[8];
+  __shared__ uint32_t base[8];
+  const int stage = blockIdx.x;
+  const int band = stage / nkb, kb = stage % nkb;
+  const int i = threadIdx.x;
+  const int ti = i >> 4, G = i & 15;
+  const int r = ti >> 3, col = ti & 7;
+  const int kt = 2 * kb + r, nt = band * s.band_tiles + col;
+  const bool valid = kt < s.tk && nt < s.tn && col < s.band_tiles;
+  if (i < 8) cnt[i] = 0;
+  __syncthreads();
+  const float pow2e = ldexpf(1.0f, s.exp2);
+  const int sw = s.scale_words;
+  uint32_t v = 0, e0 = 0;
+  int l0 = 0;
+  bool single = true;
+  mtc_tile_desc d{};
+  if (valid) {
+    d = s.tiles[(size_t)kt * s.tn + nt];
+    const uint32_t* ltab = reinterpret_cast<const uint32_t*>(s.records + d.record_off);
+    l0 = leaf_of(d.leaf_start, 4 * G);
+    single = ((d.leaf_start >> (4 * G + 1)) & 7ull) == 0ull;
+    e0 = lt_entry(ltab, l0, sw);
+    if (single) {
+      v = 4u * ((uint32_t)lt_prim(e0) | ((uint32_t)lt_sec(e0) << 16));
+    } else {
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t e = lt_entry(ltab, l0 + k, sw);
+        v += (uint32_t)lt_prim(e) | ((uint32_t)lt_sec(e) << 16);
+      }
+    }
+  }
+  // exclusive scan over the 16 groups of the tile (16 consecutive lanes)
+  const int lane = i & 31;
+  uint32_t incl = v;
+#pragma unroll
+  for (int dl = 1; dl < 16; dl <<= 1) {
+    const uint32_t u = __shfl_up_sync(0xffffffffu, incl, dl);
+    if ((lane & 15) >= dl) incl += u;
+  }
+  const uint32_t ex = incl - v;
+  int cls = kClassGeneric;
+  uint64_t entry = 0;
+  if (valid) {
+    const uint32_t stage_base = s.row_off[(size_t)band * (s.tk + 1) + 2 * kb];
+    const uint32_t rec = d.record_off - stage_base;
+    const uint32_t prim = rec + pad16(4 * sw * d.n_leaves) + (ex & 0xffffu);
+    const uint32_t sec = rec + pad16(4 * sw * d.n_leaves) + pad16(d.prim_bytes) + (ex >> 16);
+    uint32_t scale16 = 0;
+    if (single) {
+      const uint32_t* ltab = reinterpret_cast<const uint32_t*>(s.records + d.record_off);
+      const int m = lt_mode(e0);
+      cls = class_of_mode(m);
+      const float sc = lt_scale_of(ltab, l0, sw) * pow2e;
+      const __half hs = __float2half_rn(sc);
+      if (lt_slow(e0) || __half2float(hs) != sc) cls = (m == 0) ? kClassZero : kClassGeneric;
+      scale16 = *reinterpret_cast<const uint16_t*>(&hs);
+    }
+    entry = (uint64_t)(prim & 0xffffu) | ((uint64_t)(sec & 0xffffu) << 16) | ((uint64_t)scale16 << 32) |
+            ((uint64_t)cls << 48) | ((uint64_t)ti << 52) | ((uint64_t)G << 56);
+  }
+  uint32_t rank = 0;
+  if (valid) rank = atomicAdd(&cnt[cls], 1u);
+  __syncthreads();
+  if (i == 0) {
+    uint32_t acc = 0;
+    for (int c = 0; c < 8; ++c) {
+      base[c] = acc;
+      acc += cnt[c];
+    }
+    counts[stage] = acc;
+  }
+  __syncthreads();
+  if (valid) lists[(size_t)stage * 256 + base[cls] + rank] = entry;
+}
+
 }  // namespace
 }  // namespace mtc
 
 using namespace mtc;
+
+extern "C" int mtc_repack_stage_lists(const mtc_stream_desc* s, uint64_t* lists, uint32_t* counts, void* stream) {
+  clear_error();
+  MTC_REQUIRE(s && lists && counts && s->tiles && s->row_off && s->records, "mtc_repack_stage_lists: null pointer");
+  MTC_REQUIRE(s->band_tiles == 8, "mtc_repack_stage_lists: band width %d (needs 8)", s->band_tiles);
+  MTC_REQUIRE(2ull * s->max_row_bytes < 65536ull, "mtc_repack_stage_lists: stage of %u bytes exceeds 16-bit offsets",
+              2 * s->max_row_bytes);
+  const int nkb = (s->tk + 1) / 2;
+  const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
+  stage_lists_kernel<<<nb * nkb, 256, 0, as_stream(stream)>>>(*s, nkb, lists, counts);
+  MTC_CHECK_LAUNCH("mtc_repack_stage_lists");
+  return MTC_OK;
+}
 
 extern "C" int mtc_repack_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn,
                                int32_t band_tiles, int32_t scale_words, mtc_tile_desc* tiles, uint32_t* row_off,

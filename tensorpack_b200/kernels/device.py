@@ -73,6 +73,14 @@ class DeviceStream:
             _lib.check(lib.mtc_repack_fill(d_arena.data_ptr(), arena.nbytes, d_leaves.data_ptr(),
                                            d_begin.data_ptr(), ctypes.byref(self.desc), self.records.data_ptr(),
                                            scratch.data_ptr(), st), "repack fill")
+            # class-sorted 8x8-group work lists of every prefill stage
+            n_stages = self.n_bands * ((tk + 1) // 2)
+            self.stage_lists = torch.empty(n_stages * 256, dtype=torch.int64, device=dev)
+            self.stage_counts = torch.empty(n_stages, dtype=torch.int32, device=dev)
+            self.desc.stage_lists = self.stage_lists.data_ptr()
+            self.desc.stage_counts = self.stage_counts.data_ptr()
+            _lib.check(lib.mtc_repack_stage_lists(ctypes.byref(self.desc), self.stage_lists.data_ptr(),
+                                                  self.stage_counts.data_ptr(), st), "repack stage lists")
             self.row_perm = None if mat.row_perm is None else torch.from_numpy(
                 np.asarray(mat.row_perm, dtype=np.int32)).to(dev)
             self.col_perm = None if mat.col_perm is None else torch.from_numpy(

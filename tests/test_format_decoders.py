@@ -156,3 +156,67 @@ def test_fp16_weight_rounding_is_single():
         if float(f16(s)) != float(s):
             continue
         assert f16(np.float64(q) * np.float64(f16(s))) == f16(np.float32(q) * s)
+
+
+def dec_row(mode):
+    """Python twin of make_dec_row (table of the mode-uniform decoder)."""
+    wp = 2 if mode in (2, 3) else (8 if mode == 8 else 4)
+    ws = 1 if mode in (3, 5) else (2 if mode == 6 else 0)
+    bias = float(1 << (mode - 1))
+    rows = []
+    for j in range(4):
+        if wp == 2:
+            pm, pos = 0x00030003 << (2 * j), 2 * j
+        elif wp == 4:
+            pm, pos = (0x00F000F0 if j & 1 else 0x000F000F), (4 if j & 1 else 0)
+        else:
+            pm, pos = 0x00FF00FF, 0
+        sm, cs = 0, 0.0
+        if ws == 1:
+            sm, cs = 0x00010001 << j, float(1 << wp) / (1 << j)
+        if ws == 2:
+            sm, cs = 0x00030003 << (2 * j), float(1 << wp) / (1 << (2 * j))
+        c = 1.0 / (1 << pos)
+        rows.append((pm, sm, c, cs, -1024.0 * cs - bias - 1024.0 * c))
+    return wp, ws, rows
+
+
+def decode_half_uniform(m, pw, sv, h):
+    """Python twin of decode_half_uniform (without the final scale multiply)."""
+    wp, ws, rows = dec_row(m)
+    words = {2: [pw[0]], 4: pw[:2], 8: pw}[wp]
+    if wp == 2:
+        A = B = words[0] >> (8 * h)
+    elif wp == 4:
+        A = B = words[h]
+    else:
+        A, B = words[2 * h], words[2 * h + 1]
+    x = [A, A >> (8 if wp == 8 else 0), B >> (8 if wp == 4 else 0), B >> (0 if wp == 2 else 8)]
+    S = 0
+    if ws == 1:
+        S = byte_perm_4140(sv & 0xFFFF) >> (4 * h)
+    if ws == 2:
+        S = sv >> (8 * h)
+    out = []
+    for j, (pm, sm, c, cs, K) in enumerate(rows):
+        for v in (c, cs, K):
+            assert _constant_exact(v), (m, j, v)
+        fp = lop_or(x[j], pm)
+        fs = lop_or(S, sm)
+        inner = (fma16(fs[0], cs, K), fma16(fs[1], cs, K))
+        out.append((fma16(fp[0], c, inner[0]), fma16(fp[1], c, inner[1])))
+    return out
+
+
+@pytest.mark.parametrize("m", [2, 3, 4, 5, 6, 8])
+def test_uniform_decoder_is_exact(m):
+    lo, hi = QR[m]
+    rng = np.random.default_rng(100 + m)
+    cases = [np.full((4, 4), v) for v in range(lo, hi + 1)]
+    cases += [rng.integers(lo, hi + 1, size=(4, 4)) for _ in range(200)]
+    for q in cases:
+        pw, sv = encode_mb(q, m)
+        for h in range(2):
+            for j, (a, b) in enumerate(decode_half_uniform(m, pw, sv, h)):
+                c, r = 2 * h + (j >> 1), 2 * (j & 1)
+                assert float(a) == q[r][c] and float(b) == q[r + 1][c], (m, h, j)
