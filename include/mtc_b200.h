@@ -187,6 +187,40 @@ MTC_API int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M
                              const int32_t* row_perm, const int32_t* col_perm_inv, float* Y,
                              int64_t ldy, void* ws, size_t ws_bytes, uint32_t* status, void* stream);
 
+/* The three stages mtc_gemm_prefill runs, for callers that fuse or time them
+ * separately (same workspace):
+ *   gather:  ws <- fp16 X[:, row_perm] (padded to tk*32 columns)
+ *   gemm:    fused dequant + tcgen05 GEMM of that; writes Y directly
+ *            (permuted_output = 0) or the permuted-column product into ws
+ *   scatter: Y[:, col_perm] <- the permuted-column product in ws */
+MTC_API int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                               const int32_t* row_perm, void* ws, size_t ws_bytes, uint32_t* status,
+                               void* stream);
+MTC_API int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, int64_t ldy,
+                             int32_t permuted_output, void* ws, size_t ws_bytes, uint32_t* status,
+                             void* stream);
+MTC_API int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32_t* col_perm_inv,
+                                float* Y, int64_t ldy, void* ws, size_t ws_bytes, void* stream);
+
+/* Row-wise column gather: Y[m][j] = row_m[pos[j]] with row_m the
+ * concatenation of nseg segments src[g*seg_stride + m*ldp + (0..seg_len-1)]
+ * (M rows, N output columns).  Used to assemble all-gathered column shards
+ * of a multi-GPU GEMM in original column order. */
+MTC_API int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ldp, int32_t nseg,
+                             int32_t seg_len, const int32_t* pos, int32_t N, int32_t M, float* Y,
+                             int64_t ldy, void* stream);
+
+/* GPU candidate search of the rate-distortion allocators (replaces the Numba
+ * _search_kernel / _search_mode, mtc/core/allocation.py:106-160, used by
+ * rd_candidates and QuadtreeRD): for every block_size x block_size block of
+ * the K x N fp32 matrix W (row-major) and precision `mode`, the scale among
+ * sign x alpha * amax / qmax (bf16-rounded when bf16_scales) minimising
+ * sum_r h_norm[r] * sum_c (w - q s)^2.  Writes (K/bs) x (N/bs) fp64
+ * distortions and fp32 scales; bit-identical to the reference. */
+MTC_API int mtc_rd_search(const float* W, int32_t K, int32_t N, int32_t block_size, const double* h_norm,
+                          int32_t mode, const float* alphas, int32_t n_alpha, int32_t bf16_scales,
+                          double* out_dist, float* out_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

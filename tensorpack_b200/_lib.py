@@ -55,6 +55,7 @@ SIGNATURES = {
                                 ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_fill": (c_i32, [c_p, c_u64, c_p, c_p, ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
     "mtc_repack_stage_lists": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
+    "mtc_rd_search": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p, c_i32, c_i32, c_p, c_p, c_p]),
     "mtc_dequant": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, c_i64, c_p]),
     "mtc_gemv_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemv": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_i32,
@@ -62,6 +63,10 @@ SIGNATURES = {
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemm_prefill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64,
                                  c_p, c_size, c_p, c_p]),
+    "mtc_prefill_gather": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_size, c_p, c_p]),
+    "mtc_prefill_gemm": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_i64, c_i32, c_p, c_size, c_p, c_p]),
+    "mtc_prefill_scatter": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_p, c_i64, c_p, c_size, c_p]),
+    "mtc_permute_rows": (c_i32, [c_p, c_i64, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_p, c_i64, c_p]),
 }
 
 _lock = threading.Lock()

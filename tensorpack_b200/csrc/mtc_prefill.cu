@@ -366,17 +366,36 @@ __global__ void __launch_bounds__(256) gather_x_kernel(const float* __restrict__
   if (bad) flag(status, MTC_STATUS_X_RANGE);
 }
 
-// Y[m][j] = Yp[m][ipc[j]]  (Y[:, pc] = Yp).  One CTA per row.
-__global__ void __launch_bounds__(512) permute_y_kernel(const float* __restrict__ Yp, long long ldp,
-                                                        const int32_t* __restrict__ ipc, int N,
-                                                        float* __restrict__ Y, long long ldy) {
+// Y[m][j] = row_m[pos[j]], where row_m is the concatenation of nseg segments
+// src[g * seg_stride + m * ldp + (0 .. seg_len)].  One CTA per row; the row
+// is staged in shared memory so reads and writes are both coalesced.  With
+// one segment and pos = inverse column permutation this is Y[:, pc] = Yp;
+// with one segment per rank it assembles all-gathered column shards.
+__global__ void __launch_bounds__(512) permute_rows_kernel(const float* __restrict__ src, long long seg_stride,
+                                                           long long ldp, int nseg, int seg_len,
+                                                           const int32_t* __restrict__ pos, int N,
+                                                           float* __restrict__ Y, long long ldy) {
   extern __shared__ float row[];
   const int m = blockIdx.x;
-  const float* src = Yp + (long long)m * ldp;
-  for (int n = threadIdx.x; n < N; n += blockDim.x) row[n] = src[n];
+  for (int g = 0; g < nseg; ++g) {
+    const float* sg = src + g * seg_stride + (long long)m * ldp;
+    for (int c = threadIdx.x; c < seg_len; c += blockDim.x) row[g * seg_len + c] = sg[c];
+  }
   __syncthreads();
   float* dst = Y + (long long)m * ldy;
-  for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = row[ipc[j]];
+  for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = row[pos[j]];
+}
+
+int launch_permute_rows(const float* src, long long seg_stride, long long ldp, int nseg, int seg_len,
+                        const int32_t* pos, int N, int M, float* Y, long long ldy, cudaStream_t st) {
+  const size_t sm = (size_t)nseg * seg_len * 4;
+  MTC_REQUIRE(sm <= 227 * 1024, "permute: a staged row of %zu bytes exceeds shared memory", sm);
+  if (sm > 48 * 1024)
+    MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "permute: smem attribute");
+  permute_rows_kernel<<<M, 512, sm, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, Y, ldy);
+  MTC_CHECK_LAUNCH("permute_rows");
+  return MTC_OK;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -437,47 +456,95 @@ extern "C" size_t mtc_prefill_workspace_bytes(const mtc_stream_desc* s, int32_t 
   return pl.xp_bytes + pl.yp_bytes;
 }
 
+namespace {
+
+int check_prefill(const mtc_stream_desc* s, int32_t M, bool permuted, void* ws, size_t ws_bytes, PrefillPlan* pl,
+                  const char* who) {
+  MTC_REQUIRE(s && ws && s->records && s->tiles && s->row_off, "%s: null pointer argument", who);
+  MTC_REQUIRE(M >= 1, "%s: M=%d", who, M);
+  MTC_REQUIRE(s->band_tiles * kTile == BN, "%s: stream band width %d tiles, kernel needs %d", who, s->band_tiles,
+              BN / kTile);
+  MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "%s: workspace not 256-byte aligned", who);
+  MTC_REQUIRE(plan_prefill(s, M, permuted, pl), "%s: a k-tile row of %u bytes does not fit shared memory", who,
+              s->max_row_bytes);
+  if (ws_bytes < pl->xp_bytes + pl->yp_bytes) {
+    set_error("%s: workspace %zu bytes, need %zu", who, ws_bytes, pl->xp_bytes + pl->yp_bytes);
+    return MTC_ERR_WORKSPACE;
+  }
+  return MTC_OK;
+}
+
+}  // namespace
+
+extern "C" int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                                  const int32_t* row_perm, void* ws, size_t ws_bytes, uint32_t* status,
+                                  void* stream) {
+  clear_error();
+  PrefillPlan pl;
+  int rc = check_prefill(s, M, false, ws, ws_bytes, &pl, "mtc_prefill_gather");
+  if (rc != MTC_OK) return rc;
+  MTC_REQUIRE(X && ldx >= s->K, "mtc_prefill_gather: bad activations");
+  MTC_REQUIRE((size_t)s->K * 4 <= 200 * 1024, "mtc_prefill_gather: K=%d above the 51200 row-staged limit", s->K);
+  const size_t sm = (size_t)s->K * 4;
+  if (sm > 48 * 1024)
+    MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "mtc_prefill_gather: smem attribute");
+  gather_x_kernel<<<M, 256, sm, as_stream(stream)>>>(X, ldx, s->K, pl.Kp, row_perm, static_cast<__half*>(ws),
+                                                     status);
+  MTC_CHECK_LAUNCH("mtc_prefill_gather");
+  return MTC_OK;
+}
+
+extern "C" int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32_t* col_perm_inv, float* Y,
+                                   int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  PrefillPlan pl;
+  int rc = check_prefill(s, M, true, ws, ws_bytes, &pl, "mtc_prefill_scatter");
+  if (rc != MTC_OK) return rc;
+  MTC_REQUIRE(Y && col_perm_inv && ldy >= s->N, "mtc_prefill_scatter: bad output");
+  const float* Yp = reinterpret_cast<const float*>(static_cast<const uint8_t*>(ws) + pl.xp_bytes);
+  return launch_permute_rows(Yp, 0, pl.Np, 1, s->N, col_perm_inv, s->N, M, Y, ldy, as_stream(stream));
+}
+
+extern "C" int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ldp, int32_t nseg, int32_t seg_len,
+                                const int32_t* pos, int32_t N, int32_t M, float* Y, int64_t ldy, void* stream) {
+  clear_error();
+  MTC_REQUIRE(src && pos && Y && nseg >= 1 && seg_len >= 1 && N >= 1 && M >= 1 && ldy >= N,
+              "mtc_permute_rows: bad arguments");
+  return launch_permute_rows(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, as_stream(stream));
+}
+
 extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                                 const int32_t* row_perm, const int32_t* col_perm_inv, float* Y, int64_t ldy,
                                 void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
   clear_error();
-  MTC_REQUIRE(s && X && Y && ws && s->records && s->tiles && s->row_off, "mtc_gemm_prefill: null pointer argument");
-  MTC_REQUIRE(M >= 1, "mtc_gemm_prefill: M=%d", M);
-  MTC_REQUIRE(s->stage_lists && s->stage_counts,
-              "mtc_gemm_prefill: stage work lists missing (run mtc_repack_stage_lists first)");
-  MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_gemm_prefill: bad leading dimensions");
-  MTC_REQUIRE(s->band_tiles * kTile == BN, "mtc_gemm_prefill: stream band width %d tiles, kernel needs %d",
-              s->band_tiles, BN / kTile);
-  MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "mtc_gemm_prefill: workspace not 256-byte aligned");
+  int rc = mtc_prefill_gather(s, X, M, ldx, row_perm, ws, ws_bytes, status, stream);
+  if (rc != MTC_OK) return rc;
+  rc = mtc_prefill_gemm(s, M, Y, ldy, col_perm_inv != nullptr ? 1 : 0, ws, ws_bytes, status, stream);
+  if (rc != MTC_OK) return rc;
+  if (col_perm_inv) return mtc_prefill_scatter(s, M, col_perm_inv, Y, ldy, ws, ws_bytes, stream);
+  return MTC_OK;
+}
+
+extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, int64_t ldy, int32_t permuted_output,
+                                void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
+  clear_error();
   PrefillPlan pl;
-  MTC_REQUIRE(plan_prefill(s, M, col_perm_inv != nullptr, &pl),
-              "mtc_gemm_prefill: a k-tile row of %u bytes does not fit shared memory", s->max_row_bytes);
-  if (ws_bytes < pl.xp_bytes + pl.yp_bytes) {
-    set_error("mtc_gemm_prefill: workspace %zu bytes, need %zu", ws_bytes, pl.xp_bytes + pl.yp_bytes);
-    return MTC_ERR_WORKSPACE;
-  }
-  MTC_REQUIRE((size_t)s->K * 4 <= 200 * 1024 && (size_t)s->N * 4 <= 200 * 1024,
-              "mtc_gemm_prefill: K=%d / N=%d above the 51200 supported by the row-staged gather/permute", s->K,
-              s->N);
+  int rc = check_prefill(s, M, permuted_output != 0, ws, ws_bytes, &pl, "mtc_prefill_gemm");
+  if (rc != MTC_OK) return rc;
+  MTC_REQUIRE(s->stage_lists && s->stage_counts,
+              "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_lists first)");
+  MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
+  const bool col_perm_inv = permuted_output != 0;
   EncodeTiledFn enc = encode_tiled();
   if (!enc) {
-    set_error("mtc_gemm_prefill: cuTensorMapEncodeTiled unavailable from the driver");
+    set_error("mtc_prefill_gemm: cuTensorMapEncodeTiled unavailable from the driver");
     return MTC_ERR_CUDA;
   }
   cudaStream_t st = as_stream(stream);
   __half* Xp = static_cast<__half*>(ws);
   float* Yp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.xp_bytes);
-
-  // 1. gather + fp16 cast of the activations
-  {
-    const size_t sm = (size_t)s->K * 4;
-    if (sm > 48 * 1024)
-      MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                     "mtc_gemm_prefill: gather smem");
-    gather_x_kernel<<<M, 256, sm, st>>>(X, ldx, s->K, pl.Kp, row_perm, Xp, status);
-    MTC_CHECK_LAUNCH("mtc_gemm_prefill: gather_x");
-  }
-  // 2. TMA descriptor of Xp: fp16 [M][Kp], box 64 (k) x 256 (rows), 128-byte swizzle
+  // TMA descriptor of Xp: fp16 [M][Kp], box 64 (k) x 256 (rows), 128-byte swizzle
   CUtensorMap tmap;
   {
     cuuint64_t dims[2] = {(cuuint64_t)pl.Kp, (cuuint64_t)M};
@@ -488,11 +555,10 @@ extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
-      set_error("mtc_gemm_prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+      set_error("mtc_prefill_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
       return MTC_ERR_CUDA;
     }
   }
-  // 3. fused dequant + tcgen05 GEMM
   PrefillParams p;
   p.s = *s;
   p.M = M;
@@ -512,18 +578,9 @@ extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   MTC_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
-                 "mtc_gemm_prefill: smem attribute");
+                 "mtc_prefill_gemm: smem attribute");
   const int grid = pl.n_tiles < sms ? pl.n_tiles : sms;
   prefill_kernel<<<grid, kThreads, pl.smem, st>>>(tmap, p);
-  MTC_CHECK_LAUNCH("mtc_gemm_prefill: prefill");
-  // 4. output column permutation
-  if (col_perm_inv) {
-    const size_t sm = (size_t)s->N * 4;
-    if (sm > 48 * 1024)
-      MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                     "mtc_gemm_prefill: permute smem");
-    permute_y_kernel<<<M, 512, sm, st>>>(Yp, pl.Np, col_perm_inv, s->N, Y, ldy);
-    MTC_CHECK_LAUNCH("mtc_gemm_prefill: permute_y");
-  }
+  MTC_CHECK_LAUNCH("mtc_prefill_gemm");
   return MTC_OK;
 }

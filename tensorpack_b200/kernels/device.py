@@ -134,20 +134,50 @@ class DeviceStream:
                                 _stream(self.device)), "gemv")
         return Y
 
-    def prefill(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
-        """Y = X @ W for any M (fused dequant + tcgen05 kernel; used for M > 16)."""
+    def prefill_workspace(self, M: int) -> torch.Tensor:
         lib = _lib.load()
-        M = X.shape[0]
         permuted = 1 if self.col_perm_inv is not None else 0
         need = int(lib.mtc_prefill_workspace_bytes(ctypes.byref(self.desc), M, permuted))
         ws = self._ws.get("prefill")
         if ws is None or ws.numel() < need:
             ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
             self._ws["prefill"] = ws
+        return ws
+
+    def prefill(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
+        """Y = X @ W for any M (fused dequant + tcgen05 kernel; used for M > 16)."""
+        lib = _lib.load()
+        M = X.shape[0]
+        ws = self.prefill_workspace(M)
         _lib.check(lib.mtc_gemm_prefill(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
                                         _ptr(self.col_perm_inv), Y.data_ptr(), Y.stride(0), ws.data_ptr(),
                                         ws.numel(), self.status.data_ptr(), _stream(self.device)), "prefill")
         return Y
+
+    # The three prefill stages, for callers that time or fuse them separately.
+    def prefill_gather(self, X: torch.Tensor):
+        lib = _lib.load()
+        ws = self.prefill_workspace(X.shape[0])
+        _lib.check(lib.mtc_prefill_gather(ctypes.byref(self.desc), X.data_ptr(), X.shape[0], X.stride(0),
+                                          _ptr(self.row_perm), ws.data_ptr(), ws.numel(), self.status.data_ptr(),
+                                          _stream(self.device)), "prefill gather")
+
+    def prefill_gemm(self, M: int, Y: torch.Tensor):
+        lib = _lib.load()
+        ws = self.prefill_workspace(M)
+        permuted = 1 if self.col_perm_inv is not None else 0
+        _lib.check(lib.mtc_prefill_gemm(ctypes.byref(self.desc), M, Y.data_ptr(), Y.stride(0), permuted,
+                                        ws.data_ptr(), ws.numel(), self.status.data_ptr(), _stream(self.device)),
+                   "prefill gemm")
+
+    def prefill_scatter(self, M: int, Y: torch.Tensor):
+        if self.col_perm_inv is None:
+            return
+        lib = _lib.load()
+        ws = self.prefill_workspace(M)
+        _lib.check(lib.mtc_prefill_scatter(ctypes.byref(self.desc), M, self.col_perm_inv.data_ptr(), Y.data_ptr(),
+                                           Y.stride(0), ws.data_ptr(), ws.numel(), _stream(self.device)),
+                   "prefill scatter")
 
     def matmul(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
         """Y = X @ W, picking the decode kernel for M <= 16 and the tensor-core
