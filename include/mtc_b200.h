@@ -174,6 +174,23 @@ MTC_API int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int64_
              int32_t rows_per_unit, void* ws, size_t ws_bytes, uint32_t* counters,
              uint32_t* status, void* stream);
 
+/* Decode GEMM (M <= 16) that allocates nothing and takes no workspace.  No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they run a step (inside a graph capture or an allocator
+ * hook, or a plugin whose host framework only hands over inputs and
+ * outputs).  Same arguments and result as mtc_gemv minus the scratch; the
+ * split-K partial sums and band tickets live in an 8 MiB array built into
+ * the library (held on every GPU that loads it until process exit), which
+ * limits the matrix to 4096 column bands (N <= 1,048,576) and to partial
+ * sums that fit after raising the rows per split-K unit; larger requests
+ * fail with MTC_ERR_WORKSPACE.  All calls on a device share that array, so
+ * calls that overlap on the GPU race; calls ordered on one stream are safe.
+ * The first call on each device looks up the array's address: make it
+ * before any stream capture. */
+MTC_API int mtc_gemv_static(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                            const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
+                            uint32_t* status, void* stream);
+
 /* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
  * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,
  * gemm.py:541-574, and permutation.py:15-21).  Takes the INVERSE column

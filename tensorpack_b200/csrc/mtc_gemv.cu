@@ -342,3 +342,90 @@ extern "C" int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int
   MTC_CHECK_LAUNCH("mtc_gemv");
   return MTC_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Decode GEMM without caller-provided scratch.
+//
+// Some callers cannot allocate device memory at the point where they run a
+// decode step: code inside a CUDA-graph capture or an allocator hook, a
+// plugin whose host framework owns the device heap and hands it only input
+// and output buffers, or a real-time loop that must not take the allocator's
+// lock.  mtc_gemv_static serves them: it runs the same split-K kernel as
+// mtc_gemv, with its scratch (the partial sums of the split-K units and the
+// per-band tickets) taken from the fixed array below instead of from a
+// workspace argument.  It calls no cudaMalloc / cudaFree.
+//
+// Limits and sharing:
+//   * kStaticScratchBytes (8 MiB) of device memory per GPU that loads this
+//     library, held until the process exits;
+//   * band tickets for up to kStaticMaxBands column bands (N <= 1,048,576);
+//   * the split-K row count per unit is raised until the partial sums fit;
+//     a matrix whose partials cannot fit even then is rejected;
+//   * every call on a device shares the array: calls that overlap on the GPU
+//     (different streams, no ordering between them) race and corrupt each
+//     other's results.  Calls on one stream, or otherwise ordered, are safe.
+//   * the first call on each device looks up the array's device address
+//     (cudaGetSymbolAddress); make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace mtc {
+namespace {
+constexpr size_t kStaticScratchBytes = 8u << 20;
+constexpr int kStaticMaxBands = 4096;
+constexpr size_t kStaticTicketBytes = kStaticMaxBands * sizeof(uint32_t);
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+}  // namespace
+}  // namespace mtc
+
+#include <mutex>
+
+extern "C" int mtc_gemv_static(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                               const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
+                               uint32_t* status, void* stream) {
+  clear_error();
+  MTC_REQUIRE(s && X && Y && s->records && s->tiles && s->row_off, "mtc_gemv_static: null pointer argument");
+  MTC_REQUIRE(M >= 1 && M <= 16, "mtc_gemv_static: M=%d outside 1..16", M);
+  MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_gemv_static: bad leading dimensions");
+  MTC_REQUIRE(s->band_tiles == kConsumerWarps, "mtc_gemv_static: stream band width %d, kernel needs %d",
+              s->band_tiles, kConsumerWarps);
+  const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
+  MTC_REQUIRE(nb <= kStaticMaxBands, "mtc_gemv_static: %d column bands exceed the static limit of %d (N <= %d)", nb,
+              kStaticMaxBands, kStaticMaxBands * 256);
+
+  // Device address of the static array, looked up once per device.
+  static std::mutex mu;
+  static void* addr[256] = {nullptr};
+  int dev = 0;
+  MTC_CHECK_CUDA(cudaGetDevice(&dev), "mtc_gemv_static: cudaGetDevice");
+  MTC_REQUIRE(dev >= 0 && dev < 256, "mtc_gemv_static: device index %d", dev);
+  uint8_t* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "mtc_gemv_static: cudaGetSymbolAddress");
+      addr[dev] = p;
+    }
+    base = static_cast<uint8_t*>(addr[dev]);
+  }
+  uint32_t* tickets = reinterpret_cast<uint32_t*>(base);
+  void* partials = base + kStaticTicketBytes;
+  const size_t cap = kStaticScratchBytes - kStaticTicketBytes;
+
+  // Fewest rows per unit whose partial sums fit the array.
+  Plan pl;
+  make_plan(s, M, 0, &pl);
+  int rpu = pl.rpu;
+  while (pl.ws_bytes > cap && rpu < s->tk) {
+    rpu = rpu * 2 < s->tk ? rpu * 2 : s->tk;
+    make_plan(s, M, rpu, &pl);
+  }
+  if (pl.ws_bytes > cap) {
+    set_error("mtc_gemv_static: partial sums need %zu bytes, static scratch holds %zu", pl.ws_bytes, cap);
+    return MTC_ERR_WORKSPACE;
+  }
+  // Tickets must start at zero; a call that failed may have left some set.
+  cudaStream_t st = as_stream(stream);
+  MTC_CHECK_CUDA(cudaMemsetAsync(tickets, 0, nb * sizeof(uint32_t), st), "mtc_gemv_static: clear tickets");
+  return mtc_gemv(s, X, M, ldx, row_perm, col_perm, Y, ldy, rpu, partials, cap, tickets, status, stream);
+}
