@@ -105,11 +105,13 @@ typedef struct mtc_stream_desc {
   uint64_t record_bytes;         /* total bytes of `records` */
   uint32_t max_row_bytes;        /* largest k-tile row of any band */
   int32_t scale_words;           /* 1: bf16 scale in the entry, 2: extra fp32 scale word */
-  /* Prefill work lists (NULL until mtc_repack_stage_lists builds them): for
-   * every (band, stage of two k-tile rows), up to 256 8x8-group entries
-   * sorted by decode class, and their count. */
-  const uint64_t* stage_lists;   /* [n_bands * n_stages * 256] */
-  const uint32_t* stage_counts;  /* [n_bands * n_stages] */
+  /* Prefill work lists (NULL until mtc_repack_stage_plan / _fill build
+   * them), one list per (band, stage of two k-tile rows), CSR layout. */
+  const uint64_t* stage_lists;   /* entries of all stages */
+  const uint32_t* stage_counts;  /* [n_bands * n_stages]: group entries | micro-block entries << 16 */
+  const uint32_t* stage_offsets; /* [n_bands * n_stages + 1]: first entry of each stage */
+  uint32_t max_stage_bytes;      /* largest staged footprint: 256 + list + records */
+  uint32_t pad_;
 } mtc_stream_desc;
 
 MTC_API int mtc_abi_version(void);
@@ -138,17 +140,24 @@ MTC_API int mtc_repack_fill(const uint8_t* arena, uint64_t arena_bytes, const mt
                     const uint32_t* tile_leaf_begin, const mtc_stream_desc* s, uint8_t* records,
                     uint32_t* scratch_u32, void* stream);
 
-/* Repack step 3 (prefill only): for every stage (band, pair of k-tile rows)
- * write the stage's 8x8 groups as 64-bit entries sorted by decode class
- * (P0, P2, P3, P4, P5, P6, P8, then groups needing the generic per-block
- * path), so prefill dequant warps take mode-uniform batches.  Entry bits:
- * 0-15 primary-plane offset and 16-31 secondary-plane offset (bytes from the
- * stage's first record), 32-47 fp16 bits of scale * 2^exp2, 48-51 class,
- * 52-55 tile within the stage (row * 8 + column), 56-59 group (Z order).
- * `lists` holds n_bands * n_stages * 256 entries, `counts` one word per
- * stage (n_stages = ceil(tk / 2)).  Uses s->tiles, s->row_off, s->records. */
-MTC_API int mtc_repack_stage_lists(const mtc_stream_desc* s, uint64_t* lists, uint32_t* counts,
-                                   void* stream);
+/* Repack step 3 (prefill only): per stage (band, pair of k-tile rows) a work
+ * list of 64-bit entries.  An 8x8 group covered by one leaf is one "group"
+ * entry; a group of four 4x4 leaves becomes four "micro-block" entries.  Group
+ * entries come first, then micro-block entries, each sorted by decode class
+ * (0 = P0, 1..6 = P2, P3, P4, P5, P6, P8, 7 = generic: P16 or a scale not
+ * exact in fp16), so prefill dequant warps take mode-uniform work.  Entry
+ * bits: 0-15 primary-plane and 16-31 secondary-plane byte offsets from the
+ * stage's first record, 32-47 fp16 bits of scale * 2^exp2, 48-51 class,
+ * 52-55 tile in the stage (row * 8 + column), 56-59 group (Z order),
+ * 60-61 micro-block in the group, 62 micro-block entry.
+ * plan: writes `counts` (group | micro-block << 16 per stage) and CSR
+ *       `offsets` (n_stages + 1), returns out_host = {total entries, largest
+ *       staged footprint}; `scratch_u32` holds n_stages + 2 words; syncs.
+ * fill: writes the entries into `lists` (total entries). */
+MTC_API int mtc_repack_stage_plan(const mtc_stream_desc* s, uint32_t* counts, uint32_t* offsets,
+                                  uint32_t* scratch_u32, uint64_t* out_host, void* stream);
+MTC_API int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint64_t* lists,
+                                  void* stream);
 
 /* Exact dequantisation (replaces MTCMatrix.to_array, gemm.py:510-538, and
  * qt_dequant / permuted_qt_dequant, quadtree.py:157-171, permutation.py:

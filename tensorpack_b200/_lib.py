@@ -40,11 +40,12 @@ class StreamDesc(ctypes.Structure):
         ("K", c_i32), ("N", c_i32), ("tk", c_i32), ("tn", c_i32),
         ("band_tiles", c_i32), ("exp2", c_i32),
         ("record_bytes", c_u64), ("max_row_bytes", c_u32), ("scale_words", c_i32),
-        ("stage_lists", c_p), ("stage_counts", c_p),
+        ("stage_lists", c_p), ("stage_counts", c_p), ("stage_offsets", c_p),
+        ("max_stage_bytes", c_u32), ("pad_", c_u32),
     ]
 
 
-assert ctypes.sizeof(StreamDesc) == 80
+assert ctypes.sizeof(StreamDesc) == 96
 
 # name -> (restype, argtypes); every symbol declared in include/mtc_b200.h.
 SIGNATURES = {
@@ -54,7 +55,8 @@ SIGNATURES = {
     "mtc_repack_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p,
                                 ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_fill": (c_i32, [c_p, c_u64, c_p, c_p, ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
-    "mtc_repack_stage_lists": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
+    "mtc_repack_stage_plan": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, ctypes.POINTER(c_u64), c_p]),
+    "mtc_repack_stage_fill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
     "mtc_rd_search": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p, c_i32, c_i32, c_p, c_p, c_p]),
     "mtc_dequant": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, c_i64, c_p]),
     "mtc_gemv_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),

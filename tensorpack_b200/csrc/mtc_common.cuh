@@ -450,6 +450,16 @@ __device__ __forceinline__ void decode_group_generic(const uint32_t* ltab, uint6
   }
 }
 
+// One micro-block half of a known mode, scaled: four fp16x2 weight pairs.
+template <int MODE>
+__device__ __forceinline__ void decode_mb_half(const uint8_t* prim, const uint8_t* sec, int h, uint32_t s2,
+                                               uint32_t r[4]) {
+  uint32_t q[4];
+  decode_half_codes(MODE, prim, sec, h, q);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r[j] = hmul2u(q[j], s2);
+}
+
 __device__ __forceinline__ uint32_t half2_bits(float v) {
   __half x = __float2half_rn(v);
   return h2const(*reinterpret_cast<uint16_t*>(&x));

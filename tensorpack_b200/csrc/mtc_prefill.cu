@@ -41,13 +41,13 @@ constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;
 constexpr uint32_t kABytes = BM * BK * 2;
 constexpr uint32_t kBBytes = BN * BK * 2;
 constexpr int kMaxS = 4;
-constexpr int kMaxP = 4;
-// Packed slot layout: [0, 256) tile descriptors of the stage's 2 k rows,
-// [256, 2304) class-sorted group list, [2304, 2320) entry count, then records.
-constexpr int kMaxGroups = 256;
-constexpr uint32_t kListOff = 256;
-constexpr uint32_t kCountOff = kListOff + 8 * kMaxGroups;
-constexpr uint32_t kHeadBytes = kCountOff + 16;
+// Packed data of each stage sits contiguously in a shared-memory byte ring:
+// [256 B tile descriptors of the stage's 2 k rows][work list][records].
+// Stages have very different sizes (MTC-QT-P puts the high-precision columns
+// in the last bands), so a ring keeps several typical stages in flight where
+// fixed slots sized for the largest one would fit a single stage.
+constexpr int kRingSlots = 8;          // stages in flight at most
+constexpr uint32_t kDescBytes = 256;
 constexpr int kClassGeneric = 7;
 
 struct PrefillParams {
@@ -57,8 +57,8 @@ struct PrefillParams {
   long long ldy;
   uint32_t* status;
   int n_bands, n_tiles, nkb;
-  int S, P;
-  uint32_t pslot;
+  int S;
+  uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
 };
@@ -81,17 +81,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + p.S * kABytes;
   uint8_t* sP = sB + p.S * kBBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.P * p.pslot);
-  uint64_t* full_ab = bars;              // [S]
-  uint64_t* empty_ab = full_ab + kMaxS;  // [S]
-  uint64_t* pfull = empty_ab + kMaxS;    // [P]
-  uint64_t* pempty = pfull + kMaxP;      // [P]
-  uint64_t* acc_full = pempty + kMaxP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
+  uint64_t* full_ab = bars;                   // [S]
+  uint64_t* empty_ab = full_ab + kMaxS;       // [S]
+  uint64_t* pfull = empty_ab + kMaxS;         // [kRingSlots]
+  uint64_t* pempty = pfull + kRingSlots;      // [kRingSlots]
+  uint64_t* acc_full = pempty + kRingSlots;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
-  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // decoder table
+  uint32_t* pmeta = tmem_slot + 4;            // [kRingSlots][4]: ring offset, counts, list bytes
+  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 512);  // decoder table
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_ab[i], 1 + kDeqWarps);
       mbar_init(&empty_ab[i], 1);
     }
-    for (int i = 0; i < p.P; ++i) {
+    for (int i = 0; i < kRingSlots; ++i) {
       mbar_init(&pfull[i], 1);
       mbar_init(&pempty[i], kDeqWarps);
     }
@@ -122,42 +123,70 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       uint32_t it = 0;
+      uint32_t oldest = 0;                              // oldest stage not yet known to be released
+      unsigned long long ring_head = 0;                 // monotonic byte position in the ring
+      unsigned long long ring_start[kRingSlots];        // start position of each stage in flight
       for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
         const int mblk = tile / p.n_bands, band = tile % p.n_bands;
         const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
-          const int st = it % p.S, pst = it % p.P;
+          const int st = it % p.S;
           if (it >= (uint32_t)p.S && !mbar_wait(&empty_ab[st], ((it / p.S) & 1) ^ 1, p.timeout_ns)) {
             flags[0] = 1;
             break;
           }
           mbar_expect_tx(&full_ab[st], kABytes);
           tc::tma_load_2d(sA + st * kABytes, &tmap_x, kb * BK, mblk * BM, &full_ab[st]);
-          if (it >= (uint32_t)p.P && !mbar_wait(&pempty[pst], ((it / p.P) & 1) ^ 1, p.timeout_ns)) {
-            flags[0] = 1;
-            break;
-          }
+          // Packed data of the stage goes to the byte ring as one contiguous
+          // piece: tile descriptors (256 B) | work list | records.  Its ring
+          // range must be free: release older stages (FIFO) until it is.
           const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
           const uint32_t off = row_off[r0];
           const uint32_t bytes = row_off[r1] - off;
           const size_t stage = (size_t)band * p.nkb + kb;
-          const uint32_t count = s.stage_counts[stage];
-          if (bytes + kHeadBytes > p.pslot || (off & 15u) || (bytes & 15u) || count > (uint32_t)kMaxGroups) {
+          const uint32_t cnt = s.stage_counts[stage];
+          const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
+          const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
+          const uint32_t need = kDescBytes + lbytes + bytes;
+          if (need > p.ring_bytes || (off & 15u) || (bytes & 15u)) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
           }
-          // slot: tile descriptors of both k rows | sorted group list | count | records
+          unsigned long long pos = ring_head;
+          if ((pos % p.ring_bytes) + need > p.ring_bytes) pos = (pos / p.ring_bytes + 1) * p.ring_bytes;
+          // live bytes are [ring_start[oldest], ring_head): the new piece must
+          // end within one ring length of the oldest live stage's start
+          bool ok = true;
+          while (it - oldest >= (uint32_t)kRingSlots ||
+                 (oldest != it && ring_start[oldest % kRingSlots] + p.ring_bytes < pos + need)) {
+            if (!mbar_wait(&pempty[oldest % kRingSlots], (oldest / kRingSlots) & 1, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            ++oldest;
+          }
+          if (!ok) {
+            flags[0] = 1;
+            break;
+          }
+          const int ps = it % kRingSlots;
+          ring_start[ps] = pos;
+          ring_head = pos + need;
+          const uint32_t start = (uint32_t)(pos % p.ring_bytes);
+          pmeta[4 * ps + 0] = start;
+          pmeta[4 * ps + 1] = cnt;
+          pmeta[4 * ps + 2] = lbytes;
           const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
-          uint8_t* dst = sP + pst * p.pslot;
-          const uint32_t lbytes = 16u * ((count + 1u) / 2u);
-          *reinterpret_cast<uint32_t*>(dst + kCountOff) = count;
-          mbar_expect_tx(&pfull[pst], bytes + 16u * width * (r1 - r0) + lbytes);
+          uint8_t* dst = sP + start;
+          mbar_expect_tx(&pfull[ps], bytes + 16u * width * (r1 - r0) + 8u * ((n_ent + 1u) & ~1u));
           for (int r = r0; r < r1; ++r)
             bulk_g2s(dst + 128 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles, 16u * width,
-                     &pfull[pst]);
-          if (lbytes) bulk_g2s(dst + kListOff, s.stage_lists + stage * kMaxGroups, lbytes, &pfull[pst]);
-          bulk_g2s(dst + kHeadBytes, s.records + off, bytes, &pfull[pst]);
+                     &pfull[ps]);
+          if (n_ent)
+            bulk_g2s(dst + kDescBytes, s.stage_lists + s.stage_offsets[stage], 8u * ((n_ent + 1u) & ~1u),
+                     &pfull[ps]);
+          bulk_g2s(dst + kDescBytes + lbytes, s.records + off, bytes, &pfull[ps]);
         }
       }
       if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
@@ -201,16 +230,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kDeqWarp0) {
     // ---------------------------------------------------------------- dequant
-    // Each warp takes 16 entries of the stage's class-sorted group list; lane
-    // pair (2e, 2e + 1) decodes the two column halves of entry e.  Sorted
-    // entries make most warps mode-uniform, so they run one specialised path.
+    // The stage's work list holds group entries (one 8x8 leaf group, 4
+    // micro-blocks) and micro-block entries (split groups), each run sorted by
+    // decode class.  Work unit = one group entry or four consecutive
+    // micro-block entries; warp w takes units 16w .. 16w + 15, lane pair
+    // (2e, 2e + 1) decodes the two column halves of unit e.  Sorted runs make
+    // most warps mode-uniform, so they take one specialised path.
     const int dw = warp - kDeqWarp0;
     const int h = lane & 1;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
       for (int kb = 0; kb < p.nkb; ++kb, ++it) {
-        const int st = it % p.S, pst = it % p.P;
-        if (!mbar_wait(&pfull[pst], (it / p.P) & 1, p.timeout_ns)) {
+        const int st = it % p.S, ps = it % kRingSlots;
+        if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
           flags[0] = 1;
           break;
         }
@@ -219,12 +251,74 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         uint8_t* Bt = sB + st * kBBytes;
-        const uint8_t* sl = sP + pst * p.pslot;
-        const uint32_t count = reinterpret_cast<const uint32_t*>(sl + kListOff)[kMaxGroups * 2];
-        const uint8_t* payload = sl + kHeadBytes;
-        const int idx = 16 * dw + (lane >> 1);
-        const bool valid = idx < (int)count;
-        const uint64_t ent = valid ? reinterpret_cast<const uint64_t*>(sl + kListOff)[idx] : 0ull;
+        const uint8_t* sl = sP + pmeta[4 * ps];
+        const uint32_t cnt = pmeta[4 * ps + 1];
+        const uint64_t* list = reinterpret_cast<const uint64_t*>(sl + kDescBytes);
+        const uint8_t* payload = sl + kDescBytes + pmeta[4 * ps + 2];
+        const int n_group = (int)(cnt & 0xffffu), n_mb = (int)(cnt >> 16);
+        const int u = 16 * dw + (lane >> 1);
+        const bool has_mb = u >= n_group && 4 * (u - n_group) < n_mb;
+        if (__any_sync(0xffffffffu, has_mb)) {
+          // ---- micro-block entries: four per lane pair ----
+          const int j0 = n_group + 4 * (u - n_group);
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            const int j = j0 + k;
+            const bool valid = u >= n_group && j < n_group + n_mb;
+            const uint64_t ent = valid ? list[j] : 0ull;
+            const int cls = valid ? (int)((ent >> 48) & 15u) : -1;
+            const unsigned vm = __ballot_sync(0xffffffffu, valid);
+            const int cls0 = __shfl_sync(0xffffffffu, cls, vm ? __ffs(vm) - 1 : 0);
+            const uint8_t* prim = payload + (uint32_t)(ent & 0xffffu);
+            const uint8_t* sec = payload + (uint32_t)((ent >> 16) & 0xffffu);
+            const uint32_t s2 = h2const((uint16_t)((ent >> 32) & 0xffffu));
+            const int ti = (int)((ent >> 52) & 15u), G = (int)((ent >> 56) & 15u), mk = (int)((ent >> 60) & 3u);
+            uint32_t r[4] = {0u, 0u, 0u, 0u};
+            if (__all_sync(0xffffffffu, !valid || cls == cls0) && cls0 != kClassGeneric) {
+              switch (cls0) {  // warp-uniform branch
+                case 1: decode_mb_half<2>(prim, sec, h, s2, r); break;
+                case 2: decode_mb_half<3>(prim, sec, h, s2, r); break;
+                case 3: decode_mb_half<4>(prim, sec, h, s2, r); break;
+                case 4: decode_mb_half<5>(prim, sec, h, s2, r); break;
+                case 5: decode_mb_half<6>(prim, sec, h, s2, r); break;
+                case 6: decode_mb_half<8>(prim, sec, h, s2, r); break;
+                default: break;
+              }
+            } else if (valid) {
+              switch (cls) {
+                case 1: decode_mb_half<2>(prim, sec, h, s2, r); break;
+                case 2: decode_mb_half<3>(prim, sec, h, s2, r); break;
+                case 3: decode_mb_half<4>(prim, sec, h, s2, r); break;
+                case 4: decode_mb_half<5>(prim, sec, h, s2, r); break;
+                case 5: decode_mb_half<6>(prim, sec, h, s2, r); break;
+                case 6: decode_mb_half<8>(prim, sec, h, s2, r); break;
+                case kClassGeneric: {
+                  const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
+                  const uint8_t* rec =
+                      payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
+                  const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
+                  const int L = leaf_of(d.leaf_start, 4 * G + mk);
+                  decode_half_w16(lt_entry(ltab, L, s.scale_words), lt_scale_of(ltab, L, s.scale_words), prim,
+                                  sec, h, p.pow2e, r);
+                  break;
+                }
+                default: break;
+              }
+            }
+            if (valid) {
+              // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
+              const int rr = ti >> 3, col = ti & 7;
+              const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
+              const int jj = ((G >> 2) & 1) << 1 | (G & 1);
+              const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
+              const int k0 = 32 * rr + 8 * t + 4 * (mk >> 1);
+              *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r[0], r[1]);
+              *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r[2], r[3]);
+            }
+          }
+        }
+        const bool valid = u < n_group;
+        const uint64_t ent = valid ? list[u] : 0ull;
         const int cls = valid ? (int)((ent >> 48) & 15u) : -1;
         const int cls0 = __shfl_sync(0xffffffffu, cls, 0);
         const uint8_t* prim = payload + (uint32_t)(ent & 0xffffu);
@@ -291,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&full_ab[st]);
-          mbar_arrive(&pempty[pst]);
+          mbar_arrive(&pempty[ps]);
         }
       }
     }
@@ -415,8 +509,8 @@ EncodeTiledFn encode_tiled() {
 }
 
 struct PrefillPlan {
-  int Kp, Np, nkb, n_mblk, n_bands, n_tiles, S, P;
-  uint32_t pslot;
+  int Kp, Np, nkb, n_mblk, n_bands, n_tiles, S;
+  uint32_t ring_bytes;
   size_t smem, xp_bytes, yp_bytes;
 };
 
@@ -427,19 +521,20 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
   pl->n_mblk = (M + BM - 1) / BM;
   pl->n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
   pl->n_tiles = pl->n_mblk * pl->n_bands;
-  pl->pslot = (kHeadBytes + 2 * s->max_row_bytes + 127u) & ~127u;
   const size_t cap = 227 * 1024;
   const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/;
-  // Three A/B stages let dequant run two stages ahead of the MMA (absorbing
-  // the varying cost of mode mixes); packed-weight slots take what is left.
-  // (Measured: S=3/P=2 beats S=2/P=4 by 15% on a 4096x14336 layer.)
-  int S = 3, P = 2;
-  while (S >= 2 && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)P * pl->pslot > cap) --S;
-  if (S < 2) return false;
-  while (P < kMaxP && fixed + (size_t)S * (kABytes + kBBytes) + (size_t)(P + 1) * pl->pslot <= cap) ++P;
+  // Three A/B stages let dequant run two stages ahead of the MMA; the packed
+  // byte ring takes the rest.  The ring must hold the largest stage and
+  // should hold about three typical ones; fall back to two A/B stages when
+  // three leave less than twice the largest stage.
+  const size_t biggest = s->max_stage_bytes ? s->max_stage_bytes : 2 * s->max_row_bytes + 8 * 1024 + kDescBytes;
+  int S = 3;
+  while (S > 2 && cap - fixed - (size_t)S * (kABytes + kBBytes) < 2 * biggest) --S;
+  const size_t ring = (cap - fixed - (size_t)S * (kABytes + kBBytes)) & ~(size_t)127;
+  if (ring < biggest) return false;
   pl->S = S;
-  pl->P = P;
-  pl->smem = fixed + (size_t)S * (kABytes + kBBytes) + (size_t)P * pl->pslot;
+  pl->ring_bytes = (uint32_t)ring;
+  pl->smem = fixed + (size_t)S * (kABytes + kBBytes) + ring;
   pl->xp_bytes = ((size_t)M * pl->Kp * 2 + 255) & ~(size_t)255;
   pl->yp_bytes = permuted ? (size_t)M * pl->Np * 4 : 0;
   return true;
@@ -465,8 +560,8 @@ int check_prefill(const mtc_stream_desc* s, int32_t M, bool permuted, void* ws, 
   MTC_REQUIRE(s->band_tiles * kTile == BN, "%s: stream band width %d tiles, kernel needs %d", who, s->band_tiles,
               BN / kTile);
   MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "%s: workspace not 256-byte aligned", who);
-  MTC_REQUIRE(plan_prefill(s, M, permuted, pl), "%s: a k-tile row of %u bytes does not fit shared memory", who,
-              s->max_row_bytes);
+  MTC_REQUIRE(plan_prefill(s, M, permuted, pl), "%s: a stage of %u bytes does not fit shared memory", who,
+              s->max_stage_bytes);
   if (ws_bytes < pl->xp_bytes + pl->yp_bytes) {
     set_error("%s: workspace %zu bytes, need %zu", who, ws_bytes, pl->xp_bytes + pl->yp_bytes);
     return MTC_ERR_WORKSPACE;
@@ -532,8 +627,8 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   PrefillPlan pl;
   int rc = check_prefill(s, M, permuted_output != 0, ws, ws_bytes, &pl, "mtc_prefill_gemm");
   if (rc != MTC_OK) return rc;
-  MTC_REQUIRE(s->stage_lists && s->stage_counts,
-              "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_lists first)");
+  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->max_stage_bytes,
+              "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
   const bool col_perm_inv = permuted_output != 0;
   EncodeTiledFn enc = encode_tiled();
@@ -569,8 +664,7 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   p.n_tiles = pl.n_tiles;
   p.nkb = pl.nkb;
   p.S = pl.S;
-  p.P = pl.P;
-  p.pslot = pl.pslot;
+  p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
   p.timeout_ns = 2000000000ull;

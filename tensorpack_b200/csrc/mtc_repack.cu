@@ -280,12 +280,25 @@ __device__ __forceinline__ int class_of_mode(int m) {
   }
 }
 
+__device__ __forceinline__ uint32_t fp16_scale_bits(float sc, bool* exact) {
+  const __half hs = __float2half_rn(sc);
+  *exact = __half2float(hs) == sc;
+  return *reinterpret_cast<const uint16_t*>(&hs);
+}
+
 // One CTA of 256 threads per stage (band, k-tile rows 2kb and 2kb + 1);
 // thread i owns group G = i & 15 of tile (row i >> 7, column (i >> 4) & 7).
-__global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int nkb, uint64_t* __restrict__ lists,
-                                                          uint32_t* __restrict__ counts) {
-  __shared__ uint32_t cnt[8];
-  __shared__ uint32_t base[8];
+// A group covered by one leaf becomes one group entry; a group of four 4x4
+// leaves becomes four micro-block entries (each with its own mode), so every
+// entry decodes with one mode.  Group entries come first, sorted by class,
+// then micro-block entries, sorted by class.  Pass 1 (FILL = false) counts,
+// pass 2 writes at the CSR offsets.
+template <bool FILL>
+__global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int nkb, const uint32_t* __restrict__ offs,
+                                                          uint32_t* __restrict__ counts, uint32_t* __restrict__ totals,
+                                                          uint64_t* __restrict__ lists) {
+  __shared__ uint32_t cnt[16];   // [0, 8) group classes, [8, 16) micro-block classes
+  __shared__ uint32_t base[16];
   const int stage = blockIdx.x;
   const int band = stage / nkb, kb = stage % nkb;
   const int i = threadIdx.x;
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int
   const int r = ti >> 3, col = ti & 7;
   const int kt = 2 * kb + r, nt = band * s.band_tiles + col;
   const bool valid = kt < s.tk && nt < s.tn && col < s.band_tiles;
-  if (i < 8) cnt[i] = 0;
+  if (i < 16) cnt[i] = 0;
   __syncthreads();
   const float pow2e = ldexpf(1.0f, s.exp2);
   const int sw = s.scale_words;
@@ -325,39 +338,105 @@ __global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int
     if ((lane & 15) >= dl) incl += u;
   }
   const uint32_t ex = incl - v;
-  int cls = kClassGeneric;
-  uint64_t entry = 0;
+  uint64_t entry[4] = {0, 0, 0, 0};
+  int cls[4] = {-1, -1, -1, -1};  // slot < 8: group class; slot 8 + c: micro-block class c
   if (valid) {
+    const uint32_t* ltab = reinterpret_cast<const uint32_t*>(s.records + d.record_off);
     const uint32_t stage_base = s.row_off[(size_t)band * (s.tk + 1) + 2 * kb];
     const uint32_t rec = d.record_off - stage_base;
-    const uint32_t prim = rec + pad16(4 * sw * d.n_leaves) + (ex & 0xffffu);
-    const uint32_t sec = rec + pad16(4 * sw * d.n_leaves) + pad16(d.prim_bytes) + (ex >> 16);
-    uint32_t scale16 = 0;
+    uint32_t prim = rec + pad16(4 * sw * d.n_leaves) + (ex & 0xffffu);
+    uint32_t sec = rec + pad16(4 * sw * d.n_leaves) + pad16(d.prim_bytes) + (ex >> 16);
+    const uint64_t where = ((uint64_t)ti << 52) | ((uint64_t)G << 56);
     if (single) {
-      const uint32_t* ltab = reinterpret_cast<const uint32_t*>(s.records + d.record_off);
       const int m = lt_mode(e0);
-      cls = class_of_mode(m);
-      const float sc = lt_scale_of(ltab, l0, sw) * pow2e;
-      const __half hs = __float2half_rn(sc);
-      if (lt_slow(e0) || __half2float(hs) != sc) cls = (m == 0) ? kClassZero : kClassGeneric;
-      scale16 = *reinterpret_cast<const uint16_t*>(&hs);
+      bool exact;
+      const uint32_t s16 = fp16_scale_bits(lt_scale_of(ltab, l0, sw) * pow2e, &exact);
+      int c = class_of_mode(m);
+      if (m != 0 && (lt_slow(e0) || !exact)) c = kClassGeneric;
+      cls[0] = c;
+      entry[0] = (uint64_t)(prim & 0xffffu) | ((uint64_t)(sec & 0xffffu) << 16) | ((uint64_t)s16 << 32) |
+                 ((uint64_t)c << 48) | where;
+    } else {
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t e = lt_entry(ltab, l0 + k, sw);
+        const int m = lt_mode(e);
+        bool exact;
+        const uint32_t s16 = fp16_scale_bits(lt_scale_of(ltab, l0 + k, sw) * pow2e, &exact);
+        int c = class_of_mode(m);
+        if (m != 0 && (lt_slow(e) || !exact)) c = kClassGeneric;
+        cls[k] = 8 + c;
+        entry[k] = (uint64_t)(prim & 0xffffu) | ((uint64_t)(sec & 0xffffu) << 16) | ((uint64_t)s16 << 32) |
+                   ((uint64_t)c << 48) | where | ((uint64_t)k << 60) | (1ull << 62);
+        prim += lt_prim(e);
+        sec += lt_sec(e);
+      }
     }
-    entry = (uint64_t)(prim & 0xffffu) | ((uint64_t)(sec & 0xffffu) << 16) | ((uint64_t)scale16 << 32) |
-            ((uint64_t)cls << 48) | ((uint64_t)ti << 52) | ((uint64_t)G << 56);
   }
-  uint32_t rank = 0;
-  if (valid) rank = atomicAdd(&cnt[cls], 1u);
+  uint32_t rank[4] = {0, 0, 0, 0};
+  for (int k = 0; k < 4; ++k)
+    if (cls[k] >= 0) rank[k] = atomicAdd(&cnt[cls[k]], 1u);
   __syncthreads();
   if (i == 0) {
     uint32_t acc = 0;
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 16; ++c) {
       base[c] = acc;
       acc += cnt[c];
     }
-    counts[stage] = acc;
+    uint32_t ng = 0;
+    for (int c = 0; c < 8; ++c) ng += cnt[c];
+    if (!FILL) {
+      counts[stage] = ng | ((acc - ng) << 16);
+      totals[stage] = acc;
+    }
   }
   __syncthreads();
-  if (valid) lists[(size_t)stage * 256 + base[cls] + rank] = entry;
+  if (FILL) {
+    for (int k = 0; k < 4; ++k)
+      if (cls[k] >= 0) lists[(size_t)offs[stage] + base[cls[k]] + rank[k]] = entry[k];
+  }
+}
+
+// Exclusive scan of the per-stage entry totals into CSR offsets (single CTA),
+// plus the largest staged footprint: descriptors + list + records of a stage.
+__global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __restrict__ totals, int n_stages,
+                                                          mtc_stream_desc s, int nkb, uint32_t* __restrict__ offs,
+                                                          uint32_t* __restrict__ out) {
+  __shared__ uint32_t part[1024];
+  __shared__ uint32_t red[1024];
+  const int per = (n_stages + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n_stages, (int)threadIdx.x * per), hi = min(n_stages, lo + per);
+  uint32_t sum = 0, mx = 0;
+  // each stage's list starts at an even entry (16-byte aligned for the bulk copy)
+  for (int i = lo; i < hi; ++i) {
+    sum += (totals[i] + 1u) & ~1u;
+    const int band = i / nkb, kb = i % nkb;
+    const uint32_t* ro = s.row_off + (size_t)band * (s.tk + 1);
+    const uint32_t bytes = ro[min(2 * kb + 2, s.tk)] - ro[2 * kb];
+    mx = max(mx, 256u + ((8u * totals[i] + 15u) & ~15u) + bytes);
+  }
+  part[threadIdx.x] = sum;
+  red[threadIdx.x] = mx;
+  __syncthreads();
+  for (int dl = 1; dl < (int)blockDim.x; dl <<= 1) {
+    const uint32_t v = threadIdx.x >= (unsigned)dl ? part[threadIdx.x - dl] : 0u;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  uint32_t off = part[threadIdx.x] - sum;
+  for (int i = lo; i < hi; ++i) {
+    offs[i] = off;
+    off += (totals[i] + 1u) & ~1u;
+  }
+  for (int dl = blockDim.x / 2; dl > 0; dl >>= 1) {
+    if (threadIdx.x < (unsigned)dl) red[threadIdx.x] = max(red[threadIdx.x], red[threadIdx.x + dl]);
+    __syncthreads();
+  }
+  if (threadIdx.x == blockDim.x - 1) {
+    offs[n_stages] = part[blockDim.x - 1];
+    out[0] = part[blockDim.x - 1];
+  }
+  if (threadIdx.x == 0) out[1] = red[0];
 }
 
 }  // namespace
@@ -365,16 +444,40 @@ __global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int
 
 using namespace mtc;
 
-extern "C" int mtc_repack_stage_lists(const mtc_stream_desc* s, uint64_t* lists, uint32_t* counts, void* stream) {
+extern "C" int mtc_repack_stage_plan(const mtc_stream_desc* s, uint32_t* counts, uint32_t* offsets,
+                                     uint32_t* scratch_u32, uint64_t* out_host, void* stream) {
   clear_error();
-  MTC_REQUIRE(s && lists && counts && s->tiles && s->row_off && s->records, "mtc_repack_stage_lists: null pointer");
-  MTC_REQUIRE(s->band_tiles == 8, "mtc_repack_stage_lists: band width %d (needs 8)", s->band_tiles);
-  MTC_REQUIRE(2ull * s->max_row_bytes < 65536ull, "mtc_repack_stage_lists: stage of %u bytes exceeds 16-bit offsets",
+  MTC_REQUIRE(s && counts && offsets && scratch_u32 && out_host && s->tiles && s->row_off && s->records,
+              "mtc_repack_stage_plan: null pointer");
+  MTC_REQUIRE(s->band_tiles == 8, "mtc_repack_stage_plan: band width %d (needs 8)", s->band_tiles);
+  MTC_REQUIRE(2ull * s->max_row_bytes < 65536ull, "mtc_repack_stage_plan: stage of %u bytes exceeds 16-bit offsets",
               2 * s->max_row_bytes);
   const int nkb = (s->tk + 1) / 2;
   const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
-  stage_lists_kernel<<<nb * nkb, 256, 0, as_stream(stream)>>>(*s, nkb, lists, counts);
-  MTC_CHECK_LAUNCH("mtc_repack_stage_lists");
+  const int n_stages = nb * nkb;
+  cudaStream_t st = as_stream(stream);
+  uint32_t* totals = scratch_u32;
+  uint32_t* out = scratch_u32 + n_stages;
+  stage_lists_kernel<false><<<n_stages, 256, 0, st>>>(*s, nkb, nullptr, counts, totals, nullptr);
+  MTC_CHECK_LAUNCH("mtc_repack_stage_plan: count");
+  stage_scan_kernel<<<1, 1024, 0, st>>>(totals, n_stages, *s, nkb, offsets, out);
+  MTC_CHECK_LAUNCH("mtc_repack_stage_plan: scan");
+  uint32_t back[2];
+  MTC_CHECK_CUDA(cudaMemcpyAsync(back, out, 8, cudaMemcpyDeviceToHost, st), "mtc_repack_stage_plan: copy back");
+  MTC_CHECK_CUDA(cudaStreamSynchronize(st), "mtc_repack_stage_plan: sync");
+  out_host[0] = back[0];
+  out_host[1] = back[1];
+  return MTC_OK;
+}
+
+extern "C" int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint64_t* lists,
+                                     void* stream) {
+  clear_error();
+  MTC_REQUIRE(s && offsets && lists && s->tiles && s->row_off && s->records, "mtc_repack_stage_fill: null pointer");
+  const int nkb = (s->tk + 1) / 2;
+  const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
+  stage_lists_kernel<true><<<nb * nkb, 256, 0, as_stream(stream)>>>(*s, nkb, offsets, nullptr, nullptr, lists);
+  MTC_CHECK_LAUNCH("mtc_repack_stage_fill");
   return MTC_OK;
 }
 
