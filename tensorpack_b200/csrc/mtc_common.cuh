@@ -431,6 +431,26 @@ __device__ __forceinline__ void decode_half_uniform(const uint32_t* tab, int mod
   r[3] = hmul2u(hfma2u(lop_or(x[3], pm.w), c.w, hfma2u(lop_or(S, sm.w), cs.w, K.w)), s2);
 }
 
+// One micro-block half of decode class c (0 = P0 zeros; 1..6 = P2, P3, P4,
+// P5, P6, P8) through the table decoder: lanes of different classes run the
+// same instructions.  tab = the decoder table in shared memory.
+__device__ __forceinline__ void decode_half_class(const uint32_t* tab, int c, const uint8_t* prim,
+                                                  const uint8_t* sec, int h, uint32_t s2, uint32_t r[4]) {
+  const int cc = c > 0 ? c : 1;
+  const int mode = cc + 1 + (cc == 6 ? 1 : 0);
+  decode_half_uniform(tab + 20 * (cc - 1), mode, prim, sec, h, c > 0 ? s2 : 0u, r);
+}
+
+// Four micro-blocks of one leaf (a group), decode class c, through the table
+// decoder (lanes of different classes run the same instructions).
+__device__ __forceinline__ void decode_run4_class(const uint32_t* tab, int c, const uint8_t* prim,
+                                                  const uint8_t* sec, int h, uint32_t s2, uint32_t R[4][4]) {
+  const int pb = c == 6 ? 16 : (c <= 2 ? 4 : 8);
+  const int sb = (c == 2 || c == 4) ? 2 : (c == 5 ? 4 : 0);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) decode_half_class(tab, c, prim + k * pb, sec + k * sb, h, s2, R[k]);
+}
+
 // Any group through the per-micro-block path (four 4x4 leaves of possibly
 // different modes, P16, inexact fp16 scales).  prim / sec = group base.
 __device__ __forceinline__ void decode_group_generic(const uint32_t* ltab, uint64_t leaf_start, int G,
@@ -599,6 +619,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+// The same for a barrier that also receives arrivals from the other CTA of
+// a cluster: acquire at cluster scope, so that CTA's shared-memory writes
+// made before its arrive are visible here.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }

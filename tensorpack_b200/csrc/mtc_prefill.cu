@@ -10,16 +10,18 @@
 //  2. prefill:    persistent, one CTA per SM, output tile 256 tokens x 256
 //                 features, K step 64.  Warp roles:
 //                   warps 0-3  epilogue: TMEM -> registers -> global
-//                   warp  4    producer: TMA of the Xp tile (SWIZZLE_128B) and
-//                              cp.async.bulk of the band's packed k-tile rows
+//                   warp  4    A producer: TMA of the Xp tile (SWIZZLE_128B)
 //                   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
-//                   warps 6-21 dequant: one 32x32 tile each per stage,
-//                              packed codes -> fp16 W tile in the K-major
-//                              SWIZZLE_128B layout the MMA reads
+//                   warp  6    packed producer: cp.async.bulk of each stage's
+//                              descriptors, work list and records into a
+//                              shared-memory byte ring, up to 8 stages ahead
+//                   warps 7-22 dequant: the stage's work list, packed codes ->
+//                              fp16 W tile in the K-major SWIZZLE_128B layout
+//                              the MMA reads
 //                 Two 128x256 fp32 accumulators (all 512 TMEM columns) share
 //                 each dequantised W tile, so every weight is decoded once
-//                 per 256 tokens.  mbarriers link the stages; every wait is
-//                 bounded.
+//                 per 256 tokens.  A and W tiles have their own pipeline
+//                 depths; mbarriers link the stages; every wait is bounded.
 //  3. permute_y:  Y[m][j] = Yp[m][ipc[j]] for MTC-QT-P matrices (row staged in
 //                 shared memory, coalesced in and out).
 #include "mtc_common.cuh"
@@ -33,9 +35,10 @@ constexpr int BM = 256;   // tokens per CTA tile (two M=128 MMAs)
 constexpr int BN = 256;   // features per CTA tile (one column band)
 constexpr int BK = 64;    // K per pipeline stage (two k-tile rows)
 constexpr int kEpiWarps = 4;
-constexpr int kProdWarp = 4;
+constexpr int kProdWarp = 4;   // A tiles
 constexpr int kMmaWarp = 5;
-constexpr int kDeqWarp0 = 6;
+constexpr int kPackWarp = 6;   // packed stages
+constexpr int kDeqWarp0 = 7;
 constexpr int kDeqWarps = 16;
 constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;
 constexpr uint32_t kABytes = BM * BK * 2;
@@ -43,10 +46,11 @@ constexpr uint32_t kBBytes = BN * BK * 2;
 constexpr int kMaxS = 4;
 // Packed data of each stage sits contiguously in a shared-memory byte ring:
 // [256 B tile descriptors of the stage's 2 k rows][work list][records].
-// Stages have very different sizes (MTC-QT-P puts the high-precision columns
-// in the last bands), so a ring keeps several typical stages in flight where
-// fixed slots sized for the largest one would fit a single stage.
+// Stage sizes vary (in MTC-QT-P allocations the largest is about twice the
+// median), so a ring keeps several typical stages in flight where fixed slots
+// sized for the largest one would hold one or two.
 constexpr int kRingSlots = 8;          // stages in flight at most
+constexpr int kMetaChunk = 64;         // stages of metadata the packed producer stages at a time
 constexpr uint32_t kDescBytes = 256;
 constexpr int kClassGeneric = 7;
 
@@ -57,7 +61,8 @@ struct PrefillParams {
   long long ldy;
   uint32_t* status;
   int n_bands, n_tiles, nkb;
-  int S;
+  int SA, SB;         // A-tile and W-tile pipeline depths
+  int vec2;           // Y rows 8-byte aligned: float2 stores
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
@@ -79,13 +84,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the __shared__ array keeps the shared address space visible to the compiler
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
-  uint8_t* sB = sA + p.S * kABytes;
-  uint8_t* sP = sB + p.S * kBBytes;
+  uint8_t* sB = sA + p.SA * kABytes;
+  uint8_t* sP = sB + p.SB * kBBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
-  uint64_t* full_ab = bars;                   // [S]
-  uint64_t* empty_ab = full_ab + kMaxS;       // [S]
-  uint64_t* pfull = empty_ab + kMaxS;         // [kRingSlots]
-  uint64_t* pempty = pfull + kRingSlots;      // [kRingSlots]
+  uint64_t* full_a = bars;                    // [SA] TMA bytes
+  uint64_t* empty_a = full_a + kMaxS;         // [SA] MMA commit
+  uint64_t* full_b = empty_a + kMaxS;         // [SB] dequant warps
+  uint64_t* empty_b = full_b + kMaxS;         // [SB] MMA commit
+  uint64_t* pfull = empty_b + kMaxS;          // [kRingSlots] bulk-copy bytes
+  uint64_t* pempty = pfull + kRingSlots;      // [kRingSlots] dequant warps
   uint64_t* acc_full = pempty + kRingSlots;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
@@ -93,14 +100,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
   uint32_t* pmeta = tmem_slot + 4;            // [kRingSlots][4]: ring offset, counts, list bytes
   uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 512);  // decoder table
+  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1024);      // [2][kMetaChunk]
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < p.S; ++i) {
-      mbar_init(&full_ab[i], 1 + kDeqWarps);
-      mbar_init(&empty_ab[i], 1);
+    for (int i = 0; i < p.SA; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < p.SB; ++i) {
+      mbar_init(&full_b[i], kDeqWarps);
+      mbar_init(&empty_b[i], 1);
     }
     for (int i = 0; i < kRingSlots; ++i) {
       mbar_init(&pfull[i], 1);
@@ -120,31 +132,82 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kProdWarp) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- A producer
     if (lane == 0) {
       uint32_t it = 0;
-      uint32_t oldest = 0;                              // oldest stage not yet known to be released
-      unsigned long long ring_head = 0;                 // monotonic byte position in the ring
-      unsigned long long ring_start[kRingSlots];        // start position of each stage in flight
       for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
-        const int mblk = tile / p.n_bands, band = tile % p.n_bands;
-        const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
+        const int mblk = tile / p.n_bands;
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
-          const int st = it % p.S;
-          if (it >= (uint32_t)p.S && !mbar_wait(&empty_ab[st], ((it / p.S) & 1) ^ 1, p.timeout_ns)) {
+          const int sa = it % p.SA;
+          if (it >= (uint32_t)p.SA && !mbar_wait(&empty_a[sa], ((it / p.SA) & 1) ^ 1, p.timeout_ns)) {
             flags[0] = 1;
             break;
           }
-          mbar_expect_tx(&full_ab[st], kABytes);
-          tc::tma_load_2d(sA + st * kABytes, &tmap_x, kb * BK, mblk * BM, &full_ab[st]);
+          if (flags[0]) break;
+          mbar_expect_tx(&full_a[sa], kABytes);
+          tc::tma_load_2d(sA + sa * kABytes, &tmap_x, kb * BK, mblk * BM, &full_a[sa]);
+        }
+      }
+      if (flags[0]) {
+        // aborting: let the loads still in flight land before the CTA exits
+        for (uint32_t j = it > (uint32_t)p.SA ? it - p.SA : 0u; j < it; ++j)
+          (void)mbar_wait(&full_a[j % p.SA], (j / p.SA) & 1, 10000000ull);
+        flag(p.status, MTC_STATUS_TIMEOUT);
+      }
+    }
+  } else if (warp == kPackWarp) {
+    // ---------------------------------------------------------------- packed producer
+    // The whole warp loads the per-stage metadata (record range, entry
+    // counts, list offset) of 64 stages at a time into shared memory, one
+    // chunk ahead of lane 0, which issues the bulk copies; so lane 0 never
+    // waits on a global load.
+    const int n_my_tiles = blockIdx.x < p.n_tiles ? (p.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int chunks_per_tile = (p.nkb + kMetaChunk - 1) / kMetaChunk;
+    const int n_chunks = n_my_tiles * chunks_per_tile;
+    uint4 nxt[kMetaChunk / 32];
+    auto load_chunk = [&](int q) {
+      const int tile = blockIdx.x + (q / chunks_per_tile) * gridDim.x;
+      const int band = tile % p.n_bands;
+      const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
+#pragma unroll
+      for (int h = 0; h < kMetaChunk / 32; ++h) {
+        const int kb = (q % chunks_per_tile) * kMetaChunk + 32 * h + lane;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (q < n_chunks && kb < p.nkb) {
+          const size_t stage = (size_t)band * p.nkb + kb;
+          const uint32_t off = row_off[2 * kb];
+          v = make_uint4(off, row_off[min(2 * kb + 2, s.tk)] - off, s.stage_counts[stage], s.stage_offsets[stage]);
+        }
+        nxt[h] = v;
+      }
+    };
+    auto store_chunk = [&](int buf) {
+#pragma unroll
+      for (int h = 0; h < kMetaChunk / 32; ++h) smeta[buf * kMetaChunk + 32 * h + lane] = nxt[h];
+    };
+    load_chunk(0);
+    store_chunk(0);
+    __syncwarp();
+    uint32_t it = 0;
+    uint32_t oldest = 0;                              // oldest stage not yet known to be released
+    unsigned long long ring_head = 0;                 // monotonic byte position in the ring
+    uint32_t head_off = 0;                            // ring_head modulo the ring size
+    unsigned long long ring_start[kRingSlots];        // start position of each stage in flight
+    for (int q = 0; q < n_chunks; ++q) {
+      load_chunk(q + 1);                              // in flight while lane 0 issues chunk q
+      if (lane == 0) {
+        const int tile = blockIdx.x + (q / chunks_per_tile) * gridDim.x;
+        const int band = tile % p.n_bands;
+        const int kb0 = (q % chunks_per_tile) * kMetaChunk;
+        const int kb1 = min(p.nkb, kb0 + kMetaChunk);
+        const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
+        for (int kb = kb0; kb < kb1 && !flags[0]; ++kb, ++it) {
           // Packed data of the stage goes to the byte ring as one contiguous
           // piece: tile descriptors (256 B) | work list | records.  Its ring
           // range must be free: release older stages (FIFO) until it is.
+          const uint4 m = smeta[(q & 1) * kMetaChunk + (kb - kb0)];
+          const uint32_t off = m.x, bytes = m.y, cnt = m.z;
           const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
-          const uint32_t off = row_off[r0];
-          const uint32_t bytes = row_off[r1] - off;
-          const size_t stage = (size_t)band * p.nkb + kb;
-          const uint32_t cnt = s.stage_counts[stage];
           const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
           const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
           const uint32_t need = kDescBytes + lbytes + bytes;
@@ -153,8 +216,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             flags[0] = 1;
             break;
           }
+          // (positions advance without division: a piece that would cross
+          // the end of the ring starts at the next lap instead)
           unsigned long long pos = ring_head;
-          if ((pos % p.ring_bytes) + need > p.ring_bytes) pos = (pos / p.ring_bytes + 1) * p.ring_bytes;
+          uint32_t start = head_off;
+          if (start + need > p.ring_bytes) {
+            pos += p.ring_bytes - start;
+            start = 0;
+          }
           // live bytes are [ring_start[oldest], ring_head): the new piece must
           // end within one ring length of the oldest live stage's start
           bool ok = true;
@@ -173,23 +242,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ps = it % kRingSlots;
           ring_start[ps] = pos;
           ring_head = pos + need;
-          const uint32_t start = (uint32_t)(pos % p.ring_bytes);
+          head_off = start + need;
           pmeta[4 * ps + 0] = start;
           pmeta[4 * ps + 1] = cnt;
           pmeta[4 * ps + 2] = lbytes;
-          const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
           uint8_t* dst = sP + start;
           mbar_expect_tx(&pfull[ps], bytes + 16u * width * (r1 - r0) + 8u * ((n_ent + 1u) & ~1u));
           for (int r = r0; r < r1; ++r)
             bulk_g2s(dst + 128 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles, 16u * width,
                      &pfull[ps]);
           if (n_ent)
-            bulk_g2s(dst + kDescBytes, s.stage_lists + s.stage_offsets[stage], 8u * ((n_ent + 1u) & ~1u),
-                     &pfull[ps]);
+            bulk_g2s(dst + kDescBytes, s.stage_lists + m.w, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
           bulk_g2s(dst + kDescBytes + lbytes, s.records + off, bytes, &pfull[ps]);
         }
       }
-      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+      __syncwarp();
+      store_chunk((q + 1) & 1);
+      __syncwarp();
+      if (flags[0]) break;
+    }
+    if (lane == 0 && flags[0]) {
+      for (uint32_t j = it > (uint32_t)kRingSlots ? it - kRingSlots : 0u; j < it; ++j)
+        (void)mbar_wait(&pfull[j % kRingSlots], (j / kRingSlots) & 1, 10000000ull);
+      flag(p.status, MTC_STATUS_TIMEOUT);
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
@@ -203,14 +278,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::fence_after();
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
-          const int st = it % p.S;
-          if (!mbar_wait(&full_ab[st], (it / p.S) & 1, p.timeout_ns)) {
+          const int sa = it % p.SA, sb = it % p.SB;
+          if (!mbar_wait(&full_a[sa], (it / p.SA) & 1, p.timeout_ns) ||
+              !mbar_wait(&full_b[sb], (it / p.SB) & 1, p.timeout_ns)) {
             flags[0] = 1;
             break;
           }
           tc::fence_after();
-          const uint32_t a0 = smem_u32(sA + st * kABytes);
-          const uint32_t b0 = smem_u32(sB + st * kBBytes);
+          const uint32_t a0 = smem_u32(sA + sa * kABytes);
+          const uint32_t b0 = smem_u32(sB + sb * kBBytes);
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bd = tc::smem_desc_k_sw128(b0 + 32 * j);
@@ -218,7 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mma_f16_ss(tmem, tc::smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
             tc::mma_f16_ss(tmem + 256, tc::smem_desc_k_sw128(a0 + 128 * 128 + 32 * j), bd, idesc, acc);
           }
-          tc::commit(&empty_ab[st]);
+          tc::commit(&empty_a[sa]);
+          tc::commit(&empty_b[sb]);
         }
         if (flags[0]) break;
         tc::commit(acc_full);
@@ -241,79 +318,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
       for (int kb = 0; kb < p.nkb; ++kb, ++it) {
-        const int st = it % p.S, ps = it % kRingSlots;
+        const int sb = it % p.SB, ps = it % kRingSlots;
         if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
           flags[0] = 1;
           break;
         }
-        if (it >= (uint32_t)p.S && !mbar_wait(&empty_ab[st], ((it / p.S) & 1) ^ 1, p.timeout_ns)) {
+        if (it >= (uint32_t)p.SB && !mbar_wait(&empty_b[sb], ((it / p.SB) & 1) ^ 1, p.timeout_ns)) {
           flags[0] = 1;
           break;
         }
-        uint8_t* Bt = sB + st * kBBytes;
+        uint8_t* Bt = sB + sb * kBBytes;
         const uint8_t* sl = sP + pmeta[4 * ps];
         const uint32_t cnt = pmeta[4 * ps + 1];
         const uint64_t* list = reinterpret_cast<const uint64_t*>(sl + kDescBytes);
         const uint8_t* payload = sl + kDescBytes + pmeta[4 * ps + 2];
         const int n_group = (int)(cnt & 0xffffu), n_mb = (int)(cnt >> 16);
         const int u = 16 * dw + (lane >> 1);
-        const bool has_mb = u >= n_group && 4 * (u - n_group) < n_mb;
-        if (__any_sync(0xffffffffu, has_mb)) {
-          // ---- micro-block entries: four per lane pair ----
-          const int j0 = n_group + 4 * (u - n_group);
-#pragma unroll 1
+        // Lane pairs e >= e0 of this warp hold micro-block units: 4 x (16 -
+        // e0) consecutive micro-block entries, taken 16 - e0 at a time.
+        const int e0 = max(0, min(16, n_group - 16 * dw));
+        const int n_mbu = 16 - e0;
+        const int r0 = 4 * (16 * dw + e0 - n_group);
+        if (n_mbu > 0 && r0 < n_mb) {
+          // ---- micro-block entries (split groups): four passes, one half
+          // micro-block per lane each.  P2..P8 share one table-driven
+          // instruction sequence, so lanes of different modes do not
+          // serialise; generic entries (P16, inexact fp16 scales) follow in a
+          // per-lane pass.
+          // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
+          auto store_mb = [&](uint64_t e, const uint32_t (&r)[4]) {
+            const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
+            const int rr = ti >> 3, col = ti & 7;
+            const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
+            const int jj = ((G >> 2) & 1) << 1 | (G & 1);
+            const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
+            const int k0 = 32 * rr + 8 * t + 4 * (mk >> 1);
+            *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r[0], r[1]);
+            *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r[2], r[3]);
+          };
+          uint64_t ent[4];
+          bool ok[4];
+#pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int j = j0 + k;
-            const bool valid = u >= n_group && j < n_group + n_mb;
-            const uint64_t ent = valid ? list[j] : 0ull;
-            const int cls = valid ? (int)((ent >> 48) & 15u) : -1;
-            const unsigned vm = __ballot_sync(0xffffffffu, valid);
-            const int cls0 = __shfl_sync(0xffffffffu, cls, vm ? __ffs(vm) - 1 : 0);
-            const uint8_t* prim = payload + (uint32_t)(ent & 0xffffu);
-            const uint8_t* sec = payload + (uint32_t)((ent >> 16) & 0xffffu);
-            const uint32_t s2 = h2const((uint16_t)((ent >> 32) & 0xffffu));
-            const int ti = (int)((ent >> 52) & 15u), G = (int)((ent >> 56) & 15u), mk = (int)((ent >> 60) & 3u);
-            uint32_t r[4] = {0u, 0u, 0u, 0u};
-            if (__all_sync(0xffffffffu, !valid || cls == cls0) && cls0 != kClassGeneric) {
-              switch (cls0) {  // warp-uniform branch
-                case 1: decode_mb_half<2>(prim, sec, h, s2, r); break;
-                case 2: decode_mb_half<3>(prim, sec, h, s2, r); break;
-                case 3: decode_mb_half<4>(prim, sec, h, s2, r); break;
-                case 4: decode_mb_half<5>(prim, sec, h, s2, r); break;
-                case 5: decode_mb_half<6>(prim, sec, h, s2, r); break;
-                case 6: decode_mb_half<8>(prim, sec, h, s2, r); break;
-                default: break;
-              }
-            } else if (valid) {
-              switch (cls) {
-                case 1: decode_mb_half<2>(prim, sec, h, s2, r); break;
-                case 2: decode_mb_half<3>(prim, sec, h, s2, r); break;
-                case 3: decode_mb_half<4>(prim, sec, h, s2, r); break;
-                case 4: decode_mb_half<5>(prim, sec, h, s2, r); break;
-                case 5: decode_mb_half<6>(prim, sec, h, s2, r); break;
-                case 6: decode_mb_half<8>(prim, sec, h, s2, r); break;
-                case kClassGeneric: {
-                  const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
-                  const uint8_t* rec =
-                      payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
-                  const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
-                  const int L = leaf_of(d.leaf_start, 4 * G + mk);
-                  decode_half_w16(lt_entry(ltab, L, s.scale_words), lt_scale_of(ltab, L, s.scale_words), prim,
-                                  sec, h, p.pow2e, r);
-                  break;
-                }
-                default: break;
-              }
+            const int rel = r0 + k * n_mbu + ((lane >> 1) - e0);
+            ok[k] = (lane >> 1) >= e0 && rel < n_mb;
+            ent[k] = ok[k] ? list[n_group + rel] : 0ull;
+          }
+          bool any_generic = false;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int cls = (int)((ent[k] >> 48) & 15u);
+            if (ok[k] && cls == kClassGeneric) any_generic = true;
+            if (ok[k] && cls != kClassGeneric) {
+              uint32_t r[4];
+              decode_half_class(dtab, cls, payload + (uint32_t)(ent[k] & 0xffffu),
+                                payload + (uint32_t)((ent[k] >> 16) & 0xffffu), h,
+                                h2const((uint16_t)((ent[k] >> 32) & 0xffffu)), r);
+              store_mb(ent[k], r);
             }
-            if (valid) {
-              // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
-              const int rr = ti >> 3, col = ti & 7;
-              const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
-              const int jj = ((G >> 2) & 1) << 1 | (G & 1);
-              const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
-              const int k0 = 32 * rr + 8 * t + 4 * (mk >> 1);
-              *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r[0], r[1]);
-              *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r[2], r[3]);
+          }
+          if (__any_sync(0xffffffffu, any_generic)) {
+#pragma unroll 1
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t e = k == 0 ? ent[0] : k == 1 ? ent[1] : k == 2 ? ent[2] : ent[3];
+              const bool v = k == 0 ? ok[0] : k == 1 ? ok[1] : k == 2 ? ok[2] : ok[3];
+              if (v && (int)((e >> 48) & 15u) == kClassGeneric) {
+                const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
+                const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
+                const uint8_t* rec =
+                    payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
+                const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
+                const int L = leaf_of(d.leaf_start, 4 * G + mk);
+                uint32_t r[4];
+                decode_half_w16(lt_entry(ltab, L, s.scale_words), lt_scale_of(ltab, L, s.scale_words),
+                                payload + (uint32_t)(e & 0xffffu), payload + (uint32_t)((e >> 16) & 0xffffu), h,
+                                p.pow2e, r);
+                store_mb(e, r);
+              }
             }
           }
         }
@@ -384,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full_ab[st]);
+          mbar_arrive(&full_b[sb]);
           mbar_arrive(&pempty[ps]);
         }
       }
@@ -399,27 +480,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc::fence_after();
+      // 16x256b loads give each lane quad 8 consecutive columns of one row,
+      // so every float2 store instruction writes 8 full 32-byte sectors.
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
-        const int m = mblk * BM + half * 128 + 32 * warp + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t v[32];
-          tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * warp) << 16) + half * 256 + c, v);
-          const int n0 = band * BN + c;
-          if (m < p.M) {
-            float* y = p.Y + (long long)m * p.ldy + n0;
-            if (n0 + 32 <= s.N) {
+        for (int lb = 0; lb < 32; lb += 16) {
+          const int m0 = mblk * BM + half * 128 + 32 * warp + lb + (lane >> 2);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 64) {
+            uint32_t v[32];
+            tc::tmem_ld_16x256b_x8(tmem + ((uint32_t)(32 * warp + lb) << 16) + half * 256 + c, v);
+            const int nb = band * BN + c + 2 * (lane & 3);
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                *reinterpret_cast<float4*>(y + j) =
-                    make_float4(__uint_as_float(v[j]) * p.inv_pow2e, __uint_as_float(v[j + 1]) * p.inv_pow2e,
-                                __uint_as_float(v[j + 2]) * p.inv_pow2e, __uint_as_float(v[j + 3]) * p.inv_pow2e);
+            for (int hr = 0; hr < 2; ++hr) {
+              const int m = m0 + 8 * hr;
+              if (m >= p.M) continue;
+              float* y = p.Y + (long long)m * p.ldy;
+#pragma unroll
+              for (int r = 0; r < 8; ++r) {
+                const int n = nb + 8 * r;
+                const float a = __uint_as_float(v[4 * r + 2 * hr]) * p.inv_pow2e;
+                const float b = __uint_as_float(v[4 * r + 2 * hr + 1]) * p.inv_pow2e;
+                if (p.vec2 && n + 1 < s.N) {
+                  *reinterpret_cast<float2*>(y + n) = make_float2(a, b);
+                } else {
+                  if (n < s.N) y[n] = a;
+                  if (n + 1 < s.N) y[n + 1] = b;
+                }
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < s.N) y[j] = __uint_as_float(v[j]) * p.inv_pow2e;
             }
           }
         }
@@ -509,10 +598,18 @@ EncodeTiledFn encode_tiled() {
 }
 
 struct PrefillPlan {
-  int Kp, Np, nkb, n_mblk, n_bands, n_tiles, S;
+  int Kp, Np, nkb, n_mblk, n_bands, n_tiles, SA, SB;
   uint32_t ring_bytes;
   size_t smem, xp_bytes, yp_bytes;
 };
+
+// Compile-time overrides of the pipeline depths (tuning builds only).
+#ifndef MTC_PREFILL_SA
+#define MTC_PREFILL_SA 0
+#endif
+#ifndef MTC_PREFILL_SB
+#define MTC_PREFILL_SB 0
+#endif
 
 bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* pl) {
   pl->Kp = s->tk * kTile;
@@ -522,19 +619,32 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
   pl->n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
   pl->n_tiles = pl->n_mblk * pl->n_bands;
   const size_t cap = 227 * 1024;
-  const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/;
-  // Three A/B stages let dequant run two stages ahead of the MMA; the packed
-  // byte ring takes the rest.  The ring must hold the largest stage and
-  // should hold about three typical ones; fall back to two A/B stages when
-  // three leave less than twice the largest stage.
+  const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/ + 32 * kMetaChunk /*stage metadata*/;
+  // Three A stages cover the TMA latency; W stages let dequant run ahead of
+  // the MMA (two suffice while dequant is faster than the MMA).  The packed
+  // byte ring takes the rest and should hold at least two of the largest
+  // stages, so three W stages are used only when that still holds.
   const size_t biggest = s->max_stage_bytes ? s->max_stage_bytes : 2 * s->max_row_bytes + 8 * 1024 + kDescBytes;
-  int S = 3;
-  while (S > 2 && cap - fixed - (size_t)S * (kABytes + kBBytes) < 2 * biggest) --S;
-  const size_t ring = (cap - fixed - (size_t)S * (kABytes + kBBytes)) & ~(size_t)127;
+  static const int cand[3][2] = {{3, 3}, {3, 2}, {2, 2}};
+  int SA = 2, SB = 2;
+  for (int c = 0; c < 3; ++c) {
+    const size_t used = fixed + (size_t)cand[c][0] * kABytes + (size_t)cand[c][1] * kBBytes;
+    if (used + 2 * biggest <= cap || c == 2) {
+      SA = cand[c][0];
+      SB = cand[c][1];
+      break;
+    }
+  }
+  if (MTC_PREFILL_SA > 0) SA = MTC_PREFILL_SA;
+  if (MTC_PREFILL_SB > 0) SB = MTC_PREFILL_SB;
+  const size_t used = fixed + (size_t)SA * kABytes + (size_t)SB * kBBytes;
+  if (used >= cap || SA > kMaxS || SB > kMaxS) return false;
+  const size_t ring = (cap - used) & ~(size_t)127;
   if (ring < biggest) return false;
-  pl->S = S;
+  pl->SA = SA;
+  pl->SB = SB;
   pl->ring_bytes = (uint32_t)ring;
-  pl->smem = fixed + (size_t)S * (kABytes + kBBytes) + ring;
+  pl->smem = used + ring;
   pl->xp_bytes = ((size_t)M * pl->Kp * 2 + 255) & ~(size_t)255;
   pl->yp_bytes = permuted ? (size_t)M * pl->Np * 4 : 0;
   return true;
@@ -663,7 +773,9 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   p.n_bands = pl.n_bands;
   p.n_tiles = pl.n_tiles;
   p.nkb = pl.nkb;
-  p.S = pl.S;
+  p.vec2 = ((p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 7) == 0) ? 1 : 0;
+  p.SA = pl.SA;
+  p.SB = pl.SB;
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
