@@ -40,12 +40,12 @@ class StreamDesc(ctypes.Structure):
         ("K", c_i32), ("N", c_i32), ("tk", c_i32), ("tn", c_i32),
         ("band_tiles", c_i32), ("exp2", c_i32),
         ("record_bytes", c_u64), ("max_row_bytes", c_u32), ("scale_words", c_i32),
-        ("stage_lists", c_p), ("stage_counts", c_p), ("stage_offsets", c_p),
+        ("stage_lists", c_p), ("stage_counts", c_p), ("stage_offsets", c_p), ("stage_ranges", c_p),
         ("max_stage_bytes", c_u32), ("pad_", c_u32),
     ]
 
 
-assert ctypes.sizeof(StreamDesc) == 96
+assert ctypes.sizeof(StreamDesc) == 104
 
 # name -> (restype, argtypes); every symbol declared in include/mtc_b200.h.
 SIGNATURES = {
@@ -55,7 +55,7 @@ SIGNATURES = {
     "mtc_repack_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p,
                                 ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_fill": (c_i32, [c_p, c_u64, c_p, c_p, ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
-    "mtc_repack_stage_plan": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, ctypes.POINTER(c_u64), c_p]),
+    "mtc_repack_stage_plan": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, c_p, ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_stage_fill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
     "mtc_rd_search": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p, c_i32, c_i32, c_p, c_p, c_p]),
     "mtc_dequant": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_p, c_p, c_i64, c_p]),

@@ -432,13 +432,34 @@ __device__ __forceinline__ void decode_half_uniform(const uint32_t* tab, int mod
 }
 
 // One micro-block half of decode class c (0 = P0 zeros; 1..6 = P2, P3, P4,
-// P5, P6, P8) through the table decoder: lanes of different classes run the
-// same instructions.  tab = the decoder table in shared memory.
+// P5, P6, P8) through the table decoder, without branches: lanes of
+// different classes run the same instructions, and several calls can be
+// interleaved by the compiler.  Both 16-bit secondary words are always read
+// (they lie inside the staged records, or just past them in shared memory).
+// tab = the decoder table in shared memory.
 __device__ __forceinline__ void decode_half_class(const uint32_t* tab, int c, const uint8_t* prim,
                                                   const uint8_t* sec, int h, uint32_t s2, uint32_t r[4]) {
   const int cc = c > 0 ? c : 1;
-  const int mode = cc + 1 + (cc == 6 ? 1 : 0);
-  decode_half_uniform(tab + 20 * (cc - 1), mode, prim, sec, h, c > 0 ? s2 : 0u, r);
+  const bool w2 = cc <= 2, w8 = cc == 6, w4 = !w2 && !w8;       // primary plane width 2 / 4 / 8
+  const bool s1 = cc == 2 || cc == 4, s2w = cc == 5;             // secondary plane width 1 / 2
+  const int offA = w2 ? 0 : (w4 ? 4 * h : 8 * h);
+  const int offB = w8 ? 8 * h + 4 : offA;
+  const uint32_t A = ld32(prim + offA) >> (w2 ? 8 * h : 0);
+  const uint32_t B = ld32(prim + offB) >> (w2 ? 8 * h : 0);
+  const uint32_t x0 = A, x1 = A >> (w8 ? 8 : 0), x2 = B >> (w4 ? 8 : 0), x3 = B >> (w2 ? 0 : 8);
+  const uint32_t lo = ld16(sec), hi = ld16(sec + 2);
+  const uint32_t S = s1 ? (__byte_perm(lo, 0u, 0x4140) >> (4 * h)) : (s2w ? ((lo | (hi << 16)) >> (8 * h)) : 0u);
+  const uint32_t* row = tab + 20 * (cc - 1);
+  const uint4 pm = *reinterpret_cast<const uint4*>(row);
+  const uint4 sm = *reinterpret_cast<const uint4*>(row + 4);
+  const uint4 cf = *reinterpret_cast<const uint4*>(row + 8);
+  const uint4 cs = *reinterpret_cast<const uint4*>(row + 12);
+  const uint4 K = *reinterpret_cast<const uint4*>(row + 16);
+  const uint32_t sc = c > 0 ? s2 : 0u;
+  r[0] = hmul2u(hfma2u(lop_or(x0, pm.x), cf.x, hfma2u(lop_or(S, sm.x), cs.x, K.x)), sc);
+  r[1] = hmul2u(hfma2u(lop_or(x1, pm.y), cf.y, hfma2u(lop_or(S, sm.y), cs.y, K.y)), sc);
+  r[2] = hmul2u(hfma2u(lop_or(x2, pm.z), cf.z, hfma2u(lop_or(S, sm.z), cs.z, K.z)), sc);
+  r[3] = hmul2u(hfma2u(lop_or(x3, pm.w), cf.w, hfma2u(lop_or(S, sm.w), cs.w, K.w)), sc);
 }
 
 // Four micro-blocks of one leaf (a group), decode class c, through the table
@@ -619,28 +640,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
-  }
-}
-// The same for a barrier that also receives arrivals from the other CTA of
-// a cluster: acquire at cluster scope, so that CTA's shared-memory writes
-// made before its arrive are visible here.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
     if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }

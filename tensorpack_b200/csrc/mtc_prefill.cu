@@ -31,27 +31,38 @@
 namespace mtc {
 namespace {
 
-constexpr int BM = 256;   // tokens per CTA tile (two M=128 MMAs)
-constexpr int BN = 256;   // features per CTA tile (one column band)
+constexpr int CBM = 512;  // tokens per CTA pair tile (two M=256 pair MMAs)
+constexpr int BM = 256;   // tokens whose A rows one CTA holds (128 per accumulator)
+constexpr int BN = 256;   // features per pair tile (one column band)
+constexpr int BNH = 128;  // features one CTA dequantises (its half of the band)
 constexpr int BK = 64;    // K per pipeline stage (two k-tile rows)
 constexpr int kEpiWarps = 4;
 constexpr int kProdWarp = 4;   // A tiles
-constexpr int kMmaWarp = 5;
-constexpr int kPackWarp = 6;   // packed stages
+constexpr int kMmaWarp = 5;    // TMEM allocation (both CTAs), MMA issue (even CTA)
+constexpr int kPackWarp = 6;   // packed sub-stages
 constexpr int kDeqWarp0 = 7;
-constexpr int kDeqWarps = 16;
-constexpr int kThreads = (kDeqWarp0 + kDeqWarps) * 32;
-constexpr uint32_t kABytes = BM * BK * 2;
-constexpr uint32_t kBBytes = BN * BK * 2;
+constexpr int kDeqWarps = 8;   // dequant warps per stage
+// Dequant groups take alternate stages, so each group has two stage times
+// for one stage: a stage's decode is latency-bound (dependent shared-memory
+// loads, decode, stores), and a second group hides that latency.
+#ifndef MTC_DEQ_GROUPS
+#define MTC_DEQ_GROUPS 2
+#endif
+constexpr int kDeqGroups = MTC_DEQ_GROUPS;
+constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
+constexpr uint32_t kAHalf = 128 * BK * 2;   // A rows of one accumulator
+constexpr uint32_t kABytes = 2 * kAHalf;
+constexpr uint32_t kBBytes = BNH * BK * 2;
 constexpr int kMaxS = 4;
-// Packed data of each stage sits contiguously in a shared-memory byte ring:
-// [256 B tile descriptors of the stage's 2 k rows][work list][records].
-// Stage sizes vary (in MTC-QT-P allocations the largest is about twice the
-// median), so a ring keeps several typical stages in flight where fixed slots
-// sized for the largest one would hold one or two.
-constexpr int kRingSlots = 8;          // stages in flight at most
-constexpr int kMetaChunk = 64;         // stages of metadata the packed producer stages at a time
-constexpr uint32_t kDescBytes = 256;
+// Packed data of each sub-stage sits contiguously in a shared-memory byte
+// ring: [128 B tile descriptors: 4 of k-row 2kb, 4 of k-row 2kb + 1][work
+// list][records of the row-0 part][records of the row-1 part].  Sub-stage
+// sizes vary (in MTC-QT-P allocations the largest is about twice the
+// median), so a ring keeps several typical ones in flight where fixed slots
+// sized for the largest would hold one or two.
+constexpr int kRingSlots = 8;          // sub-stages in flight at most
+constexpr int kMetaChunk = 32;         // sub-stages of metadata the packed producer stages at a time
+constexpr uint32_t kDescBytes = 128;
 constexpr int kClassGeneric = 7;
 
 struct PrefillParams {
@@ -77,33 +88,38 @@ __device__ __forceinline__ uint32_t sw128_off(int n, int k) {
   return (uint32_t)n * 128u + ((((uint32_t)k >> 3) ^ ((uint32_t)n & 7u)) << 4) + (((uint32_t)k & 7u) << 1);
 }
 
+// Launched as clusters of two CTAs; cluster c takes pair tiles c, c + G, ...
+// (G = number of clusters), each 512 tokens x one band of 256 features.
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte aligned base for the SWIZZLE_128B atoms; pointer arithmetic on
-  // the __shared__ array keeps the shared address space visible to the compiler
+  // 1024-byte aligned base for the SWIZZLE_128B atoms (the same offset in
+  // both CTAs, which the pair MMA requires); pointer arithmetic on the
+  // __shared__ array keeps the shared address space visible to the compiler
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = sA + p.SA * kABytes;
   uint8_t* sP = sB + p.SB * kBBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
-  uint64_t* full_a = bars;                    // [SA] TMA bytes
-  uint64_t* empty_a = full_a + kMaxS;         // [SA] MMA commit
-  uint64_t* full_b = empty_a + kMaxS;         // [SB] dequant warps
-  uint64_t* empty_b = full_b + kMaxS;         // [SB] MMA commit
+  uint64_t* full_a = bars;                    // [SA] even CTA: TMA bytes of both CTAs
+  uint64_t* empty_a = full_a + kMaxS;         // [SA] MMA commit (both CTAs)
+  uint64_t* full_b = empty_a + kMaxS;         // [SB] even CTA: dequant warps of both CTAs
+  uint64_t* empty_b = full_b + kMaxS;         // [SB] MMA commit (both CTAs)
   uint64_t* pfull = empty_b + kMaxS;          // [kRingSlots] bulk-copy bytes
   uint64_t* pempty = pfull + kRingSlots;      // [kRingSlots] dequant warps
-  uint64_t* acc_full = pempty + kRingSlots;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_empty + 1;
+  uint64_t* acc_full = pempty + kRingSlots;   // MMA commit (both CTAs)
+  uint64_t* acc_empty = acc_full + 1;         // even CTA: epilogue warps of both CTAs
+  uint64_t* drain = acc_empty + 1;            // MMA commit (both CTAs)
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
-  uint32_t* pmeta = tmem_slot + 4;            // [kRingSlots][4]: ring offset, counts, list bytes
+  uint32_t* pmeta = tmem_slot + 4;            // [kRingSlots][4]: ring offset, counts, list bytes, part-0 bytes
   uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 512);  // decoder table
-  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1024);      // [2][kMetaChunk]
+  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1024);      // [2][kMetaChunk][2]
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = tc::cluster_rank();
+  const int cid = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
 
   if (tid == 0) {
     for (int i = 0; i < p.SA; ++i) {
@@ -111,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty_a[i], 1);
     }
     for (int i = 0; i < p.SB; ++i) {
-      mbar_init(&full_b[i], kDeqWarps);
+      mbar_init(&full_b[i], 2 * kDeqWarps);
       mbar_init(&empty_b[i], 1);
     }
     for (int i = 0; i < kRingSlots; ++i) {
@@ -119,23 +135,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&pempty[i], kDeqWarps);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kEpiWarps);
+    mbar_init(acc_empty, 2 * kEpiWarps);
     mbar_init(drain, 1);
     flags[0] = 0;
-    fence_barrier_init();
+    tc::fence_mbarrier_init_cluster();
   }
   if (warp == 0) load_dec_table(dtab, lane);
-  if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, 512);
+  if (warp == kMmaWarp) tc::tmem_alloc_pair(tmem_slot, 512);
   tc::fence_before();
-  __syncthreads();
+  tc::cluster_sync();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kProdWarp) {
     // ---------------------------------------------------------------- A producer
+    // This CTA's A rows are rows 256 * rank .. + 255 of the pair tile, one
+    // box: the first 128 feed accumulator 0, the next 128 accumulator 1 (the
+    // pair MMA takes accumulator rows 0-127 from the even CTA and 128-255
+    // from the odd one); the bytes count on the even CTA's barrier.
     if (lane == 0) {
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
+      for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters) {
         const int mblk = tile / p.n_bands;
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int sa = it % p.SA;
@@ -144,74 +164,69 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (flags[0]) break;
-          mbar_expect_tx(&full_a[sa], kABytes);
-          tc::tma_load_2d(sA + sa * kABytes, &tmap_x, kb * BK, mblk * BM, &full_a[sa]);
+          if (rank == 0) mbar_expect_tx(&full_a[sa], 2 * kABytes);
+          const uint32_t bar = tc::mapa(&full_a[sa], 0);
+          tc::tma_load_2d_pair(sA + sa * kABytes, &tmap_x, kb * BK, mblk * CBM + 256 * (int)rank, bar);
         }
       }
-      if (flags[0]) {
-        // aborting: let the loads still in flight land before the CTA exits
-        for (uint32_t j = it > (uint32_t)p.SA ? it - p.SA : 0u; j < it; ++j)
-          (void)mbar_wait(&full_a[j % p.SA], (j / p.SA) & 1, 10000000ull);
-        flag(p.status, MTC_STATUS_TIMEOUT);
-      }
+      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
     }
   } else if (warp == kPackWarp) {
     // ---------------------------------------------------------------- packed producer
-    // The whole warp loads the per-stage metadata (record range, entry
-    // counts, list offset) of 64 stages at a time into shared memory, one
-    // chunk ahead of lane 0, which issues the bulk copies; so lane 0 never
-    // waits on a global load.
-    const int n_my_tiles = blockIdx.x < p.n_tiles ? (p.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    // The whole warp loads the metadata (record ranges, entry counts, list
+    // offset) of 32 sub-stages at a time into shared memory, one chunk ahead
+    // of lane 0, which issues the bulk copies; so lane 0 never waits on a
+    // global load.
+    const int n_my_tiles = cid < p.n_tiles ? (p.n_tiles - 1 - cid) / n_clusters + 1 : 0;
     const int chunks_per_tile = (p.nkb + kMetaChunk - 1) / kMetaChunk;
     const int n_chunks = n_my_tiles * chunks_per_tile;
-    uint4 nxt[kMetaChunk / 32];
+    uint4 nxt0, nxt1;
     auto load_chunk = [&](int q) {
-      const int tile = blockIdx.x + (q / chunks_per_tile) * gridDim.x;
+      const int tile = cid + (q / chunks_per_tile) * n_clusters;
       const int band = tile % p.n_bands;
-      const uint32_t* row_off = s.row_off + (size_t)band * (s.tk + 1);
-#pragma unroll
-      for (int h = 0; h < kMetaChunk / 32; ++h) {
-        const int kb = (q % chunks_per_tile) * kMetaChunk + 32 * h + lane;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (q < n_chunks && kb < p.nkb) {
-          const size_t stage = (size_t)band * p.nkb + kb;
-          const uint32_t off = row_off[2 * kb];
-          v = make_uint4(off, row_off[min(2 * kb + 2, s.tk)] - off, s.stage_counts[stage], s.stage_offsets[stage]);
-        }
-        nxt[h] = v;
+      const int kb = (q % chunks_per_tile) * kMetaChunk + lane;
+      nxt0 = make_uint4(0u, 0u, 0u, 0u);
+      nxt1 = make_uint4(0u, 0u, 0u, 0u);
+      if (q < n_chunks && kb < p.nkb) {
+        const size_t sub = 2 * ((size_t)band * p.nkb + kb) + rank;
+        nxt0 = *reinterpret_cast<const uint4*>(s.stage_ranges + 4 * sub);
+        nxt1 = make_uint4(s.stage_counts[sub], s.stage_offsets[sub], 0u, 0u);
       }
     };
     auto store_chunk = [&](int buf) {
-#pragma unroll
-      for (int h = 0; h < kMetaChunk / 32; ++h) smeta[buf * kMetaChunk + 32 * h + lane] = nxt[h];
+      smeta[2 * (buf * kMetaChunk + lane)] = nxt0;
+      smeta[2 * (buf * kMetaChunk + lane) + 1] = nxt1;
     };
     load_chunk(0);
     store_chunk(0);
     __syncwarp();
     uint32_t it = 0;
-    uint32_t oldest = 0;                              // oldest stage not yet known to be released
+    uint32_t oldest = 0;                              // oldest sub-stage not yet known to be released
     unsigned long long ring_head = 0;                 // monotonic byte position in the ring
     uint32_t head_off = 0;                            // ring_head modulo the ring size
-    unsigned long long ring_start[kRingSlots];        // start position of each stage in flight
+    unsigned long long ring_start[kRingSlots];        // start position of each sub-stage in flight
     for (int q = 0; q < n_chunks; ++q) {
       load_chunk(q + 1);                              // in flight while lane 0 issues chunk q
       if (lane == 0) {
-        const int tile = blockIdx.x + (q / chunks_per_tile) * gridDim.x;
+        const int tile = cid + (q / chunks_per_tile) * n_clusters;
         const int band = tile % p.n_bands;
         const int kb0 = (q % chunks_per_tile) * kMetaChunk;
         const int kb1 = min(p.nkb, kb0 + kMetaChunk);
-        const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
+        const int width = max(0, min(4, s.tn - band * s.band_tiles - 4 * (int)rank));  // tiles of this half
         for (int kb = kb0; kb < kb1 && !flags[0]; ++kb, ++it) {
-          // Packed data of the stage goes to the byte ring as one contiguous
-          // piece: tile descriptors (256 B) | work list | records.  Its ring
-          // range must be free: release older stages (FIFO) until it is.
-          const uint4 m = smeta[(q & 1) * kMetaChunk + (kb - kb0)];
-          const uint32_t off = m.x, bytes = m.y, cnt = m.z;
+          // The sub-stage goes to the byte ring as one contiguous piece:
+          // descriptors (128 B) | work list | row-0 records | row-1 records.
+          // Its ring range must be free: release older sub-stages (FIFO)
+          // until it is.
+          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0))];
+          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0)) + 1];
+          const uint32_t cnt = mc.x;
           const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
           const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
           const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
+          const uint32_t bytes = rg.y + rg.w;
           const uint32_t need = kDescBytes + lbytes + bytes;
-          if (need > p.ring_bytes || (off & 15u) || (bytes & 15u)) {
+          if (need > p.ring_bytes || ((rg.x | rg.y | rg.z | rg.w) & 15u)) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
@@ -225,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             start = 0;
           }
           // live bytes are [ring_start[oldest], ring_head): the new piece must
-          // end within one ring length of the oldest live stage's start
+          // end within one ring length of the oldest live sub-stage's start
           bool ok = true;
           while (it - oldest >= (uint32_t)kRingSlots ||
                  (oldest != it && ring_start[oldest % kRingSlots] + p.ring_bytes < pos + need)) {
@@ -246,14 +261,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           pmeta[4 * ps + 0] = start;
           pmeta[4 * ps + 1] = cnt;
           pmeta[4 * ps + 2] = lbytes;
+          pmeta[4 * ps + 3] = rg.y;
           uint8_t* dst = sP + start;
-          mbar_expect_tx(&pfull[ps], bytes + 16u * width * (r1 - r0) + 8u * ((n_ent + 1u) & ~1u));
-          for (int r = r0; r < r1; ++r)
-            bulk_g2s(dst + 128 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles, 16u * width,
-                     &pfull[ps]);
-          if (n_ent)
-            bulk_g2s(dst + kDescBytes, s.stage_lists + m.w, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
-          bulk_g2s(dst + kDescBytes + lbytes, s.records + off, bytes, &pfull[ps]);
+          const uint32_t dbytes = width > 0 ? 16u * width * (r1 - r0) : 0u;
+          mbar_expect_tx(&pfull[ps], bytes + dbytes + 8u * ((n_ent + 1u) & ~1u));
+          if (width > 0) {
+            for (int r = r0; r < r1; ++r)
+              bulk_g2s(dst + 64 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles + 4 * rank,
+                       16u * width, &pfull[ps]);
+          }
+          if (n_ent) bulk_g2s(dst + kDescBytes, s.stage_lists + mc.y, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
+          if (rg.y) bulk_g2s(dst + kDescBytes + lbytes, s.records + rg.x, rg.y, &pfull[ps]);
+          if (rg.w) bulk_g2s(dst + kDescBytes + lbytes + rg.y, s.records + rg.z, rg.w, &pfull[ps]);
         }
       }
       __syncwarp();
@@ -267,11 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       flag(p.status, MTC_STATUS_TIMEOUT);
     }
   } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16_f32(128, BN);
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16_f32(256, BN);
       uint32_t it = 0, tcount = 0;
-      for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x, ++tcount) {
+      for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters, ++tcount) {
         if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1, p.timeout_ns)) {
           flags[0] = 1;
           break;
@@ -291,33 +310,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bd = tc::smem_desc_k_sw128(b0 + 32 * j);
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            tc::mma_f16_ss(tmem, tc::smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
-            tc::mma_f16_ss(tmem + 256, tc::smem_desc_k_sw128(a0 + 128 * 128 + 32 * j), bd, idesc, acc);
+            tc::mma_f16_ss_pair(tmem, tc::smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
+            tc::mma_f16_ss_pair(tmem + 256, tc::smem_desc_k_sw128(a0 + kAHalf + 32 * j), bd, idesc, acc);
           }
-          tc::commit(&empty_a[sa]);
-          tc::commit(&empty_b[sb]);
+          tc::commit_pair(&empty_a[sa]);
+          tc::commit_pair(&empty_b[sb]);
         }
         if (flags[0]) break;
-        tc::commit(acc_full);
+        tc::commit_pair(acc_full);
       }
       // make sure no MMA is still reading shared memory or writing TMEM
-      tc::commit(drain);
+      tc::commit_pair(drain);
       (void)mbar_wait(drain, 0, 100000000ull);
       if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
     }
   } else if (warp >= kDeqWarp0) {
     // ---------------------------------------------------------------- dequant
-    // The stage's work list holds group entries (one 8x8 leaf group, 4
+    // The sub-stage's work list holds group entries (one 8x8 leaf group, 4
     // micro-blocks) and micro-block entries (split groups), each run sorted by
-    // decode class.  Work unit = one group entry or four consecutive
-    // micro-block entries; warp w takes units 16w .. 16w + 15, lane pair
-    // (2e, 2e + 1) decodes the two column halves of unit e.  Sorted runs make
-    // most warps mode-uniform, so they take one specialised path.
-    const int dw = warp - kDeqWarp0;
+    // decode class.  Work unit = one group entry or four micro-block entries;
+    // warp w takes units 16w .. 16w + 15, lane pair (2e, 2e + 1) decodes the
+    // two column halves of unit e.  Sorted runs make most warps mode-uniform,
+    // so they take one specialised path; others use the table decoder.
+    const int grp = (warp - kDeqWarp0) / kDeqWarps;
+    const int dw = (warp - kDeqWarp0) % kDeqWarps;
     const int h = lane & 1;
+    const uint32_t full_b_remote = tc::mapa(full_b, 0);
     uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x) {
+    for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters) {
       for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        if ((int)(it % kDeqGroups) != grp) continue;  // the other group's stage
         const int sb = it % p.SB, ps = it % kRingSlots;
         if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
           flags[0] = 1;
@@ -332,6 +354,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t cnt = pmeta[4 * ps + 1];
         const uint64_t* list = reinterpret_cast<const uint64_t*>(sl + kDescBytes);
         const uint8_t* payload = sl + kDescBytes + pmeta[4 * ps + 2];
+        const uint32_t part0 = pmeta[4 * ps + 3];
+        const mtc_tile_desc* descs = reinterpret_cast<const mtc_tile_desc*>(sl);
+        // record of tile ti (row * 4 + column) inside the payload
+        auto tile_record = [&](int ti) -> const uint8_t* {
+          const mtc_tile_desc& d = descs[ti];
+          return (ti >> 2) == 0 ? payload + (d.record_off - descs[0].record_off)
+                                : payload + part0 + (d.record_off - descs[4].record_off);
+        };
         const int n_group = (int)(cnt & 0xffffu), n_mb = (int)(cnt >> 16);
         const int u = 16 * dw + (lane >> 1);
         // Lane pairs e >= e0 of this warp hold micro-block units: 4 x (16 -
@@ -348,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
           auto store_mb = [&](uint64_t e, const uint32_t (&r)[4]) {
             const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
-            const int rr = ti >> 3, col = ti & 7;
+            const int rr = ti >> 2, col = ti & 3;
             const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
             const int jj = ((G >> 2) & 1) << 1 | (G & 1);
             const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
@@ -364,19 +394,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok[k] = (lane >> 1) >= e0 && rel < n_mb;
             ent[k] = ok[k] ? list[n_group + rel] : 0ull;
           }
+          // all four decodes run unconditionally (invalid and generic lanes
+          // decode zeros at offset 0), so the compiler can interleave them;
+          // only the stores are predicated
           bool any_generic = false;
+          uint32_t r4[4][4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int cls = (int)((ent[k] >> 48) & 15u);
             if (ok[k] && cls == kClassGeneric) any_generic = true;
-            if (ok[k] && cls != kClassGeneric) {
-              uint32_t r[4];
-              decode_half_class(dtab, cls, payload + (uint32_t)(ent[k] & 0xffffu),
-                                payload + (uint32_t)((ent[k] >> 16) & 0xffffu), h,
-                                h2const((uint16_t)((ent[k] >> 32) & 0xffffu)), r);
-              store_mb(ent[k], r);
-            }
+            const bool dec = ok[k] && cls != kClassGeneric;
+            const uint64_t e = dec ? ent[k] : 0ull;
+            decode_half_class(dtab, dec ? cls : 0, payload + (uint32_t)(e & 0xffffu),
+                              payload + (uint32_t)((e >> 16) & 0xffffu), h, h2const((uint16_t)((e >> 32) & 0xffffu)),
+                              r4[k]);
           }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (ok[k] && (int)((ent[k] >> 48) & 15u) != kClassGeneric) store_mb(ent[k], r4[k]);
           if (__any_sync(0xffffffffu, any_generic)) {
 #pragma unroll 1
             for (int k = 0; k < 4; ++k) {
@@ -384,11 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const bool v = k == 0 ? ok[0] : k == 1 ? ok[1] : k == 2 ? ok[2] : ok[3];
               if (v && (int)((e >> 48) & 15u) == kClassGeneric) {
                 const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
-                const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
-                const uint8_t* rec =
-                    payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
-                const uint32_t* ltab = reinterpret_cast<const uint32_t*>(rec);
-                const int L = leaf_of(d.leaf_start, 4 * G + mk);
+                const uint32_t* ltab = reinterpret_cast<const uint32_t*>(tile_record(ti));
+                const int L = leaf_of(descs[ti].leaf_start, 4 * G + mk);
                 uint32_t r[4];
                 decode_half_w16(lt_entry(ltab, L, s.scale_words), lt_scale_of(ltab, L, s.scale_words),
                                 payload + (uint32_t)(e & 0xffffu), payload + (uint32_t)((e >> 16) & 0xffffu), h,
@@ -407,7 +439,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s2 = h2const((uint16_t)((ent >> 32) & 0xffffu));
         const int ti = (int)((ent >> 52) & 15u), G = (int)((ent >> 56) & 15u);
         uint32_t R[4][4];
-        if (__all_sync(0xffffffffu, !valid || cls == cls0) && cls0 != kClassGeneric) {
+        const bool uniform = __all_sync(0xffffffffu, !valid || cls == cls0);
+        if (uniform && cls0 != kClassGeneric) {
           switch (cls0) {  // warp-uniform branch
             case 1: decode_run4<2>(prim, sec, h, s2, R); break;
             case 2: decode_run4<3>(prim, sec, h, s2, R); break;
@@ -420,29 +453,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
           }
         } else {
-          switch (cls) {  // class boundary inside the warp, or generic groups
-            case 1: decode_run4<2>(prim, sec, h, s2, R); break;
-            case 2: decode_run4<3>(prim, sec, h, s2, R); break;
-            case 3: decode_run4<4>(prim, sec, h, s2, R); break;
-            case 4: decode_run4<5>(prim, sec, h, s2, R); break;
-            case 5: decode_run4<6>(prim, sec, h, s2, R); break;
-            case 6: decode_run4<8>(prim, sec, h, s2, R); break;
-            case kClassGeneric: {
-              const mtc_tile_desc d = reinterpret_cast<const mtc_tile_desc*>(sl)[ti];
-              const uint8_t* rec = payload + (d.record_off - reinterpret_cast<const mtc_tile_desc*>(sl)[0].record_off);
-              decode_group_generic(reinterpret_cast<const uint32_t*>(rec), d.leaf_start, G, prim, sec,
-                                   s.scale_words, h, p.pow2e, R);
-              break;
-            }
-            default:
-#pragma unroll
-              for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
-          }
+          // class boundary inside the warp: table decoder for P0..P8 (one
+          // instruction sequence), per-lane generic path for the rest
+          if (valid && cls != kClassGeneric) decode_run4_class(dtab, cls, prim, sec, h, s2, R);
+          if (valid && cls == kClassGeneric)
+            decode_group_generic(reinterpret_cast<const uint32_t*>(tile_record(ti)), descs[ti].leaf_start, G, prim,
+                                 sec, s.scale_words, h, p.pow2e, R);
         }
         if (valid) {
           // R[2 di + dj] = micro-block (2t + di, 2jj + dj) of group G: pairs 0,1
           // feature 2h (k rows 0..3), pairs 2,3 feature 2h + 1; di selects k 0..3 / 4..7
-          const int r = ti >> 3, col = ti & 7;
+          const int r = ti >> 2, col = ti & 3;
           const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
           const int jj = ((G >> 2) & 1) << 1 | (G & 1);
 #pragma unroll
@@ -456,8 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (2 * kb + 1 >= s.tk) {
           // odd number of k-tile rows: the stage's second row is zero padding
-          const int tid_d = tid - kDeqWarp0 * 32;
-          for (int c = tid_d; c < BN * 4; c += kDeqWarps * 32) {
+          const int tid_d = tid - (kDeqWarp0 + grp * kDeqWarps) * 32;
+          for (int c = tid_d; c < BNH * 4; c += kDeqWarps * 32) {
             const int f = c >> 2, ch = 4 + (c & 3);
             *reinterpret_cast<uint4*>(Bt + f * 128 + ((ch ^ (f & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
           }
@@ -465,15 +486,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full_b[sb]);
+          if (rank == 0) mbar_arrive(&full_b[sb]);
+          else tc::mbar_arrive_cluster(full_b_remote + 8u * sb);
           mbar_arrive(&pempty[ps]);
         }
       }
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 0-3)
+    // This CTA's TMEM holds its pair-tile rows 256 * rank + 128 * half + lane
+    // (half = accumulator).
+    const uint32_t acc_empty_remote = tc::mapa(acc_empty, 0);
     uint32_t tcount = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles && !flags[0]; tile += gridDim.x, ++tcount) {
+    for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters, ++tcount) {
       const int mblk = tile / p.n_bands, band = tile % p.n_bands;
       if (!mbar_wait(acc_full, tcount & 1, p.timeout_ns)) {
         flags[0] = 1;
@@ -486,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int half = 0; half < 2; ++half) {
 #pragma unroll 1
         for (int lb = 0; lb < 32; lb += 16) {
-          const int m0 = mblk * BM + half * 128 + 32 * warp + lb + (lane >> 2);
+          const int m0 = mblk * CBM + 256 * (int)rank + 128 * half + 32 * warp + lb + (lane >> 2);
 #pragma unroll 1
           for (int c = 0; c < BN; c += 64) {
             uint32_t v[32];
@@ -515,16 +540,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(acc_empty);
+        else tc::mbar_arrive_cluster(acc_empty_remote);
+      }
     }
     if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
   }
 
+  // Both CTAs are done with each other's shared memory and TMEM only when
+  // both reach this point (the even CTA's MMA thread has drained).
   tc::fence_before();
-  __syncthreads();
+  tc::cluster_sync();
   if (warp == kMmaWarp) {
     tc::fence_after();
-    tc::tmem_dealloc(tmem, 512);
+    tc::tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -615,21 +645,21 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
   pl->Kp = s->tk * kTile;
   pl->Np = s->tn * kTile;
   pl->nkb = (s->tk + 1) / 2;
-  pl->n_mblk = (M + BM - 1) / BM;
+  pl->n_mblk = (M + CBM - 1) / CBM;
   pl->n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
   pl->n_tiles = pl->n_mblk * pl->n_bands;
   const size_t cap = 227 * 1024;
-  const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/ + 32 * kMetaChunk /*stage metadata*/;
-  // Three A stages cover the TMA latency; W stages let dequant run ahead of
-  // the MMA (two suffice while dequant is faster than the MMA).  The packed
-  // byte ring takes the rest and should hold at least two of the largest
-  // stages, so three W stages are used only when that still holds.
-  const size_t biggest = s->max_stage_bytes ? s->max_stage_bytes : 2 * s->max_row_bytes + 8 * 1024 + kDescBytes;
-  static const int cand[3][2] = {{3, 3}, {3, 2}, {2, 2}};
+  const size_t fixed = 1024 /*align*/ + 1024 /*barriers, flags, decoder table*/ + 64 * kMetaChunk /*stage metadata*/;
+  // Deep A and W pipelines cover the TMA latency and let dequant run ahead
+  // of the MMA; the packed byte ring takes the rest and should hold at least
+  // two of the largest sub-stages, so the deepest pipelines that leave that
+  // much are used.
+  const size_t biggest = s->max_stage_bytes ? s->max_stage_bytes : s->max_row_bytes + 4 * 1024 + kDescBytes;
+  static const int cand[5][2] = {{4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
   int SA = 2, SB = 2;
-  for (int c = 0; c < 3; ++c) {
+  for (int c = 0; c < 5; ++c) {
     const size_t used = fixed + (size_t)cand[c][0] * kABytes + (size_t)cand[c][1] * kBBytes;
-    if (used + 2 * biggest <= cap || c == 2) {
+    if (used + 2 * biggest <= cap || c == 4) {
       SA = cand[c][0];
       SB = cand[c][1];
       break;
@@ -737,7 +767,7 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   PrefillPlan pl;
   int rc = check_prefill(s, M, permuted_output != 0, ws, ws_bytes, &pl, "mtc_prefill_gemm");
   if (rc != MTC_OK) return rc;
-  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->max_stage_bytes,
+  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
               "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
   const bool col_perm_inv = permuted_output != 0;
@@ -754,7 +784,7 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   {
     cuuint64_t dims[2] = {(cuuint64_t)pl.Kp, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)pl.Kp * 2};
-    cuuint32_t box[2] = {BK, BM};
+    cuuint32_t box[2] = {BK, 256};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Xp, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -780,13 +810,29 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
   p.timeout_ns = 2000000000ull;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   MTC_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
                  "mtc_prefill_gemm: smem attribute");
-  const int grid = pl.n_tiles < sms ? pl.n_tiles : sms;
-  prefill_kernel<<<grid, kThreads, pl.smem, st>>>(tmap, p);
+  // CTA pairs: one cluster of two CTAs per pair tile, as many clusters as
+  // can be resident at once (persistent; each loops over tiles)
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  cfg.gridDim = dim3(2, 1, 1);
+  MTC_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, prefill_kernel, &cfg),
+                 "mtc_prefill_gemm: cluster occupancy");
+  MTC_REQUIRE(max_clusters >= 1, "mtc_prefill_gemm: no CTA pair of %zu bytes of shared memory fits", pl.smem);
+  const int clusters = pl.n_tiles < max_clusters ? pl.n_tiles : max_clusters;
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  MTC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, prefill_kernel, tmap, p), "mtc_prefill_gemm: launch");
   MTC_CHECK_LAUNCH("mtc_prefill_gemm");
   return MTC_OK;
 }

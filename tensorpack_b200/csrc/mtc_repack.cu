@@ -286,28 +286,45 @@ __device__ __forceinline__ uint32_t fp16_scale_bits(float sc, bool* exact) {
   return *reinterpret_cast<const uint16_t*>(&hs);
 }
 
-// One CTA of 256 threads per stage (band, k-tile rows 2kb and 2kb + 1);
-// thread i owns group G = i & 15 of tile (row i >> 7, column (i >> 4) & 7).
-// A group covered by one leaf becomes one group entry; a group of four 4x4
-// leaves becomes four micro-block entries (each with its own mode), so every
-// entry decodes with one mode.  Group entries come first, sorted by class,
-// then micro-block entries, sorted by class.  Pass 1 (FILL = false) counts,
-// pass 2 writes at the CSR offsets.
+// Record range of the four tiles 4 * half .. 4 * half + 3 of band `band` in
+// k-tile row kt: {byte offset, bytes} (empty beyond the matrix).
+__device__ __forceinline__ uint2 half_row_range(const mtc_stream_desc& s, int band, int half, int kt) {
+  const int width = min(s.band_tiles, s.tn - band * s.band_tiles);
+  const int c0 = 4 * half;
+  if (kt >= s.tk || c0 >= width) return make_uint2(0u, 0u);
+  const uint32_t start = s.tiles[(size_t)kt * s.tn + band * s.band_tiles + c0].record_off;
+  const uint32_t end = (c0 + 4 < width) ? s.tiles[(size_t)kt * s.tn + band * s.band_tiles + c0 + 4].record_off
+                                        : s.row_off[(size_t)band * (s.tk + 1) + kt + 1];
+  return make_uint2(start, end - start);
+}
+
+// One CTA of 128 threads per sub-stage q = 2 * (band * nkb + kb) + half:
+// thread i owns group G = i & 15 of tile (row i >> 6, column 4 * half +
+// ((i >> 4) & 3)).  A group covered by one leaf becomes one group entry; a
+// group of four 4x4 leaves becomes four micro-block entries (each with its own
+// mode), so every entry decodes with one mode.  Group entries come first,
+// sorted by class, then micro-block entries, sorted by class.  Pass 1
+// (FILL = false) counts and records the sub-stage's record ranges, pass 2
+// writes at the CSR offsets.
 template <bool FILL>
-__global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int nkb, const uint32_t* __restrict__ offs,
+__global__ void __launch_bounds__(128) stage_lists_kernel(mtc_stream_desc s, int nkb, const uint32_t* __restrict__ offs,
                                                           uint32_t* __restrict__ counts, uint32_t* __restrict__ totals,
+                                                          uint32_t* __restrict__ ranges,
                                                           uint64_t* __restrict__ lists) {
   __shared__ uint32_t cnt[16];   // [0, 8) group classes, [8, 16) micro-block classes
   __shared__ uint32_t base[16];
-  const int stage = blockIdx.x;
+  const int q = blockIdx.x;
+  const int half = q & 1, stage = q >> 1;
   const int band = stage / nkb, kb = stage % nkb;
   const int i = threadIdx.x;
-  const int ti = i >> 4, G = i & 15;
-  const int r = ti >> 3, col = ti & 7;
-  const int kt = 2 * kb + r, nt = band * s.band_tiles + col;
-  const bool valid = kt < s.tk && nt < s.tn && col < s.band_tiles;
+  const int t8 = i >> 4, G = i & 15;
+  const int r = t8 >> 2, colh = t8 & 3;
+  const int kt = 2 * kb + r, nt = band * s.band_tiles + 4 * half + colh;
+  const bool valid = kt < s.tk && nt < s.tn && 4 * half + colh < s.band_tiles;
   if (i < 16) cnt[i] = 0;
   __syncthreads();
+  const uint2 p0 = half_row_range(s, band, half, 2 * kb);
+  const uint2 p1 = half_row_range(s, band, half, 2 * kb + 1);
   const float pow2e = ldexpf(1.0f, s.exp2);
   const int sw = s.scale_words;
   uint32_t v = 0, e0 = 0;
@@ -342,11 +359,11 @@ __global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int
   int cls[4] = {-1, -1, -1, -1};  // slot < 8: group class; slot 8 + c: micro-block class c
   if (valid) {
     const uint32_t* ltab = reinterpret_cast<const uint32_t*>(s.records + d.record_off);
-    const uint32_t stage_base = s.row_off[(size_t)band * (s.tk + 1) + 2 * kb];
-    const uint32_t rec = d.record_off - stage_base;
+    // position of this tile's record in the sub-stage payload (row-0 part, then row-1 part)
+    const uint32_t rec = r == 0 ? d.record_off - p0.x : d.record_off - p1.x + p0.y;
     uint32_t prim = rec + pad16(4 * sw * d.n_leaves) + (ex & 0xffffu);
     uint32_t sec = rec + pad16(4 * sw * d.n_leaves) + pad16(d.prim_bytes) + (ex >> 16);
-    const uint64_t where = ((uint64_t)ti << 52) | ((uint64_t)G << 56);
+    const uint64_t where = ((uint64_t)t8 << 52) | ((uint64_t)G << 56);
     if (single) {
       const int m = lt_mode(e0);
       bool exact;
@@ -385,34 +402,36 @@ __global__ void __launch_bounds__(256) stage_lists_kernel(mtc_stream_desc s, int
     uint32_t ng = 0;
     for (int c = 0; c < 8; ++c) ng += cnt[c];
     if (!FILL) {
-      counts[stage] = ng | ((acc - ng) << 16);
-      totals[stage] = acc;
+      counts[q] = ng | ((acc - ng) << 16);
+      totals[q] = acc;
+      ranges[4 * (size_t)q + 0] = p0.x;
+      ranges[4 * (size_t)q + 1] = p0.y;
+      ranges[4 * (size_t)q + 2] = p1.x;
+      ranges[4 * (size_t)q + 3] = p1.y;
     }
   }
   __syncthreads();
   if (FILL) {
     for (int k = 0; k < 4; ++k)
-      if (cls[k] >= 0) lists[(size_t)offs[stage] + base[cls[k]] + rank[k]] = entry[k];
+      if (cls[k] >= 0) lists[(size_t)offs[q] + base[cls[k]] + rank[k]] = entry[k];
   }
 }
 
-// Exclusive scan of the per-stage entry totals into CSR offsets (single CTA),
-// plus the largest staged footprint: descriptors + list + records of a stage.
-__global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __restrict__ totals, int n_stages,
-                                                          mtc_stream_desc s, int nkb, uint32_t* __restrict__ offs,
-                                                          uint32_t* __restrict__ out) {
+// Exclusive scan of the per-sub-stage entry totals into CSR offsets (single
+// CTA), plus the largest staged footprint: descriptors + list + records.
+__global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __restrict__ totals, int n_sub,
+                                                          const uint32_t* __restrict__ ranges,
+                                                          uint32_t* __restrict__ offs, uint32_t* __restrict__ out) {
   __shared__ uint32_t part[1024];
   __shared__ uint32_t red[1024];
-  const int per = (n_stages + blockDim.x - 1) / blockDim.x;
-  const int lo = min(n_stages, (int)threadIdx.x * per), hi = min(n_stages, lo + per);
+  const int per = (n_sub + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n_sub, (int)threadIdx.x * per), hi = min(n_sub, lo + per);
   uint32_t sum = 0, mx = 0;
-  // each stage's list starts at an even entry (16-byte aligned for the bulk copy)
+  // each list starts at an even entry (16-byte aligned for the bulk copy)
   for (int i = lo; i < hi; ++i) {
     sum += (totals[i] + 1u) & ~1u;
-    const int band = i / nkb, kb = i % nkb;
-    const uint32_t* ro = s.row_off + (size_t)band * (s.tk + 1);
-    const uint32_t bytes = ro[min(2 * kb + 2, s.tk)] - ro[2 * kb];
-    mx = max(mx, 256u + ((8u * totals[i] + 15u) & ~15u) + bytes);
+    const uint32_t bytes = ranges[4 * (size_t)i + 1] + ranges[4 * (size_t)i + 3];
+    mx = max(mx, 128u + ((8u * totals[i] + 15u) & ~15u) + bytes);
   }
   part[threadIdx.x] = sum;
   red[threadIdx.x] = mx;
@@ -433,7 +452,7 @@ __global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __rest
     __syncthreads();
   }
   if (threadIdx.x == blockDim.x - 1) {
-    offs[n_stages] = part[blockDim.x - 1];
+    offs[n_sub] = part[blockDim.x - 1];
     out[0] = part[blockDim.x - 1];
   }
   if (threadIdx.x == 0) out[1] = red[0];
@@ -445,22 +464,22 @@ __global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __rest
 using namespace mtc;
 
 extern "C" int mtc_repack_stage_plan(const mtc_stream_desc* s, uint32_t* counts, uint32_t* offsets,
-                                     uint32_t* scratch_u32, uint64_t* out_host, void* stream) {
+                                     uint32_t* ranges, uint32_t* scratch_u32, uint64_t* out_host, void* stream) {
   clear_error();
-  MTC_REQUIRE(s && counts && offsets && scratch_u32 && out_host && s->tiles && s->row_off && s->records,
+  MTC_REQUIRE(s && counts && offsets && ranges && scratch_u32 && out_host && s->tiles && s->row_off && s->records,
               "mtc_repack_stage_plan: null pointer");
   MTC_REQUIRE(s->band_tiles == 8, "mtc_repack_stage_plan: band width %d (needs 8)", s->band_tiles);
   MTC_REQUIRE(2ull * s->max_row_bytes < 65536ull, "mtc_repack_stage_plan: stage of %u bytes exceeds 16-bit offsets",
               2 * s->max_row_bytes);
   const int nkb = (s->tk + 1) / 2;
   const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
-  const int n_stages = nb * nkb;
+  const int n_sub = 2 * nb * nkb;
   cudaStream_t st = as_stream(stream);
   uint32_t* totals = scratch_u32;
-  uint32_t* out = scratch_u32 + n_stages;
-  stage_lists_kernel<false><<<n_stages, 256, 0, st>>>(*s, nkb, nullptr, counts, totals, nullptr);
+  uint32_t* out = scratch_u32 + n_sub;
+  stage_lists_kernel<false><<<n_sub, 128, 0, st>>>(*s, nkb, nullptr, counts, totals, ranges, nullptr);
   MTC_CHECK_LAUNCH("mtc_repack_stage_plan: count");
-  stage_scan_kernel<<<1, 1024, 0, st>>>(totals, n_stages, *s, nkb, offsets, out);
+  stage_scan_kernel<<<1, 1024, 0, st>>>(totals, n_sub, ranges, offsets, out);
   MTC_CHECK_LAUNCH("mtc_repack_stage_plan: scan");
   uint32_t back[2];
   MTC_CHECK_CUDA(cudaMemcpyAsync(back, out, 8, cudaMemcpyDeviceToHost, st), "mtc_repack_stage_plan: copy back");
@@ -476,7 +495,8 @@ extern "C" int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* o
   MTC_REQUIRE(s && offsets && lists && s->tiles && s->row_off && s->records, "mtc_repack_stage_fill: null pointer");
   const int nkb = (s->tk + 1) / 2;
   const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
-  stage_lists_kernel<true><<<nb * nkb, 256, 0, as_stream(stream)>>>(*s, nkb, offsets, nullptr, nullptr, lists);
+  stage_lists_kernel<true><<<2 * nb * nkb, 128, 0, as_stream(stream)>>>(*s, nkb, offsets, nullptr, nullptr, nullptr,
+                                                                        lists);
   MTC_CHECK_LAUNCH("mtc_repack_stage_fill");
   return MTC_OK;
 }

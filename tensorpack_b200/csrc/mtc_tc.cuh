@@ -106,9 +106,13 @@ __device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
                : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
   return r;
 }
-// Arrive (release, cluster scope) on an mbarrier given by shared::cluster address.
+// Arrive on the other CTA's mbarrier (shared::cluster address) with the
+// default (CTA-scope release) semantics.  Enough for what it publishes: the
+// shared-memory tiles a pair MMA reads are read by this CTA's own SM (after a
+// fence.proxy.async here), and TMEM reads are ordered by tcgen05 fences; a
+// cluster-scope release would add a fence of about a microsecond per call.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 // 2-D TMA tile load into this CTA's shared memory whose completion bytes go
 // to the mbarrier at `bar_cluster` (the even CTA's barrier).
@@ -118,6 +122,21 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "[%4];" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
       : "memory");
+}
+// The same with an L2 cache policy (createpolicy) for the loaded lines.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map, int x, int y,
+                                                      uint32_t bar_cluster, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%2, %3}], [%4], %5;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+// L2 policy keeping lines resident (evict_last) for data read many times.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ void mma_f16_ss_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                 uint32_t accumulate) {

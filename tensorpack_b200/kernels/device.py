@@ -73,13 +73,16 @@ class DeviceStream:
             _lib.check(lib.mtc_repack_fill(d_arena.data_ptr(), arena.nbytes, d_leaves.data_ptr(),
                                            d_begin.data_ptr(), ctypes.byref(self.desc), self.records.data_ptr(),
                                            scratch.data_ptr(), st), "repack fill")
-            # class-sorted work lists of every prefill stage (CSR: counts, offsets, entries)
-            n_stages = self.n_bands * ((tk + 1) // 2)
-            self.stage_counts = torch.empty(n_stages, dtype=torch.int32, device=dev)
-            self.stage_offsets = torch.empty(n_stages + 1, dtype=torch.int32, device=dev)
-            st_scratch = torch.empty(n_stages + 2, dtype=torch.int32, device=dev)
+            # class-sorted work lists of every prefill sub-stage (half a band, two
+            # k-tile rows): CSR counts, offsets, entries, plus record ranges
+            n_sub = 2 * self.n_bands * ((tk + 1) // 2)
+            self.stage_counts = torch.empty(n_sub, dtype=torch.int32, device=dev)
+            self.stage_offsets = torch.empty(n_sub + 1, dtype=torch.int32, device=dev)
+            self.stage_ranges = torch.empty(4 * n_sub, dtype=torch.int32, device=dev)
+            st_scratch = torch.empty(n_sub + 2, dtype=torch.int32, device=dev)
             _lib.check(lib.mtc_repack_stage_plan(ctypes.byref(self.desc), self.stage_counts.data_ptr(),
-                                                 self.stage_offsets.data_ptr(), st_scratch.data_ptr(), out, st),
+                                                 self.stage_offsets.data_ptr(), self.stage_ranges.data_ptr(),
+                                                 st_scratch.data_ptr(), out, st),
                        "repack stage plan")
             self.stage_lists = torch.zeros(max(int(out[0]), 2), dtype=torch.int64, device=dev)
             self.max_stage_bytes = int(out[1])
@@ -88,6 +91,7 @@ class DeviceStream:
             self.desc.stage_lists = self.stage_lists.data_ptr()
             self.desc.stage_counts = self.stage_counts.data_ptr()
             self.desc.stage_offsets = self.stage_offsets.data_ptr()
+            self.desc.stage_ranges = self.stage_ranges.data_ptr()
             self.desc.max_stage_bytes = self.max_stage_bytes
             self.row_perm = None if mat.row_perm is None else torch.from_numpy(
                 np.asarray(mat.row_perm, dtype=np.int32)).to(dev)

@@ -40,7 +40,7 @@ def test_abi_version_and_error_text(lib):
 
 
 def test_struct_sizes_match_header():
-    assert ctypes.sizeof(_lib.StreamDesc) == 96
+    assert ctypes.sizeof(_lib.StreamDesc) == 104
     from tensorpack_b200.core.layout import LEAF_IN_DTYPE
     assert LEAF_IN_DTYPE.itemsize == 12
 
