@@ -191,6 +191,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--decode-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
+                    help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -260,34 +262,47 @@ def main():
         return float(t.item())
 
     # --- prefill (headline) ---
-    for _ in range(args.warmup):
+    do_prefill = args.only in ("all", "prefill")
+    for _ in range(args.warmup if do_prefill else 0):
         gemm(X, Y)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    barrier()
-    with ClockSampler(local_rank) as clocks:
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+    flops = 2.0 * M_PREFILL * K_IN * N_OUT
+    step_ms = kern_ms = value = achieved = None
+    clocks = None
+    if do_prefill:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        barrier()
+        with ClockSampler(local_rank) as clocks:
+            for i in range(args.steps):
+                flush.zero_()
+                ev[i][0].record(stream)
+                gemm(X, Y)
+                ev[i][1].record(stream)
+            barrier()
+        step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps)
+        flops = 2.0 * M_PREFILL * K_IN * N_OUT
+        value = flops / (step_ms * 1e-3) / 1e12
+        ds.check_status()
+        # prefill kernel alone (its own stream), for the roofline
         for i in range(args.steps):
             flush.zero_()
-            ev[i][0].record(stream)
-            gemm(X, Y)
-            ev[i][1].record(stream)
+            ds.prefill_gather(X)
+            kev[i][0].record(stream)
+            ds.prefill_gemm(M_PREFILL, Y)
+            kev[i][1].record(stream)
         barrier()
-    step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps)
-    flops = 2.0 * M_PREFILL * K_IN * N_OUT
-    value = flops / (step_ms * 1e-3) / 1e12
-    ds.check_status()
-    # prefill kernel alone (its own stream), for the roofline
-    for i in range(args.steps):
-        flush.zero_()
-        ds.prefill_gather(X)
-        kev[i][0].record(stream)
-        ds.prefill_gemm(M_PREFILL, Y)
-        kev[i][1].record(stream)
-    barrier()
-    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps)
-    local_flops = 2.0 * M_PREFILL * K_IN * ds.N
-    hbm_peak, tc_peak, peak_src = measured_peaks()
-    achieved = local_flops / (kern_ms * 1e-3) / 1e12
+        kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps)
+        local_flops = 2.0 * M_PREFILL * K_IN * ds.N
+        achieved = local_flops / (kern_ms * 1e-3) / 1e12
+        if args.only == "prefill":
+            if rank == 0:
+                print(json.dumps({"only": "prefill", "ms_per_step": step_ms, "kernel_ms": kern_ms,
+                                  "kernel_tflops": achieved, "config": workload_config(args)}), flush=True)
+            if world > 1:
+                barrier()
+                dist.destroy_process_group()
+            return
     launches_per_step = 3
 
     # --- decode M = 1 over rotating copies of the stream (> 4x L2) ---
@@ -327,6 +342,14 @@ def main():
     ds.check_status()
     dec_gbs = accounted_bytes / (dec_us * 1e-6) / 1e9          # whole layer bytes / slowest rank time
     dec_local_gbs = local_bytes / (dec_us * 1e-6) / 1e9
+    if args.only == "decode":
+        if rank == 0:
+            print(json.dumps({"only": "decode", "us_per_call": dec_us, "GB/s": dec_gbs,
+                              "config": workload_config(args)}), flush=True)
+        if world > 1:
+            barrier()
+            dist.destroy_process_group()
+        return
 
     # --- end to end through the public API with pinned host buffers ---
     Xh = torch.from_numpy(X_host).pin_memory()
