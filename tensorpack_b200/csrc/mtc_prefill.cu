@@ -599,14 +599,172 @@ __global__ void __launch_bounds__(512) permute_rows_kernel(const float* __restri
   for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = row[pos[j]];
 }
 
+// Persistent row kernels for the HBM-bound gather / scatter around the GEMM:
+// each CTA takes rows blockIdx.x, + gridDim.x, ...; a row arrives by bulk
+// copy into one of two shared-memory buffers while the previous row is
+// written out, and every thread keeps the source index of its output
+// elements in registers (the permutation is the same for every row).
+constexpr int kRowThreads = 512;
+constexpr int kRowNJ = 32;  // most output elements (permute) or pairs (gather) per thread per row
+
+__device__ __forceinline__ bool row_wait_all(uint64_t* bar, uint32_t parity) {
+  const bool ok = mbar_wait(bar, parity, 2000000000ull);
+  return __syncthreads_and(ok) != 0;
+}
+
+template <int NJ>
+__global__ void __launch_bounds__(kRowThreads)
+    permute_rows_bulk_kernel(const float* __restrict__ src, long long seg_stride, long long ldp, int nseg,
+                             int seg_len, const int32_t* __restrict__ pos, int N, int M, float* __restrict__ Y,
+                             long long ldy, int buf_floats, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* buf = reinterpret_cast<float*>(smem_raw);  // [2][buf_floats]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + 2 * buf_floats);
+  const int tid = threadIdx.x;
+  int pj[NJ];
+#pragma unroll
+  for (int i = 0; i < NJ; ++i) {
+    const int j = tid + i * kRowThreads;
+    pj[i] = j < N ? pos[j] : 0;
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t row_bytes = (uint32_t)nseg * (uint32_t)seg_len * 4u;
+  auto issue = [&](int m, int b) {
+    mbar_expect_tx(&bars[b], row_bytes);
+    for (int g = 0; g < nseg; ++g)
+      bulk_g2s(buf + b * buf_floats + g * seg_len, src + g * seg_stride + (long long)m * ldp, (uint32_t)seg_len * 4u,
+               &bars[b]);
+  };
+  if (tid == 0 && (int)blockIdx.x < M) issue(blockIdx.x, 0);
+  uint32_t r = 0;
+  int issued = (int)blockIdx.x < M ? 1 : 0;
+  for (int m = blockIdx.x; m < M; m += gridDim.x, ++r) {
+    const int b = r & 1;
+    if (m + (int)gridDim.x < M) {
+      if (tid == 0) issue(m + gridDim.x, b ^ 1);  // buffer b ^ 1 was released by the last __syncthreads
+      ++issued;
+    }
+    if (!row_wait_all(&bars[b], (r >> 1) & 1)) {
+      if (tid == 0) {
+        flag(status, MTC_STATUS_TIMEOUT);
+        // let copies still in flight land before the CTA exits
+        for (uint32_t q = r; q < (uint32_t)issued; ++q) (void)mbar_wait(&bars[q & 1], (q >> 1) & 1, 10000000ull);
+      }
+      return;
+    }
+    const float* row = buf + b * buf_floats;
+    float* dst = Y + (long long)m * ldy;
+#pragma unroll
+    for (int i = 0; i < NJ; ++i) {
+      const int j = tid + i * kRowThreads;
+      if (j < N) dst[j] = row[pj[i]];
+    }
+    __syncthreads();
+  }
+}
+
+// Xp[m][k] = fp16(X[m][pr[k]]) for k < K, zero up to Kp; pairs of k per thread.
+template <int NJ>
+__global__ void __launch_bounds__(kRowThreads)
+    gather_x_bulk_kernel(const float* __restrict__ X, long long ldx, int K, int Kp, const int32_t* __restrict__ pr,
+                         int M, __half* __restrict__ Xp, int buf_floats, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* buf = reinterpret_cast<float*>(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + 2 * buf_floats);
+  const int tid = threadIdx.x;
+  int p0[NJ], p1[NJ];
+#pragma unroll
+  for (int i = 0; i < NJ; ++i) {
+    const int k = 2 * (tid + i * kRowThreads);
+    p0[i] = k < K ? (pr ? pr[k] : k) : -1;
+    p1[i] = k + 1 < K ? (pr ? pr[k + 1] : k + 1) : -1;
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int m, int b) {
+    mbar_expect_tx(&bars[b], (uint32_t)K * 4u);
+    bulk_g2s(buf + b * buf_floats, X + (long long)m * ldx, (uint32_t)K * 4u, &bars[b]);
+  };
+  if (tid == 0 && (int)blockIdx.x < M) issue(blockIdx.x, 0);
+  uint32_t r = 0, bad = 0;
+  int issued = (int)blockIdx.x < M ? 1 : 0;
+  for (int m = blockIdx.x; m < M; m += gridDim.x, ++r) {
+    const int b = r & 1;
+    if (m + (int)gridDim.x < M) {
+      if (tid == 0) issue(m + gridDim.x, b ^ 1);
+      ++issued;
+    }
+    if (!row_wait_all(&bars[b], (r >> 1) & 1)) {
+      if (tid == 0) {
+        flag(status, MTC_STATUS_TIMEOUT);
+        for (uint32_t q = r; q < (uint32_t)issued; ++q) (void)mbar_wait(&bars[q & 1], (q >> 1) & 1, 10000000ull);
+      }
+      return;
+    }
+    const float* row = buf + b * buf_floats;
+    __half* out = Xp + (long long)m * Kp;
+#pragma unroll
+    for (int i = 0; i < NJ; ++i) {
+      const int k = 2 * (tid + i * kRowThreads);
+      if (k < Kp) {
+        const float a = p0[i] >= 0 ? row[p0[i]] : 0.f;
+        const float c = p1[i] >= 0 ? row[p1[i]] : 0.f;
+        if (!(fabsf(a) <= 65504.0f) || !(fabsf(c) <= 65504.0f)) bad = 1;
+        *reinterpret_cast<__half2*>(out + k) = __floats2half2_rn(a, c);
+      }
+    }
+    __syncthreads();
+  }
+  if (bad) flag(status, MTC_STATUS_X_RANGE);
+}
+
+int row_grid(const void* kernel, size_t smem, int M) {
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kRowThreads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const long long g = (long long)sms * per_sm;
+  return (int)(M < g ? M : g);
+}
+
 int launch_permute_rows(const float* src, long long seg_stride, long long ldp, int nseg, int seg_len,
-                        const int32_t* pos, int N, int M, float* Y, long long ldy, cudaStream_t st) {
-  const size_t sm = (size_t)nseg * seg_len * 4;
-  MTC_REQUIRE(sm <= 227 * 1024, "permute: a staged row of %zu bytes exceeds shared memory", sm);
-  if (sm > 48 * 1024)
-    MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                        const int32_t* pos, int N, int M, float* Y, long long ldy, uint32_t* status,
+                        cudaStream_t st) {
+  const size_t row = (size_t)nseg * seg_len * 4;
+  const size_t buf_floats = ((size_t)nseg * seg_len + 31) & ~(size_t)31;
+  const size_t sm2 = 2 * buf_floats * 4 + 64;
+  const bool bulk = N <= kRowThreads * kRowNJ && sm2 <= 227 * 1024 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                    (seg_stride & 3) == 0 && (ldp & 3) == 0 && (seg_len & 3) == 0;
+  if (bulk) {
+    auto go = [&](auto kernel) -> int {
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2),
+                     "permute: smem attribute");
+      const int grid = row_grid(reinterpret_cast<const void*>(kernel), sm2, M);
+      kernel<<<grid, kRowThreads, sm2, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, (int)buf_floats,
+                                             status);
+      MTC_CHECK_LAUNCH("permute_rows");
+      return MTC_OK;
+    };
+    if (N <= kRowThreads * 4) return go(permute_rows_bulk_kernel<4>);
+    if (N <= kRowThreads * 8) return go(permute_rows_bulk_kernel<8>);
+    if (N <= kRowThreads * 16) return go(permute_rows_bulk_kernel<16>);
+    return go(permute_rows_bulk_kernel<32>);
+  }
+  MTC_REQUIRE(row <= 227 * 1024, "permute: a staged row of %zu bytes exceeds shared memory", row);
+  if (row > 48 * 1024)
+    MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row),
                    "permute: smem attribute");
-  permute_rows_kernel<<<M, 512, sm, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, Y, ldy);
+  permute_rows_kernel<<<M, 512, row, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, Y, ldy);
   MTC_CHECK_LAUNCH("permute_rows");
   return MTC_OK;
 }
@@ -720,6 +878,24 @@ extern "C" int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int3
   if (rc != MTC_OK) return rc;
   MTC_REQUIRE(X && ldx >= s->K, "mtc_prefill_gather: bad activations");
   MTC_REQUIRE((size_t)s->K * 4 <= 200 * 1024, "mtc_prefill_gather: K=%d above the 51200 row-staged limit", s->K);
+  const size_t buf_floats = ((size_t)s->K + 31) & ~(size_t)31;
+  const size_t sm2 = 2 * buf_floats * 4 + 64;
+  if (pl.Kp <= 2 * kRowThreads * kRowNJ && sm2 <= 227 * 1024 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 &&
+      (ldx & 3) == 0 && (s->K & 3) == 0) {
+    auto go = [&](auto kernel) -> int {
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2),
+                     "mtc_prefill_gather: smem attribute");
+      const int grid = row_grid(reinterpret_cast<const void*>(kernel), sm2, M);
+      kernel<<<grid, kRowThreads, sm2, as_stream(stream)>>>(X, ldx, s->K, pl.Kp, row_perm, M, static_cast<__half*>(ws),
+                                                            (int)buf_floats, status);
+      MTC_CHECK_LAUNCH("mtc_prefill_gather");
+      return MTC_OK;
+    };
+    if (pl.Kp <= 2 * kRowThreads * 4) return go(gather_x_bulk_kernel<4>);
+    if (pl.Kp <= 2 * kRowThreads * 8) return go(gather_x_bulk_kernel<8>);
+    if (pl.Kp <= 2 * kRowThreads * 16) return go(gather_x_bulk_kernel<16>);
+    return go(gather_x_bulk_kernel<32>);
+  }
   const size_t sm = (size_t)s->K * 4;
   if (sm > 48 * 1024)
     MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
@@ -738,7 +914,7 @@ extern "C" int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const in
   if (rc != MTC_OK) return rc;
   MTC_REQUIRE(Y && col_perm_inv && ldy >= s->N, "mtc_prefill_scatter: bad output");
   const float* Yp = reinterpret_cast<const float*>(static_cast<const uint8_t*>(ws) + pl.xp_bytes);
-  return launch_permute_rows(Yp, 0, pl.Np, 1, s->N, col_perm_inv, s->N, M, Y, ldy, as_stream(stream));
+  return launch_permute_rows(Yp, 0, pl.Np, 1, s->N, col_perm_inv, s->N, M, Y, ldy, nullptr, as_stream(stream));
 }
 
 extern "C" int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ldp, int32_t nseg, int32_t seg_len,
@@ -746,7 +922,7 @@ extern "C" int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ld
   clear_error();
   MTC_REQUIRE(src && pos && Y && nseg >= 1 && seg_len >= 1 && N >= 1 && M >= 1 && ldy >= N,
               "mtc_permute_rows: bad arguments");
-  return launch_permute_rows(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, as_stream(stream));
+  return launch_permute_rows(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, nullptr, as_stream(stream));
 }
 
 extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
