@@ -32,12 +32,6 @@
 
 #include "../../include/mtc_b200.h"
 
-// Decoder used when the lanes of a warp hold groups of different modes:
-// 1 = one table-driven instruction sequence for all modes, 0 = per-mode
-// specialised code (lanes of other modes idle while each path runs).
-#ifndef MTC_MIXED_TABLE_DECODE
-#define MTC_MIXED_TABLE_DECODE 0
-#endif
 
 namespace mtc {
 
@@ -394,6 +388,11 @@ __host__ __device__ constexpr DecRow make_dec_row(int mode) {
   return r;
 }
 
+// decode class of a mode: 0 = P0, 1..6 = P2, P3, P4, P5, P6, P8, 7 = P16
+__device__ __forceinline__ int dec_class_of(int m) {
+  return m > 8 ? 7 : (int)((0x675432170ull >> (4 * m)) & 15ull);
+}
+
 // mode -> row of the parameter table (2,3,4,5,6,8 -> 0..5)
 __device__ __forceinline__ int dec_row_index(int mode) { return (0x5F43210u >> (4 * (mode - 2))) & 15u; }
 
@@ -555,40 +554,52 @@ __device__ __forceinline__ void decode_group_w16(const uint8_t* rec, uint16_t n_
         return;
     }
   }
-#if MTC_MIXED_TABLE_DECODE == 0
-  if (fast) {
-    const uint32_t s2 = half2_bits(lt_scale_of(ltab, l0, sw) * pow2e);
-    switch (mode0) {
-      case 2: decode_run4<2>(prim, sec, c.h, s2, R); return;
-      case 3: decode_run4<3>(prim, sec, c.h, s2, R); return;
-      case 4: decode_run4<4>(prim, sec, c.h, s2, R); return;
-      case 5: decode_run4<5>(prim, sec, c.h, s2, R); return;
-      case 6: decode_run4<6>(prim, sec, c.h, s2, R); return;
-      case 8: decode_run4<8>(prim, sec, c.h, s2, R); return;
-      default:
-#pragma unroll
-        for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
-        return;
-    }
-  }
-#endif
-  // mixed modes across the warp: one table-driven sequence for P2..P8,
-  // branches only for P0 / P16 / inexact-scale micro-blocks
+  // Modes differ across the warp: every micro-block of P0..P8 with an fp16-exact
+  // scale goes through the branch-free table decoder (all lanes run the same
+  // instructions, and the four decodes interleave); the rest (P16, flagged
+  // slow, inexact scale) decode as zeros there and are redone per lane below.
   uint32_t po = 0, so = 0;
+  bool generic = false;
+  uint32_t ent[4];
+  float scl[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int L = single ? l0 : l0 + k;
-    const uint32_t e = lt_entry(ltab, L, sw);
-    const int m = lt_mode(e);
-    const float scl = lt_scale_of(ltab, L, sw);
-    if (MTC_MIXED_TABLE_DECODE && m >= 2 && m != 16 && !lt_slow(e)) {
-      decode_half_uniform(dtab + 20 * dec_row_index(m), m, prim + po, sec + so, c.h, half2_bits(scl * pow2e),
-                          R[k]);
-    } else {
-      decode_half_w16(e, scl, prim + po, sec + so, c.h, pow2e, R[k]);
+    ent[k] = lt_entry(ltab, L, sw);
+    scl[k] = lt_scale_of(ltab, L, sw);
+    const int m = lt_mode(ent[k]);
+    const float sv = scl[k] * pow2e;
+    const __half hs = __float2half_rn(sv);
+    const bool exact = __half2float(hs) == sv;
+    int cls = dec_class_of(m);
+    if (m != 0 && (lt_slow(ent[k]) || !exact)) cls = 7;
+    if (cls == 7) generic = true;
+    decode_half_class(dtab, cls == 7 ? 0 : cls, prim + po, sec + so, c.h,
+                      h2const(*reinterpret_cast<const uint16_t*>(&hs)), R[k]);
+    po += lt_prim(ent[k]);
+    so += lt_sec(ent[k]);
+  }
+  if (__any_sync(0xffffffffu, generic)) {
+    po = 0;
+    so = 0;
+#pragma unroll 1
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t e = k == 0 ? ent[0] : k == 1 ? ent[1] : k == 2 ? ent[2] : ent[3];
+      const float sk = k == 0 ? scl[0] : k == 1 ? scl[1] : k == 2 ? scl[2] : scl[3];
+      const int m = lt_mode(e);
+      const float sv = sk * pow2e;
+      const bool exact = __half2float(__float2half_rn(sv)) == sv;
+      if (m == 16 || (m != 0 && (lt_slow(e) || !exact))) {
+        uint32_t r[4];
+        decode_half_w16(e, sk, prim + po, sec + so, c.h, pow2e, r);
+        if (k == 0) { R[0][0] = r[0]; R[0][1] = r[1]; R[0][2] = r[2]; R[0][3] = r[3]; }
+        if (k == 1) { R[1][0] = r[0]; R[1][1] = r[1]; R[1][2] = r[2]; R[1][3] = r[3]; }
+        if (k == 2) { R[2][0] = r[0]; R[2][1] = r[1]; R[2][2] = r[2]; R[2][3] = r[3]; }
+        if (k == 3) { R[3][0] = r[0]; R[3][1] = r[1]; R[3][2] = r[2]; R[3][3] = r[3]; }
+      }
+      po += lt_prim(e);
+      so += lt_sec(e);
     }
-    po += lt_prim(e);
-    so += lt_sec(e);
   }
 }
 
