@@ -12,7 +12,7 @@ tensorpack_b200.quant.
   value     prefill: Y = X @ W at M = 4096 through the fused dequant +
             tcgen05 path (gather, GEMM, column scatter), TFLOP/s = 2 M K N / t,
             L2 flushed before every step (256 MB write)
-  decode    M = 1 through the split-K decode kernel, GB/s of accounted packed
+  decode    M = 1 through the tensor-core decode kernel, GB/s of accounted packed
             bytes (payload + scales + modes + split flags + permutation
             indices), rotating over copies of the stream totalling > 4x L2
   e2e       the prefill metric through the public API (mtc_gemm) with pinned
@@ -306,28 +306,33 @@ def main():
     launches_per_step = 3
 
     # --- decode M = 1 over rotating copies of the stream (> 4x L2) ---
-    copies = max(2, int(4 * L2_BYTES // max(ds.record_bytes, 1)) + 1)
+    # Every buffer the decode kernel streams is copied: tile records and
+    # descriptors, row offsets and the sub-stage work lists.
+    stream_bytes = ds.record_bytes + ds.stage_lists.numel() * 8
+    copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
     descs, keep = [], []
     for _ in range(copies):
-        r, t, ro = ds.records.clone(), ds.tiles.clone(), ds.row_off.clone()
-        keep += [r, t, ro]
+        bufs = [ds.records.clone(), ds.tiles.clone(), ds.row_off.clone(), ds.stage_lists.clone(),
+                ds.stage_counts.clone(), ds.stage_offsets.clone(), ds.stage_ranges.clone()]
+        keep += bufs
         d = _lib.StreamDesc.from_buffer_copy(ds.desc)
-        d.records, d.tiles, d.row_off = r.data_ptr(), t.data_ptr(), ro.data_ptr()
+        (d.records, d.tiles, d.row_off, d.stage_lists, d.stage_counts, d.stage_offsets,
+         d.stage_ranges) = [b.data_ptr() for b in bufs]
         descs.append(d)
     lib = _lib.load()
     import ctypes
 
     x1 = X[:1].contiguous()
     y1 = torch.empty(1, ds.N, dtype=torch.float32, device=dev)
-    ws = ds._workspace(1, 0)
-    counters = [torch.zeros(ds.n_bands, dtype=torch.int32, device=dev) for _ in range(copies)]
+    ws = torch.empty(max(int(lib.mtc_decode_workspace_bytes(ctypes.byref(ds.desc), 1)), 256), dtype=torch.uint8,
+                     device=dev)
 
     def decode(i):
-        _lib.check(lib.mtc_gemv(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0),
-                                None if ds.row_perm is None else ds.row_perm.data_ptr(),
-                                None if ds.col_perm is None else ds.col_perm.data_ptr(), y1.data_ptr(),
-                                y1.stride(0), 0, ws.data_ptr(), ws.numel() * 4, counters[i % copies].data_ptr(),
-                                ds.status.data_ptr(), stream.cuda_stream), "decode")
+        _lib.check(lib.mtc_decode(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0),
+                                  None if ds.row_perm is None else ds.row_perm.data_ptr(),
+                                  None if ds.col_perm is None else ds.col_perm.data_ptr(), y1.data_ptr(),
+                                  y1.stride(0), ws.data_ptr(), ws.numel(), ds.decode_counters.data_ptr(),
+                                  ds.status.data_ptr(), stream.cuda_stream), "decode")
 
     for i in range(max(args.warmup, copies)):
         decode(i)
@@ -397,7 +402,7 @@ def main():
             "decode": {"value": dec_gbs, "unit": "GB/s", "us_per_call": dec_us, "M": 1,
                        "accounted_bytes": accounted_bytes, "device_bytes": ds.device_bytes,
                        "roofline": {"bound": "hbm", "achieved": dec_local_gbs, "peak": hbm_peak, "unit": "GB/s",
-                                    "frac": dec_local_gbs / hbm_peak, "traffic": committed_traffic("gemv_kernel"),
+                                    "frac": dec_local_gbs / hbm_peak, "traffic": committed_traffic("decode_kernel"),
                                     "peak_source": peak_src},
                        "copies_rotated": copies},
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",

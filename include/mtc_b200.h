@@ -207,6 +207,20 @@ MTC_API int mtc_gemv_static(const mtc_stream_desc* s, const float* X, int32_t M,
                             const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
                             uint32_t* status, void* stream);
 
+/* Tensor-core decode GEMM for M <= 16: Y[:, col_perm] = X[:, row_perm] @ Wp
+ * (replaces mtc_gemm, gemm.py:541-574, and the gather/GEMM/scatter of
+ * permutation.py:15-21).  Same product as mtc_gemv, computed swap-AB with
+ * tcgen05 (D = 128 features x 16 tokens in TMEM) from the prefill's
+ * class-sorted work lists (needs mtc_repack_stage_plan / _fill).  `ws`
+ * (256-byte aligned, size from mtc_decode_workspace_bytes) holds the fp16
+ * gathered activations and the split-K partial sums; `counters` points at
+ * 2 * n_bands u32 that are zero before the first call and are left zero by
+ * every successful call.  `status` (nullable) receives MTC_STATUS_* bits. */
+MTC_API size_t mtc_decode_workspace_bytes(const mtc_stream_desc* s, int32_t M);
+MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
+                       const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy, void* ws,
+                       size_t ws_bytes, uint32_t* counters, uint32_t* status, void* stream);
+
 /* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
  * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,
  * gemm.py:541-574, and permutation.py:15-21).  Takes the INVERSE column

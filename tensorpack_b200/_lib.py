@@ -63,6 +63,9 @@ SIGNATURES = {
     "mtc_gemv": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_i32,
                          c_p, c_size, c_p, c_p, c_p]),
     "mtc_gemv_static": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_p]),
+    "mtc_decode_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32]),
+    "mtc_decode": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_size, c_p,
+                           c_p, c_p]),
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemm_prefill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64,
                                  c_p, c_size, c_p, c_p]),

@@ -1,0 +1,486 @@
+// Tensor-core decode GEMM for M <= 16 tokens: Y[:, pc] = X[:, pr] @ Wp.
+//
+// Replaces the reference's packed GEMM (mtc/kernels/gemm.py:124-210, 541-574)
+// and the MTC-QT-P gather / scatter (mtc/core/permutation.py:15-21) for
+// decode-sized M.  The packed weights are read from HBM once; the product is
+// computed swap-AB on the tensor cores: D (128 features x 16 tokens, fp32
+// in TMEM) += W^T tile (128 features x 64 k, dequantised into shared memory)
+// x X^T tile (16 tokens x 64 k, fp16, TMA).  The SMs' issue slots go to the
+// dequantisation alone.
+//
+//  * work unit = (half band: 4 tiles = 128 features, range of k stages of
+//    64); persistent CTAs, one per SM, take units u = blockIdx.x, + grid, ...
+//  * warp roles (as in the prefill kernel):
+//      warps 0-3  epilogue: TMEM -> partial sums of the unit -> workspace;
+//                 the last unit of a half band (atomic ticket) reduces the
+//                 partials in a fixed order and scatters Y[:, pc]
+//      warp  4    X producer: TMA of the Xp tile of each stage
+//      warp  5    TMEM allocator + single-thread tcgen05.mma issuer
+//      warp  6    packed producer: sub-stage descriptors, work list and
+//                 records into a shared-memory byte ring (cp.async.bulk)
+//      warps 7-22 dequant, two groups taking alternate stages
+//                 (dequant_substage, shared with the prefill)
+//  * two TMEM accumulators (32 columns each) alternate between units, so a
+//    unit's epilogue overlaps the next unit's MMAs.
+// Every mbarrier wait is bounded; a timeout sets MTC_STATUS_TIMEOUT.
+#include "mtc_common.cuh"
+#include "mtc_internal.h"
+#include "mtc_substage.cuh"
+#include "mtc_tc.cuh"
+
+namespace mtc {
+namespace {
+
+constexpr int kTok = 16;        // token columns of the MMA (N); M <= 16
+constexpr int BK = 64;          // K per stage (two k-tile rows)
+constexpr int kFeat = 128;      // features per unit (MMA M)
+constexpr int kEpiWarps = 4;
+constexpr int kXWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kPackWarp = 6;
+constexpr int kDeqWarp0 = 7;
+constexpr int kDeqWarps = kSubWarps;
+constexpr int kDeqGroups = 2;
+constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
+constexpr uint32_t kXBytes = kTok * BK * 2;     // 2 KB
+constexpr uint32_t kWBytes = kFeat * BK * 2;    // 16 KB
+constexpr int kMaxS = 8;
+constexpr int kRingSlots = 8;
+constexpr int kMetaChunk = 32;
+constexpr uint32_t kTmemCols = 64;              // two accumulators of 32 columns
+
+struct DecodeParams {
+  mtc_stream_desc s;
+  int M;
+  float* Y;
+  long long ldy;
+  const int32_t* pc;   // column permutation (Y[:, pc[n]] = Yp[:, n]) or null
+  float* part;         // [units][kTok][kFeat] partial sums
+  uint32_t* counters;  // [half bands] tickets, zero between calls
+  uint32_t* status;
+  int n_hb, nkb, n_kr, R, n_units;
+  int SX, SW;
+  uint32_t ring_bytes;
+  float pow2e, inv_pow2e;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
+  if (st) atomicOr(st, bits);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tmap_x, const DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sX = smem;                               // [SX][2 KB], 1024-byte aligned
+  uint8_t* sW = sX + ((p.SX * kXBytes + 1023u) & ~1023u);  // [SW][16 KB]
+  uint8_t* sP = sW + p.SW * kWBytes;                // packed byte ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
+  uint64_t* full_x = bars;
+  uint64_t* empty_x = full_x + kMaxS;
+  uint64_t* full_w = empty_x + kMaxS;
+  uint64_t* empty_w = full_w + kMaxS;
+  uint64_t* pfull = empty_w + kMaxS;
+  uint64_t* pempty = pfull + kRingSlots;
+  uint64_t* acc_full = pempty + kRingSlots;         // [2]
+  uint64_t* acc_empty = acc_full + 2;               // [2]
+  uint64_t* drain = acc_empty + 2;
+  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort, [1] last unit
+  uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
+  uint32_t* pmeta = tmem_slot + 4;                  // [kRingSlots][4]
+  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1024);
+  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1536);  // [2][kMetaChunk][2]
+
+  const mtc_stream_desc& s = p.s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.SX; ++i) {
+      mbar_init(&full_x[i], 1);
+      mbar_init(&empty_x[i], 1);
+    }
+    for (int i = 0; i < p.SW; ++i) {
+      mbar_init(&full_w[i], kDeqWarps);
+      mbar_init(&empty_w[i], 1);
+    }
+    for (int i = 0; i < kRingSlots; ++i) {
+      mbar_init(&pfull[i], 1);
+      mbar_init(&pempty[i], kDeqWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) load_dec_table(dtab, lane);
+  if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, kTmemCols);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // unit u -> half band hb = u / n_kr, stages [kb0, kb1)
+  auto unit_range = [&](int u, int& hb, int& kb0, int& kb1) {
+    hb = u / p.n_kr;
+    kb0 = (u % p.n_kr) * p.R;
+    kb1 = min(p.nkb, kb0 + p.R);
+  };
+
+  if (warp == kXWarp) {
+    // ---------------------------------------------------------------- X producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x) {
+        int hb, kb0, kb1;
+        unit_range(u, hb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int sx = it % p.SX;
+          if (it >= (uint32_t)p.SX && !mbar_wait(&empty_x[sx], ((it / p.SX) & 1) ^ 1, p.timeout_ns)) {
+            flags[0] = 1;
+            break;
+          }
+          if (flags[0]) break;
+          mbar_expect_tx(&full_x[sx], kXBytes);
+          tc::tma_load_2d(sX + sx * kXBytes, &tmap_x, kb * BK, 0, &full_x[sx]);
+        }
+      }
+      if (flags[0]) {
+        for (uint32_t j = it > (uint32_t)p.SX ? it - p.SX : 0u; j < it; ++j)
+          (void)mbar_wait(&full_x[j % p.SX], (j / p.SX) & 1, 10000000ull);
+        flag(p.status, MTC_STATUS_TIMEOUT);
+      }
+    }
+  } else if (warp == kPackWarp) {
+    // ---------------------------------------------------------------- packed producer
+    // Metadata of up to 32 consecutive sub-stages of a unit, loaded by the
+    // whole warp one chunk ahead of lane 0, which issues the bulk copies.
+    const int n_my_units = (int)blockIdx.x < p.n_units ? (p.n_units - 1 - (int)blockIdx.x) / gridDim.x + 1 : 0;
+    const int chunks_per_unit = (p.R + kMetaChunk - 1) / kMetaChunk;
+    const int n_chunks = n_my_units * chunks_per_unit;
+    uint4 nxt0, nxt1;
+    auto load_chunk = [&](int q) {
+      nxt0 = make_uint4(0u, 0u, 0u, 0u);
+      nxt1 = make_uint4(0u, 0u, 0u, 0u);
+      if (q >= n_chunks) return;
+      int hb, kb0, kb1;
+      unit_range(blockIdx.x + (q / chunks_per_unit) * gridDim.x, hb, kb0, kb1);
+      const int kb = kb0 + (q % chunks_per_unit) * kMetaChunk + lane;
+      if (kb < kb1) {
+        const size_t sub = 2 * ((size_t)(hb >> 1) * p.nkb + kb) + (hb & 1);
+        nxt0 = *reinterpret_cast<const uint4*>(s.stage_ranges + 4 * sub);
+        nxt1 = make_uint4(s.stage_counts[sub], s.stage_offsets[sub], 0u, 0u);
+      }
+    };
+    auto store_chunk = [&](int buf) {
+      smeta[2 * (buf * kMetaChunk + lane)] = nxt0;
+      smeta[2 * (buf * kMetaChunk + lane) + 1] = nxt1;
+    };
+    load_chunk(0);
+    store_chunk(0);
+    __syncwarp();
+    uint32_t it = 0, oldest = 0;
+    unsigned long long ring_head = 0;
+    uint32_t head_off = 0;
+    unsigned long long ring_start[kRingSlots];
+    for (int q = 0; q < n_chunks; ++q) {
+      load_chunk(q + 1);
+      if (lane == 0) {
+        int hb, kb0, kb1;
+        unit_range(blockIdx.x + (q / chunks_per_unit) * gridDim.x, hb, kb0, kb1);
+        const int band = hb >> 1, half = hb & 1;
+        const int c0 = kb0 + (q % chunks_per_unit) * kMetaChunk;
+        const int c1 = min(kb1, c0 + kMetaChunk);
+        const int width = max(0, min(4, s.tn - band * s.band_tiles - 4 * half));
+        for (int kb = c0; kb < c1 && !flags[0]; ++kb, ++it) {
+          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0))];
+          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0)) + 1];
+          const uint32_t cnt = mc.x;
+          const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
+          const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
+          const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
+          const uint32_t bytes = rg.y + rg.w;
+          const uint32_t need = kSubDescBytes + lbytes + bytes;
+          if (need > p.ring_bytes || ((rg.x | rg.y | rg.z | rg.w) & 15u)) {
+            flag(p.status, MTC_STATUS_BAD_STREAM);
+            flags[0] = 1;
+            break;
+          }
+          unsigned long long pos = ring_head;
+          uint32_t start = head_off;
+          if (start + need > p.ring_bytes) {
+            pos += p.ring_bytes - start;
+            start = 0;
+          }
+          bool ok = true;
+          while (it - oldest >= (uint32_t)kRingSlots ||
+                 (oldest != it && ring_start[oldest % kRingSlots] + p.ring_bytes < pos + need)) {
+            if (!mbar_wait(&pempty[oldest % kRingSlots], (oldest / kRingSlots) & 1, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            ++oldest;
+          }
+          if (!ok) {
+            flags[0] = 1;
+            break;
+          }
+          const int ps = it % kRingSlots;
+          ring_start[ps] = pos;
+          ring_head = pos + need;
+          head_off = start + need;
+          pmeta[4 * ps + 0] = start;
+          pmeta[4 * ps + 1] = cnt;
+          pmeta[4 * ps + 2] = lbytes;
+          pmeta[4 * ps + 3] = rg.y;
+          uint8_t* dst = sP + start;
+          const uint32_t dbytes = width > 0 ? 16u * width * (r1 - r0) : 0u;
+          mbar_expect_tx(&pfull[ps], bytes + dbytes + 8u * ((n_ent + 1u) & ~1u));
+          if (width > 0) {
+            for (int r = r0; r < r1; ++r)
+              bulk_g2s(dst + 64 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles + 4 * half,
+                       16u * width, &pfull[ps]);
+          }
+          if (n_ent) bulk_g2s(dst + kSubDescBytes, s.stage_lists + mc.y, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
+          if (rg.y) bulk_g2s(dst + kSubDescBytes + lbytes, s.records + rg.x, rg.y, &pfull[ps]);
+          if (rg.w) bulk_g2s(dst + kSubDescBytes + lbytes + rg.y, s.records + rg.z, rg.w, &pfull[ps]);
+        }
+      }
+      __syncwarp();
+      store_chunk((q + 1) & 1);
+      __syncwarp();
+      if (flags[0]) break;
+    }
+    if (lane == 0 && flags[0]) {
+      for (uint32_t j = it > (uint32_t)kRingSlots ? it - kRingSlots : 0u; j < it; ++j)
+        (void)mbar_wait(&pfull[j % kRingSlots], (j / kRingSlots) & 1, 10000000ull);
+      flag(p.status, MTC_STATUS_TIMEOUT);
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16_f32(kFeat, kTok);
+      uint32_t it = 0, ucount = 0;
+      for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x, ++ucount) {
+        int hb, kb0, kb1;
+        unit_range(u, hb, kb0, kb1);
+        const int d = ucount & 1;
+        if (ucount >= 2 && !mbar_wait(&acc_empty[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        tc::fence_after();
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int sx = it % p.SX, sw = it % p.SW;
+          if (!mbar_wait(&full_x[sx], (it / p.SX) & 1, p.timeout_ns) ||
+              !mbar_wait(&full_w[sw], (it / p.SW) & 1, p.timeout_ns)) {
+            flags[0] = 1;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t w0 = smem_u32(sW + sw * kWBytes);
+          const uint32_t x0 = smem_u32(sX + sx * kXBytes);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            tc::mma_f16_ss(tmem + 32u * d, tc::smem_desc_k_sw128(w0 + 32 * j), tc::smem_desc_k_sw128(x0 + 32 * j),
+                           idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+          tc::commit(&empty_x[sx]);
+          tc::commit(&empty_w[sw]);
+        }
+        if (flags[0]) break;
+        tc::commit(&acc_full[d]);
+      }
+      tc::commit(drain);
+      (void)mbar_wait(drain, 0, 100000000ull);
+      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+    }
+  } else if (warp >= kDeqWarp0) {
+    // ---------------------------------------------------------------- dequant
+    const int grp = (warp - kDeqWarp0) / kDeqWarps;
+    const int dw = (warp - kDeqWarp0) % kDeqWarps;
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x) {
+      int hb, kb0, kb1;
+      unit_range(u, hb, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        if ((int)(it % kDeqGroups) != grp) continue;
+        const int sw = it % p.SW, ps = it % kRingSlots;
+        if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        if (it >= (uint32_t)p.SW && !mbar_wait(&empty_w[sw], ((it / p.SW) & 1) ^ 1, p.timeout_ns)) {
+          flags[0] = 1;
+          break;
+        }
+        dequant_substage(sW + sw * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
+                         pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
+                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full_w[sw]);
+          mbar_arrive(&pempty[ps]);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    // Thread (warp w, lane l) owns feature 32 w + l of the unit.
+    const int f = 32 * warp + lane;
+    uint32_t ucount = 0;
+    for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x, ++ucount) {
+      int hb, kb0, kb1;
+      unit_range(u, hb, kb0, kb1);
+      const int d = ucount & 1;
+      if (!mbar_wait(&acc_full[d], (ucount >> 1) & 1, p.timeout_ns)) {
+        flags[0] = 1;
+        break;
+      }
+      tc::fence_after();
+      uint32_t v[16];
+      tc::tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * warp) << 16) + 32u * d, v);
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[d]);
+      float* part = p.part + (size_t)u * kTok * kFeat;
+#pragma unroll
+      for (int t = 0; t < kTok; ++t)
+        if (t < p.M) part[t * kFeat + f] = __uint_as_float(v[t]);
+      // ticket: the last unit of the half band reduces in a fixed order
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (tid == 0) flags[1] = atomicAdd(&p.counters[hb], 1u) == (uint32_t)(p.n_kr - 1) ? 1u : 0u;
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (flags[1]) {
+        __threadfence();
+        const int n = hb * kFeat + f;
+        if (n < s.N) {
+          const int col = p.pc ? p.pc[n] : n;
+          for (int t = 0; t < p.M; ++t) {
+            float sum = 0.0f;
+            for (int r = 0; r < p.n_kr; ++r)
+              sum += __ldcg(p.part + ((size_t)(hb * p.n_kr + r) * kTok + t) * kFeat + f);
+            p.Y[(long long)t * p.ldy + col] = sum * p.inv_pow2e;
+          }
+        }
+        if (tid == 0) p.counters[hb] = 0u;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+    }
+    if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
+  }
+
+  tc::fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+struct DecodePlan {
+  int Kp, nkb, n_hb, R, n_kr, n_units, SX, SW, grid;
+  uint32_t ring_bytes;
+  size_t smem, xp_bytes, part_bytes;
+};
+
+bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
+  if (M < 1 || M > kTok) return false;
+  pl->Kp = s->tk * kTile;
+  pl->nkb = (s->tk + 1) / 2;
+  const int n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
+  pl->n_hb = 2 * n_bands;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // about four units per SM, at least four stages each
+  const long long total = (long long)pl->n_hb * pl->nkb;
+  long long R = (total + 4LL * sms - 1) / (4LL * sms);
+  R = R < 4 ? 4 : R;
+  pl->R = (int)(R < pl->nkb ? R : pl->nkb);
+  pl->n_kr = (pl->nkb + pl->R - 1) / pl->R;
+  pl->n_units = pl->n_hb * pl->n_kr;
+  pl->grid = pl->n_units < sms ? pl->n_units : sms;
+  pl->SX = 4;
+  pl->SW = 4;
+  const size_t cap = 227 * 1024;
+  const size_t fixed = 1024 /*align*/ + 1536 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
+  const size_t xb = ((size_t)pl->SX * kXBytes + 1023) & ~(size_t)1023;
+  const size_t used = fixed + xb + (size_t)pl->SW * kWBytes;
+  const size_t ring = (cap - used) & ~(size_t)127;
+  if (s->max_stage_bytes == 0 || ring < s->max_stage_bytes) return false;
+  pl->ring_bytes = (uint32_t)ring;
+  pl->smem = used + ring;
+  pl->xp_bytes = ((size_t)kTok * pl->Kp * 2 + 255) & ~(size_t)255;
+  pl->part_bytes = (size_t)pl->n_units * kTok * kFeat * sizeof(float);
+  return true;
+}
+
+}  // namespace
+}  // namespace mtc
+
+using namespace mtc;
+
+extern "C" size_t mtc_decode_workspace_bytes(const mtc_stream_desc* s, int32_t M) {
+  DecodePlan pl;
+  if (!s || !plan_decode(s, M, &pl)) return 0;
+  return pl.xp_bytes + pl.part_bytes;
+}
+
+extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx, const int32_t* row_perm,
+                          const int32_t* col_perm, float* Y, int64_t ldy, void* ws, size_t ws_bytes,
+                          uint32_t* counters, uint32_t* status, void* stream) {
+  clear_error();
+  MTC_REQUIRE(s && X && Y && ws && counters && s->records && s->tiles && s->row_off,
+              "mtc_decode: null pointer argument");
+  MTC_REQUIRE(M >= 1 && M <= kTok, "mtc_decode: M=%d outside 1..%d (use mtc_gemm_prefill)", M, kTok);
+  MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_decode: bad leading dimensions");
+  MTC_REQUIRE(s->band_tiles * kTile == 2 * kFeat, "mtc_decode: stream band width %d tiles, kernel needs %d",
+              s->band_tiles, 2 * kFeat / kTile);
+  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
+              "mtc_decode: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
+  MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "mtc_decode: workspace not 256-byte aligned");
+  DecodePlan pl;
+  MTC_REQUIRE(plan_decode(s, M, &pl), "mtc_decode: a sub-stage of %u bytes does not fit shared memory",
+              s->max_stage_bytes);
+  if (ws_bytes < pl.xp_bytes + pl.part_bytes) {
+    set_error("mtc_decode: workspace %zu bytes, need %zu", ws_bytes, pl.xp_bytes + pl.part_bytes);
+    return MTC_ERR_WORKSPACE;
+  }
+  cudaStream_t st = as_stream(stream);
+  __half* Xp = static_cast<__half*>(ws);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.xp_bytes);
+  int rc = launch_gather_x(X, ldx, s->K, pl.Kp, row_perm, M, Xp, status, st);
+  if (rc != MTC_OK) return rc;
+  CUtensorMap tmap;
+  rc = encode_xp_map(&tmap, Xp, pl.Kp, M, kTok, "mtc_decode");
+  if (rc != MTC_OK) return rc;
+  DecodeParams p;
+  p.s = *s;
+  p.M = M;
+  p.Y = Y;
+  p.ldy = ldy;
+  p.pc = col_perm;
+  p.part = part;
+  p.counters = counters;
+  p.status = status;
+  p.n_hb = pl.n_hb;
+  p.nkb = pl.nkb;
+  p.n_kr = pl.n_kr;
+  p.R = pl.R;
+  p.n_units = pl.n_units;
+  p.SX = pl.SX;
+  p.SW = pl.SW;
+  p.ring_bytes = pl.ring_bytes;
+  p.pow2e = ldexpf(1.0f, s->exp2);
+  p.inv_pow2e = ldexpf(1.0f, -s->exp2);
+  p.timeout_ns = 2000000000ull;
+  MTC_CHECK_CUDA(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
+                 "mtc_decode: smem attribute");
+  decode_kernel<<<pl.grid, kThreads, pl.smem, st>>>(tmap, p);
+  MTC_CHECK_LAUNCH("mtc_decode");
+  return MTC_OK;
+}

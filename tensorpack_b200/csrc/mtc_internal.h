@@ -3,6 +3,8 @@
 // negative return code plus a message for mtc_last_error().
 #pragma once
 
+#include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -41,5 +43,11 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
       return MTC_ERR_INVALID;                                       \
     }                                                               \
   } while (0)
+
+// Shared launch helpers (mtc_prefill.cu): the X row gather into fp16 Xp and
+// the TMA descriptor of Xp used by the prefill and decode kernels.
+int launch_gather_x(const float* X, long long ldx, int K, int Kp, const int32_t* row_perm, int M, __half* Xp,
+                    uint32_t* status, cudaStream_t st);
+int encode_xp_map(CUtensorMap* map, const __half* Xp, int Kp, int M, int box_rows, const char* who);
 
 }  // namespace mtc

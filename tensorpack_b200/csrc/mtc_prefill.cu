@@ -26,6 +26,7 @@
 //                 shared memory, coalesced in and out).
 #include "mtc_common.cuh"
 #include "mtc_internal.h"
+#include "mtc_substage.cuh"
 #include "mtc_tc.cuh"
 
 namespace mtc {
@@ -41,7 +42,7 @@ constexpr int kProdWarp = 4;   // A tiles
 constexpr int kMmaWarp = 5;    // TMEM allocation (both CTAs), MMA issue (even CTA)
 constexpr int kPackWarp = 6;   // packed sub-stages
 constexpr int kDeqWarp0 = 7;
-constexpr int kDeqWarps = 8;   // dequant warps per stage
+constexpr int kDeqWarps = kSubWarps;   // dequant warps per stage
 // Dequant groups take alternate stages, so each group has two stage times
 // for one stage: a stage's decode is latency-bound (dependent shared-memory
 // loads, decode, stores), and a second group hides that latency.
@@ -62,8 +63,7 @@ constexpr int kMaxS = 4;
 // sized for the largest would hold one or two.
 constexpr int kRingSlots = 8;          // sub-stages in flight at most
 constexpr int kMetaChunk = 32;         // sub-stages of metadata the packed producer stages at a time
-constexpr uint32_t kDescBytes = 128;
-constexpr int kClassGeneric = 7;
+constexpr uint32_t kDescBytes = kSubDescBytes;
 
 struct PrefillParams {
   mtc_stream_desc s;
@@ -83,10 +83,6 @@ __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
   if (st) atomicOr(st, bits);
 }
 
-// byte offset of element (row n, k) in a K-major SWIZZLE_128B tile of 64 fp16 per row
-__device__ __forceinline__ uint32_t sw128_off(int n, int k) {
-  return (uint32_t)n * 128u + ((((uint32_t)k >> 3) ^ ((uint32_t)n & 7u)) << 4) + (((uint32_t)k & 7u) << 1);
-}
 
 // Launched as clusters of two CTAs; cluster c takes pair tiles c, c + G, ...
 // (G = number of clusters), each 512 tokens x one band of 256 features.
@@ -349,140 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           flags[0] = 1;
           break;
         }
-        uint8_t* Bt = sB + sb * kBBytes;
-        const uint8_t* sl = sP + pmeta[4 * ps];
-        const uint32_t cnt = pmeta[4 * ps + 1];
-        const uint64_t* list = reinterpret_cast<const uint64_t*>(sl + kDescBytes);
-        const uint8_t* payload = sl + kDescBytes + pmeta[4 * ps + 2];
-        const uint32_t part0 = pmeta[4 * ps + 3];
-        const mtc_tile_desc* descs = reinterpret_cast<const mtc_tile_desc*>(sl);
-        // record of tile ti (row * 4 + column) inside the payload
-        auto tile_record = [&](int ti) -> const uint8_t* {
-          const mtc_tile_desc& d = descs[ti];
-          return (ti >> 2) == 0 ? payload + (d.record_off - descs[0].record_off)
-                                : payload + part0 + (d.record_off - descs[4].record_off);
-        };
-        const int n_group = (int)(cnt & 0xffffu), n_mb = (int)(cnt >> 16);
-        const int u = 16 * dw + (lane >> 1);
-        // Lane pairs e >= e0 of this warp hold micro-block units: 4 x (16 -
-        // e0) consecutive micro-block entries, taken 16 - e0 at a time.
-        const int e0 = max(0, min(16, n_group - 16 * dw));
-        const int n_mbu = 16 - e0;
-        const int r0 = 4 * (16 * dw + e0 - n_group);
-        if (n_mbu > 0 && r0 < n_mb) {
-          // ---- micro-block entries (split groups): four passes, one half
-          // micro-block per lane each.  P2..P8 share one table-driven
-          // instruction sequence, so lanes of different modes do not
-          // serialise; generic entries (P16, inexact fp16 scales) follow in a
-          // per-lane pass.
-          // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
-          auto store_mb = [&](uint64_t e, const uint32_t (&r)[4]) {
-            const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
-            const int rr = ti >> 2, col = ti & 3;
-            const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
-            const int jj = ((G >> 2) & 1) << 1 | (G & 1);
-            const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
-            const int k0 = 32 * rr + 8 * t + 4 * (mk >> 1);
-            *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r[0], r[1]);
-            *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r[2], r[3]);
-          };
-          uint64_t ent[4];
-          bool ok[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int rel = r0 + k * n_mbu + ((lane >> 1) - e0);
-            ok[k] = (lane >> 1) >= e0 && rel < n_mb;
-            ent[k] = ok[k] ? list[n_group + rel] : 0ull;
-          }
-          // all four decodes run unconditionally (invalid and generic lanes
-          // decode zeros at offset 0), so the compiler can interleave them;
-          // only the stores are predicated
-          bool any_generic = false;
-          uint32_t r4[4][4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int cls = (int)((ent[k] >> 48) & 15u);
-            if (ok[k] && cls == kClassGeneric) any_generic = true;
-            const bool dec = ok[k] && cls != kClassGeneric;
-            const uint64_t e = dec ? ent[k] : 0ull;
-            decode_half_class(dtab, dec ? cls : 0, payload + (uint32_t)(e & 0xffffu),
-                              payload + (uint32_t)((e >> 16) & 0xffffu), h, h2const((uint16_t)((e >> 32) & 0xffffu)),
-                              r4[k]);
-          }
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (ok[k] && (int)((ent[k] >> 48) & 15u) != kClassGeneric) store_mb(ent[k], r4[k]);
-          if (__any_sync(0xffffffffu, any_generic)) {
-#pragma unroll 1
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t e = k == 0 ? ent[0] : k == 1 ? ent[1] : k == 2 ? ent[2] : ent[3];
-              const bool v = k == 0 ? ok[0] : k == 1 ? ok[1] : k == 2 ? ok[2] : ok[3];
-              if (v && (int)((e >> 48) & 15u) == kClassGeneric) {
-                const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
-                const uint32_t* ltab = reinterpret_cast<const uint32_t*>(tile_record(ti));
-                const int L = leaf_of(descs[ti].leaf_start, 4 * G + mk);
-                uint32_t r[4];
-                decode_half_w16(lt_entry(ltab, L, s.scale_words), lt_scale_of(ltab, L, s.scale_words),
-                                payload + (uint32_t)(e & 0xffffu), payload + (uint32_t)((e >> 16) & 0xffffu), h,
-                                p.pow2e, r);
-                store_mb(e, r);
-              }
-            }
-          }
-        }
-        const bool valid = u < n_group;
-        const uint64_t ent = valid ? list[u] : 0ull;
-        const int cls = valid ? (int)((ent >> 48) & 15u) : -1;
-        const int cls0 = __shfl_sync(0xffffffffu, cls, 0);
-        const uint8_t* prim = payload + (uint32_t)(ent & 0xffffu);
-        const uint8_t* sec = payload + (uint32_t)((ent >> 16) & 0xffffu);
-        const uint32_t s2 = h2const((uint16_t)((ent >> 32) & 0xffffu));
-        const int ti = (int)((ent >> 52) & 15u), G = (int)((ent >> 56) & 15u);
-        uint32_t R[4][4];
-        const bool uniform = __all_sync(0xffffffffu, !valid || cls == cls0);
-        if (uniform && cls0 != kClassGeneric) {
-          switch (cls0) {  // warp-uniform branch
-            case 1: decode_run4<2>(prim, sec, h, s2, R); break;
-            case 2: decode_run4<3>(prim, sec, h, s2, R); break;
-            case 3: decode_run4<4>(prim, sec, h, s2, R); break;
-            case 4: decode_run4<5>(prim, sec, h, s2, R); break;
-            case 5: decode_run4<6>(prim, sec, h, s2, R); break;
-            case 6: decode_run4<8>(prim, sec, h, s2, R); break;
-            default:
-#pragma unroll
-              for (int k = 0; k < 4; ++k) R[k][0] = R[k][1] = R[k][2] = R[k][3] = 0u;
-          }
-        } else {
-          // class boundary inside the warp: table decoder for P0..P8 (one
-          // instruction sequence), per-lane generic path for the rest
-          if (valid && cls != kClassGeneric) decode_run4_class(dtab, cls, prim, sec, h, s2, R);
-          if (valid && cls == kClassGeneric)
-            decode_group_generic(reinterpret_cast<const uint32_t*>(tile_record(ti)), descs[ti].leaf_start, G, prim,
-                                 sec, s.scale_words, h, p.pow2e, R);
-        }
-        if (valid) {
-          // R[2 di + dj] = micro-block (2t + di, 2jj + dj) of group G: pairs 0,1
-          // feature 2h (k rows 0..3), pairs 2,3 feature 2h + 1; di selects k 0..3 / 4..7
-          const int r = ti >> 2, col = ti & 3;
-          const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
-          const int jj = ((G >> 2) & 1) << 1 | (G & 1);
-#pragma unroll
-          for (int dj = 0; dj < 2; ++dj) {
-            const int f = 32 * col + 4 * (2 * jj + dj) + 2 * h;
-            *reinterpret_cast<uint4*>(Bt + sw128_off(f, 32 * r + 8 * t)) =
-                make_uint4(R[dj][0], R[dj][1], R[2 + dj][0], R[2 + dj][1]);
-            *reinterpret_cast<uint4*>(Bt + sw128_off(f + 1, 32 * r + 8 * t)) =
-                make_uint4(R[dj][2], R[dj][3], R[2 + dj][2], R[2 + dj][3]);
-          }
-        }
-        if (2 * kb + 1 >= s.tk) {
-          // odd number of k-tile rows: the stage's second row is zero padding
-          const int tid_d = tid - (kDeqWarp0 + grp * kDeqWarps) * 32;
-          for (int c = tid_d; c < BNH * 4; c += kDeqWarps * 32) {
-            const int f = c >> 2, ch = 4 + (c & 3);
-            *reinterpret_cast<uint4*>(Bt + f * 128 + ((ch ^ (f & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
+        dequant_substage(sB + sb * kBBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
+                         pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
+                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32);
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
@@ -839,6 +704,58 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
 }
 
 }  // namespace
+
+// Xp[m][k] = fp16(X[m][pr[k]]) (zero for K <= k < Kp), m < M: the persistent
+// bulk-copy kernel when rows are 16-byte aligned, else one CTA per row.
+int launch_gather_x(const float* X, long long ldx, int K, int Kp, const int32_t* row_perm, int M, __half* Xp,
+                    uint32_t* status, cudaStream_t st) {
+  MTC_REQUIRE((size_t)K * 4 <= 200 * 1024, "gather: K=%d above the 51200 row-staged limit", K);
+  const size_t buf_floats = ((size_t)K + 31) & ~(size_t)31;
+  const size_t sm2 = 2 * buf_floats * 4 + 64;
+  if (Kp <= 2 * kRowThreads * kRowNJ && sm2 <= 227 * 1024 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 &&
+      (ldx & 3) == 0 && (K & 3) == 0) {
+    auto go = [&](auto kernel) -> int {
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2),
+                     "gather: smem attribute");
+      const int grid = row_grid(reinterpret_cast<const void*>(kernel), sm2, M);
+      kernel<<<grid, kRowThreads, sm2, st>>>(X, ldx, K, Kp, row_perm, M, Xp, (int)buf_floats, status);
+      MTC_CHECK_LAUNCH("gather_x");
+      return MTC_OK;
+    };
+    if (Kp <= 2 * kRowThreads * 4) return go(gather_x_bulk_kernel<4>);
+    if (Kp <= 2 * kRowThreads * 8) return go(gather_x_bulk_kernel<8>);
+    if (Kp <= 2 * kRowThreads * 16) return go(gather_x_bulk_kernel<16>);
+    return go(gather_x_bulk_kernel<32>);
+  }
+  const size_t sm = (size_t)K * 4;
+  if (sm > 48 * 1024)
+    MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                   "gather: smem attribute");
+  gather_x_kernel<<<M, 256, sm, st>>>(X, ldx, K, Kp, row_perm, Xp, status);
+  MTC_CHECK_LAUNCH("gather_x");
+  return MTC_OK;
+}
+
+// TMA descriptor of Xp (fp16 [M][Kp]): box 64 (k) x box_rows, 128-byte swizzle.
+int encode_xp_map(CUtensorMap* map, const __half* Xp, int Kp, int M, int box_rows, const char* who) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) {
+    set_error("%s: cuTensorMapEncodeTiled unavailable from the driver", who);
+    return MTC_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(Xp), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d)", who, (int)r);
+    return MTC_ERR_CUDA;
+  }
+  return MTC_OK;
+}
 }  // namespace mtc
 
 using namespace mtc;
@@ -877,33 +794,7 @@ extern "C" int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int3
   int rc = check_prefill(s, M, false, ws, ws_bytes, &pl, "mtc_prefill_gather");
   if (rc != MTC_OK) return rc;
   MTC_REQUIRE(X && ldx >= s->K, "mtc_prefill_gather: bad activations");
-  MTC_REQUIRE((size_t)s->K * 4 <= 200 * 1024, "mtc_prefill_gather: K=%d above the 51200 row-staged limit", s->K);
-  const size_t buf_floats = ((size_t)s->K + 31) & ~(size_t)31;
-  const size_t sm2 = 2 * buf_floats * 4 + 64;
-  if (pl.Kp <= 2 * kRowThreads * kRowNJ && sm2 <= 227 * 1024 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 &&
-      (ldx & 3) == 0 && (s->K & 3) == 0) {
-    auto go = [&](auto kernel) -> int {
-      MTC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2),
-                     "mtc_prefill_gather: smem attribute");
-      const int grid = row_grid(reinterpret_cast<const void*>(kernel), sm2, M);
-      kernel<<<grid, kRowThreads, sm2, as_stream(stream)>>>(X, ldx, s->K, pl.Kp, row_perm, M, static_cast<__half*>(ws),
-                                                            (int)buf_floats, status);
-      MTC_CHECK_LAUNCH("mtc_prefill_gather");
-      return MTC_OK;
-    };
-    if (pl.Kp <= 2 * kRowThreads * 4) return go(gather_x_bulk_kernel<4>);
-    if (pl.Kp <= 2 * kRowThreads * 8) return go(gather_x_bulk_kernel<8>);
-    if (pl.Kp <= 2 * kRowThreads * 16) return go(gather_x_bulk_kernel<16>);
-    return go(gather_x_bulk_kernel<32>);
-  }
-  const size_t sm = (size_t)s->K * 4;
-  if (sm > 48 * 1024)
-    MTC_CHECK_CUDA(cudaFuncSetAttribute(gather_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                   "mtc_prefill_gather: smem attribute");
-  gather_x_kernel<<<M, 256, sm, as_stream(stream)>>>(X, ldx, s->K, pl.Kp, row_perm, static_cast<__half*>(ws),
-                                                     status);
-  MTC_CHECK_LAUNCH("mtc_prefill_gather");
-  return MTC_OK;
+  return launch_gather_x(X, ldx, s->K, pl.Kp, row_perm, M, static_cast<__half*>(ws), status, as_stream(stream));
 }
 
 extern "C" int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32_t* col_perm_inv, float* Y,
@@ -947,29 +838,12 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
               "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
   const bool col_perm_inv = permuted_output != 0;
-  EncodeTiledFn enc = encode_tiled();
-  if (!enc) {
-    set_error("mtc_prefill_gemm: cuTensorMapEncodeTiled unavailable from the driver");
-    return MTC_ERR_CUDA;
-  }
   cudaStream_t st = as_stream(stream);
   __half* Xp = static_cast<__half*>(ws);
   float* Yp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.xp_bytes);
-  // TMA descriptor of Xp: fp16 [M][Kp], box 64 (k) x 256 (rows), 128-byte swizzle
   CUtensorMap tmap;
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)pl.Kp, (cuuint64_t)M};
-    cuuint64_t strides[1] = {(cuuint64_t)pl.Kp * 2};
-    cuuint32_t box[2] = {BK, 256};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Xp, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("mtc_prefill_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
-      return MTC_ERR_CUDA;
-    }
-  }
+  rc = encode_xp_map(&tmap, Xp, pl.Kp, M, 256, "mtc_prefill_gemm");
+  if (rc != MTC_OK) return rc;
   PrefillParams p;
   p.s = *s;
   p.M = M;

@@ -103,6 +103,7 @@ class DeviceStream:
                 inv[np.asarray(mat.col_perm)] = np.arange(self.N, dtype=np.int32)
                 self.col_perm_inv = torch.from_numpy(inv).to(dev)
             self.counters = torch.zeros(self.n_bands, dtype=torch.int32, device=dev)
+            self.decode_counters = torch.zeros(2 * self.n_bands, dtype=torch.int32, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ws = {}
         self.n_leaves = len(ls)
@@ -144,6 +145,21 @@ class DeviceStream:
                                 _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), rows_per_unit, ws.data_ptr(),
                                 ws.numel() * 4, self.counters.data_ptr(), self.status.data_ptr(),
                                 _stream(self.device)), "gemv")
+        return Y
+
+    def decode(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
+        """Y[:M] = X @ W for M <= 16 (tensor-core decode kernel)."""
+        lib = _lib.load()
+        M = X.shape[0]
+        need = int(lib.mtc_decode_workspace_bytes(ctypes.byref(self.desc), M))
+        ws = self._ws.get("decode")
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+            self._ws["decode"] = ws
+        _lib.check(lib.mtc_decode(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
+                                  _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), ws.data_ptr(), ws.numel(),
+                                  self.decode_counters.data_ptr(), self.status.data_ptr(), _stream(self.device)),
+                   "decode")
         return Y
 
     def prefill_workspace(self, M: int) -> torch.Tensor:
@@ -195,7 +211,7 @@ class DeviceStream:
         """Y = X @ W, picking the decode kernel for M <= 16 and the tensor-core
         prefill kernel above."""
         if X.shape[0] <= DECODE_MAX_M:
-            return self.gemv(X, Y)
+            return self.decode(X, Y)
         return self.prefill(X, Y)
 
     def check_status(self):

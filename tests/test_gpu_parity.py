@@ -203,6 +203,36 @@ def test_gemv_forced_modes(dev, M):
     check_gemm(m, deq, deq, X, dev)
 
 
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_cuda_core_gemv_matches_reference(golden_dir, dev, M):
+    """mtc_gemv (split-K mma.sync kernel, also behind mtc_gemv_static) against the reference; mtc_gemm itself
+    routes M <= 16 to the tensor-core mtc_decode."""
+    import torch
+
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g = load(golden_dir, "llm_like_256x512.npz")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    tag = "b4.25_"
+    inner = qt_from_golden(g, tag + "inner_")
+    pr, pc = g[tag + "row_perm"], g[tag + "col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g[tag + "total_bits"])))
+    stored = O.quadtree_dequant(W[pr][:, pc], inner.sizes, inner.leaf, inner.modes, inner.scales)
+    X = inputs.llm_activations(M, 256, seed=M + 40, outlier_seed=1)
+    ds = m.device_stream(dev)
+    Xt = torch.from_numpy(X).to(dev)
+    Y1 = torch.empty(M, 512, device=dev)
+    Y2 = torch.empty(M, 512, device=dev)
+    ds.gemv(Xt, Y1)
+    ds.decode(Xt, Y2)
+    torch.cuda.synchronize()
+    ds.check_status()
+    ref = X.astype(np.float64) @ O.unpermute(stored, pr, pc).astype(np.float64)
+    assert O.relative_frobenius_error(ref, Y1.cpu().numpy()) < TOL_REF
+    # both compute the exact fp16-operand product; only the accumulation order differs
+    assert O.relative_frobenius_error(Y1.double().cpu().numpy(), Y2.cpu().numpy()) < TOL_F16
+
+
 def test_gemv_multiscale(golden_dir, dev):
     from tensorpack_b200.kernels.gemm import MTCMatrix
 
