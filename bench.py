@@ -306,18 +306,17 @@ def main():
     launches_per_step = 3
 
     # --- decode M = 1 over rotating copies of the stream (> 4x L2) ---
-    # Every buffer the decode kernel streams is copied: tile records and
-    # descriptors, row offsets and the sub-stage work lists.
-    stream_bytes = ds.record_bytes + ds.stage_lists.numel() * 8
+    # Every buffer the decode kernel streams is copied: the sub-stage images
+    # and their metadata.
+    stream_bytes = ds.stage_images.numel()
     copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
     descs, keep = [], []
     for _ in range(copies):
-        bufs = [ds.records.clone(), ds.tiles.clone(), ds.row_off.clone(), ds.stage_lists.clone(),
-                ds.stage_counts.clone(), ds.stage_offsets.clone(), ds.stage_ranges.clone()]
+        bufs = [ds.stage_images.clone(), ds.stage_counts.clone(), ds.stage_offsets.clone(),
+                ds.stage_ranges.clone()]
         keep += bufs
         d = _lib.StreamDesc.from_buffer_copy(ds.desc)
-        (d.records, d.tiles, d.row_off, d.stage_lists, d.stage_counts, d.stage_offsets,
-         d.stage_ranges) = [b.data_ptr() for b in bufs]
+        d.stage_images, d.stage_counts, d.stage_offsets, d.stage_ranges = [b.data_ptr() for b in bufs]
         descs.append(d)
     lib = _lib.load()
     import ctypes

@@ -105,15 +105,18 @@ typedef struct mtc_stream_desc {
   uint64_t record_bytes;         /* total bytes of `records` */
   uint32_t max_row_bytes;        /* largest k-tile row of any band */
   int32_t scale_words;           /* 1: bf16 scale in the entry, 2: extra fp32 scale word */
-  /* Prefill work lists (NULL until mtc_repack_stage_plan / _fill build
-   * them), CSR layout, one list per sub-stage q = 2 * (band * n_kb + kb) +
-   * half: the four tiles 4 * half .. 4 * half + 3 of a band in k-tile rows
-   * 2 kb and 2 kb + 1 (n_kb = (tk + 1) / 2). */
-  const uint64_t* stage_lists;   /* entries of all sub-stages */
+  /* Sub-stage images for the tensor-core kernels (NULL until
+   * mtc_repack_stage_plan / _fill build them), one per sub-stage q =
+   * 2 * (band * n_kb + kb) + half: the four tiles 4 * half .. 4 * half + 3
+   * of a band in k-tile rows 2 kb and 2 kb + 1 (n_kb = (tk + 1) / 2).  An
+   * image is what the kernels stage in shared memory, read with one bulk
+   * copy: [128 B tile descriptors (4 of row 2 kb, 4 of row 2 kb + 1)][work
+   * list][records of row 2 kb][records of row 2 kb + 1]. */
+  const uint8_t* stage_images;   /* all images, each 16-byte aligned */
   const uint32_t* stage_counts;  /* [n_sub]: group entries | micro-block entries << 16 */
-  const uint32_t* stage_offsets; /* [n_sub + 1]: first entry of each sub-stage */
-  const uint32_t* stage_ranges;  /* [n_sub][4]: record byte offset and length of the two row parts */
-  uint32_t max_stage_bytes;      /* largest staged footprint: 128 + list + records */
+  const uint32_t* stage_offsets; /* [n_sub + 1]: byte offset of each image (last = total) */
+  const uint32_t* stage_ranges;  /* [n_sub][4]: image bytes, work-list bytes, row-0 record bytes, row-1 record bytes */
+  uint32_t max_stage_bytes;      /* largest image */
   uint32_t pad_;
 } mtc_stream_desc;
 
@@ -143,27 +146,27 @@ MTC_API int mtc_repack_fill(const uint8_t* arena, uint64_t arena_bytes, const mt
                     const uint32_t* tile_leaf_begin, const mtc_stream_desc* s, uint8_t* records,
                     uint32_t* scratch_u32, void* stream);
 
-/* Repack step 3 (prefill only): per sub-stage (half a band: four tiles, in a
- * pair of k-tile rows; one per CTA of the prefill kernel's CTA pair) a work
- * list of 64-bit entries.  An 8x8 group covered by one leaf is one "group"
+/* Repack step 3 (tensor-core kernels): per sub-stage (half a band: four
+ * tiles, in a pair of k-tile rows) an image holding the tile descriptors, a
+ * work list of 64-bit entries and a copy of the records.  An 8x8 group covered by one leaf is one "group"
  * entry; a group of four 4x4 leaves becomes four "micro-block" entries.  Group
  * entries come first, then micro-block entries, each sorted by decode class
  * (0 = P0, 1..6 = P2, P3, P4, P5, P6, P8, 7 = generic: P16 or a scale not
  * exact in fp16), so prefill dequant warps take mode-uniform work.  Entry
  * bits: 0-15 primary-plane and 16-31 secondary-plane byte offsets into the
- * sub-stage's records (its row-0 part, then its row-1 part), 32-47 fp16 bits
+ * image's records (its row-0 part, then its row-1 part), 32-47 fp16 bits
  * of scale * 2^exp2, 48-51 class, 52-55 tile in the sub-stage (row * 4 +
  * column), 56-59 group (Z order), 60-61 micro-block in the group, 62
  * micro-block entry.
- * plan: writes `counts` (group | micro-block << 16 per sub-stage), CSR
- *       `offsets` (n_sub + 1) and `ranges` (n_sub x 4 words: row-0 part
- *       offset and bytes, row-1 part offset and bytes), returns out_host =
- *       {total entries, largest staged footprint}; `scratch_u32` holds
- *       n_sub + 2 words; syncs.
- * fill: writes the entries into `lists` (total entries). */
+ * plan: writes `counts` (group | micro-block << 16 per sub-stage), image
+ *       `offsets` (n_sub + 1 byte offsets) and `ranges` (n_sub x 4 words:
+ *       image, list, row-0 record and row-1 record bytes), returns out_host =
+ *       {total image bytes, largest image}; `scratch_u32` holds 5 n_sub + 2
+ *       words; syncs.
+ * fill: writes the images into `images` (total image bytes). */
 MTC_API int mtc_repack_stage_plan(const mtc_stream_desc* s, uint32_t* counts, uint32_t* offsets,
                                   uint32_t* ranges, uint32_t* scratch_u32, uint64_t* out_host, void* stream);
-MTC_API int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint64_t* lists,
+MTC_API int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint8_t* images,
                                   void* stream);
 
 /* Exact dequantisation (replaces MTCMatrix.to_array, gemm.py:510-538, and

@@ -191,30 +191,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         int hb, kb0, kb1;
         unit_range(blockIdx.x + (q / chunks_per_unit) * gridDim.x, hb, kb0, kb1);
-        const int band = hb >> 1, half = hb & 1;
         const int c0 = kb0 + (q % chunks_per_unit) * kMetaChunk;
         const int c1 = min(kb1, c0 + kMetaChunk);
-        const int width = max(0, min(4, s.tn - band * s.band_tiles - 4 * half));
         for (int kb = c0; kb < c1 && !flags[0]; ++kb, ++it) {
-          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0))];
-          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0)) + 1];
+          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0))];  // bytes: image, list, row 0, row 1
+          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0)) + 1];  // counts, image offset
           const uint32_t cnt = mc.x;
-          const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
-          const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
-          const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
-          const uint32_t bytes = rg.y + rg.w;
-          const uint32_t need = kSubDescBytes + lbytes + bytes;
-          if (need > p.ring_bytes || ((rg.x | rg.y | rg.z | rg.w) & 15u)) {
+          const uint32_t need = rg.x;
+          if (need > p.ring_bytes || ((need | mc.y) & 15u)) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
           }
+          // (positions advance without division: a piece that would cross
+          // the end of the ring starts at the next lap instead)
           unsigned long long pos = ring_head;
           uint32_t start = head_off;
           if (start + need > p.ring_bytes) {
             pos += p.ring_bytes - start;
             start = 0;
           }
+          // live bytes are [ring_start[oldest], ring_head): the new piece must
+          // end within one ring length of the oldest live sub-stage's start
           bool ok = true;
           while (it - oldest >= (uint32_t)kRingSlots ||
                  (oldest != it && ring_start[oldest % kRingSlots] + p.ring_bytes < pos + need)) {
@@ -234,19 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           head_off = start + need;
           pmeta[4 * ps + 0] = start;
           pmeta[4 * ps + 1] = cnt;
-          pmeta[4 * ps + 2] = lbytes;
-          pmeta[4 * ps + 3] = rg.y;
-          uint8_t* dst = sP + start;
-          const uint32_t dbytes = width > 0 ? 16u * width * (r1 - r0) : 0u;
-          mbar_expect_tx(&pfull[ps], bytes + dbytes + 8u * ((n_ent + 1u) & ~1u));
-          if (width > 0) {
-            for (int r = r0; r < r1; ++r)
-              bulk_g2s(dst + 64 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles + 4 * half,
-                       16u * width, &pfull[ps]);
-          }
-          if (n_ent) bulk_g2s(dst + kSubDescBytes, s.stage_lists + mc.y, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
-          if (rg.y) bulk_g2s(dst + kSubDescBytes + lbytes, s.records + rg.x, rg.y, &pfull[ps]);
-          if (rg.w) bulk_g2s(dst + kSubDescBytes + lbytes + rg.y, s.records + rg.z, rg.w, &pfull[ps]);
+          pmeta[4 * ps + 2] = rg.y;
+          pmeta[4 * ps + 3] = rg.z;
+          // the whole sub-stage image in one bulk copy
+          mbar_expect_tx(&pfull[ps], need);
+          bulk_g2s(sP + start, s.stage_images + mc.y, need, &pfull[ps]);
         }
       }
       __syncwarp();
@@ -440,7 +430,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   MTC_REQUIRE(ldx >= s->K && ldy >= s->N, "mtc_decode: bad leading dimensions");
   MTC_REQUIRE(s->band_tiles * kTile == 2 * kFeat, "mtc_decode: stream band width %d tiles, kernel needs %d",
               s->band_tiles, 2 * kFeat / kTile);
-  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
+  MTC_REQUIRE(s->stage_images && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
               "mtc_decode: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, "mtc_decode: workspace not 256-byte aligned");
   DecodePlan pl;

@@ -204,25 +204,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int q = 0; q < n_chunks; ++q) {
       load_chunk(q + 1);                              // in flight while lane 0 issues chunk q
       if (lane == 0) {
-        const int tile = cid + (q / chunks_per_tile) * n_clusters;
-        const int band = tile % p.n_bands;
         const int kb0 = (q % chunks_per_tile) * kMetaChunk;
         const int kb1 = min(p.nkb, kb0 + kMetaChunk);
-        const int width = max(0, min(4, s.tn - band * s.band_tiles - 4 * (int)rank));  // tiles of this half
         for (int kb = kb0; kb < kb1 && !flags[0]; ++kb, ++it) {
           // The sub-stage goes to the byte ring as one contiguous piece:
           // descriptors (128 B) | work list | row-0 records | row-1 records.
           // Its ring range must be free: release older sub-stages (FIFO)
           // until it is.
-          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0))];
-          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0)) + 1];
+          const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0))];  // bytes: image, list, row 0, row 1
+          const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - kb0)) + 1];  // counts, image offset
           const uint32_t cnt = mc.x;
-          const int r0 = 2 * kb, r1 = min(2 * kb + 2, s.tk);
-          const uint32_t n_ent = (cnt & 0xffffu) + (cnt >> 16);
-          const uint32_t lbytes = (8u * n_ent + 15u) & ~15u;
-          const uint32_t bytes = rg.y + rg.w;
-          const uint32_t need = kDescBytes + lbytes + bytes;
-          if (need > p.ring_bytes || ((rg.x | rg.y | rg.z | rg.w) & 15u)) {
+          const uint32_t need = rg.x;
+          if (need > p.ring_bytes || ((need | mc.y) & 15u)) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
@@ -256,19 +249,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           head_off = start + need;
           pmeta[4 * ps + 0] = start;
           pmeta[4 * ps + 1] = cnt;
-          pmeta[4 * ps + 2] = lbytes;
-          pmeta[4 * ps + 3] = rg.y;
-          uint8_t* dst = sP + start;
-          const uint32_t dbytes = width > 0 ? 16u * width * (r1 - r0) : 0u;
-          mbar_expect_tx(&pfull[ps], bytes + dbytes + 8u * ((n_ent + 1u) & ~1u));
-          if (width > 0) {
-            for (int r = r0; r < r1; ++r)
-              bulk_g2s(dst + 64 * (r - r0), s.tiles + (size_t)r * s.tn + band * s.band_tiles + 4 * rank,
-                       16u * width, &pfull[ps]);
-          }
-          if (n_ent) bulk_g2s(dst + kDescBytes, s.stage_lists + mc.y, 8u * ((n_ent + 1u) & ~1u), &pfull[ps]);
-          if (rg.y) bulk_g2s(dst + kDescBytes + lbytes, s.records + rg.x, rg.y, &pfull[ps]);
-          if (rg.w) bulk_g2s(dst + kDescBytes + lbytes + rg.y, s.records + rg.z, rg.w, &pfull[ps]);
+          pmeta[4 * ps + 2] = rg.y;
+          pmeta[4 * ps + 3] = rg.z;
+          // the whole sub-stage image in one bulk copy
+          mbar_expect_tx(&pfull[ps], need);
+          bulk_g2s(sP + start, s.stage_images + mc.y, need, &pfull[ps]);
         }
       }
       __syncwarp();
@@ -834,7 +819,7 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   PrefillPlan pl;
   int rc = check_prefill(s, M, permuted_output != 0, ws, ws_bytes, &pl, "mtc_prefill_gemm");
   if (rc != MTC_OK) return rc;
-  MTC_REQUIRE(s->stage_lists && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
+  MTC_REQUIRE(s->stage_images && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
               "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
   const bool col_perm_inv = permuted_output != 0;

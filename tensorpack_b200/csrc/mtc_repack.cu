@@ -304,13 +304,15 @@ __device__ __forceinline__ uint2 half_row_range(const mtc_stream_desc& s, int ba
 // group of four 4x4 leaves becomes four micro-block entries (each with its own
 // mode), so every entry decodes with one mode.  Group entries come first,
 // sorted by class, then micro-block entries, sorted by class.  Pass 1
-// (FILL = false) counts and records the sub-stage's record ranges, pass 2
-// writes at the CSR offsets.
+// (FILL = false) counts the entries and measures the two record parts; pass
+// 2 writes the image: descriptors, entries, a copy of the records.
+constexpr uint32_t kImgDescBytes = 128;
+
 template <bool FILL>
 __global__ void __launch_bounds__(128) stage_lists_kernel(mtc_stream_desc s, int nkb, const uint32_t* __restrict__ offs,
                                                           uint32_t* __restrict__ counts, uint32_t* __restrict__ totals,
                                                           uint32_t* __restrict__ ranges,
-                                                          uint64_t* __restrict__ lists) {
+                                                          uint8_t* __restrict__ images) {
   __shared__ uint32_t cnt[16];   // [0, 8) group classes, [8, 16) micro-block classes
   __shared__ uint32_t base[16];
   const int q = blockIdx.x;
@@ -404,55 +406,75 @@ __global__ void __launch_bounds__(128) stage_lists_kernel(mtc_stream_desc s, int
     if (!FILL) {
       counts[q] = ng | ((acc - ng) << 16);
       totals[q] = acc;
-      ranges[4 * (size_t)q + 0] = p0.x;
-      ranges[4 * (size_t)q + 1] = p0.y;
-      ranges[4 * (size_t)q + 2] = p1.x;
+      ranges[4 * (size_t)q + 2] = p0.y;
       ranges[4 * (size_t)q + 3] = p1.y;
     }
   }
   __syncthreads();
   if (FILL) {
+    uint8_t* img = images + offs[q];
+    uint64_t* list = reinterpret_cast<uint64_t*>(img + kImgDescBytes);
     for (int k = 0; k < 4; ++k)
-      if (cls[k] >= 0) lists[(size_t)offs[q] + base[cls[k]] + rank[k]] = entry[k];
+      if (cls[k] >= 0) list[base[cls[k]] + rank[k]] = entry[k];
+    // descriptors of the 4 x 2 tiles (zero where the tile lies beyond the matrix)
+    if (i < 8) {
+      const int rr = i >> 2, cc = i & 3;
+      const int kt2 = 2 * kb + rr, nt2 = band * s.band_tiles + 4 * half + cc;
+      uint4 dsc = make_uint4(0u, 0u, 0u, 0u);
+      if (kt2 < s.tk && nt2 < s.tn && 4 * half + cc < s.band_tiles)
+        dsc = *reinterpret_cast<const uint4*>(s.tiles + (size_t)kt2 * s.tn + nt2);
+      reinterpret_cast<uint4*>(img)[i] = dsc;
+    }
+    // the records of the two row parts, 16 bytes per thread-step
+    const uint32_t lbytes = (8u * (base[15] + cnt[15]) + 15u) & ~15u;
+    uint4* dst = reinterpret_cast<uint4*>(img + kImgDescBytes + lbytes);
+    const uint4* src0 = reinterpret_cast<const uint4*>(s.records + p0.x);
+    const uint4* src1 = reinterpret_cast<const uint4*>(s.records + p1.x);
+    for (uint32_t c = i; c < p0.y / 16u; c += blockDim.x) dst[c] = src0[c];
+    for (uint32_t c = i; c < p1.y / 16u; c += blockDim.x) dst[p0.y / 16u + c] = src1[c];
   }
 }
 
-// Exclusive scan of the per-sub-stage entry totals into CSR offsets (single
-// CTA), plus the largest staged footprint: descriptors + list + records.
+// Image sizes (descriptors + list + records, 16-byte multiples) and their
+// exclusive scan into byte offsets (single CTA); ranges[q] = {image bytes,
+// list bytes, row-0 record bytes, row-1 record bytes}; out = {total, largest}.
 __global__ void __launch_bounds__(1024) stage_scan_kernel(const uint32_t* __restrict__ totals, int n_sub,
-                                                          const uint32_t* __restrict__ ranges,
-                                                          uint32_t* __restrict__ offs, uint32_t* __restrict__ out) {
-  __shared__ uint32_t part[1024];
+                                                          uint32_t* __restrict__ ranges, uint32_t* __restrict__ offs,
+                                                          unsigned long long* __restrict__ out) {
+  __shared__ unsigned long long part[1024];
   __shared__ uint32_t red[1024];
   const int per = (n_sub + blockDim.x - 1) / blockDim.x;
   const int lo = min(n_sub, (int)threadIdx.x * per), hi = min(n_sub, lo + per);
-  uint32_t sum = 0, mx = 0;
-  // each list starts at an even entry (16-byte aligned for the bulk copy)
+  unsigned long long sum = 0;
+  uint32_t mx = 0;
   for (int i = lo; i < hi; ++i) {
-    sum += (totals[i] + 1u) & ~1u;
-    const uint32_t bytes = ranges[4 * (size_t)i + 1] + ranges[4 * (size_t)i + 3];
-    mx = max(mx, 128u + ((8u * totals[i] + 15u) & ~15u) + bytes);
+    const uint32_t lbytes = (8u * totals[i] + 15u) & ~15u;
+    const uint32_t size = kImgDescBytes + lbytes + ranges[4 * (size_t)i + 2] + ranges[4 * (size_t)i + 3];
+    ranges[4 * (size_t)i + 0] = size;
+    ranges[4 * (size_t)i + 1] = lbytes;
+    sum += size;
+    mx = max(mx, size);
   }
   part[threadIdx.x] = sum;
   red[threadIdx.x] = mx;
   __syncthreads();
   for (int dl = 1; dl < (int)blockDim.x; dl <<= 1) {
-    const uint32_t v = threadIdx.x >= (unsigned)dl ? part[threadIdx.x - dl] : 0u;
+    const unsigned long long v = threadIdx.x >= (unsigned)dl ? part[threadIdx.x - dl] : 0ull;
     __syncthreads();
     part[threadIdx.x] += v;
     __syncthreads();
   }
-  uint32_t off = part[threadIdx.x] - sum;
+  unsigned long long off = part[threadIdx.x] - sum;
   for (int i = lo; i < hi; ++i) {
-    offs[i] = off;
-    off += (totals[i] + 1u) & ~1u;
+    offs[i] = (uint32_t)off;
+    off += ranges[4 * (size_t)i + 0];
   }
   for (int dl = blockDim.x / 2; dl > 0; dl >>= 1) {
     if (threadIdx.x < (unsigned)dl) red[threadIdx.x] = max(red[threadIdx.x], red[threadIdx.x + dl]);
     __syncthreads();
   }
   if (threadIdx.x == blockDim.x - 1) {
-    offs[n_sub] = part[blockDim.x - 1];
+    offs[n_sub] = (uint32_t)part[blockDim.x - 1];
     out[0] = part[blockDim.x - 1];
   }
   if (threadIdx.x == 0) out[1] = red[0];
@@ -476,27 +498,30 @@ extern "C" int mtc_repack_stage_plan(const mtc_stream_desc* s, uint32_t* counts,
   const int n_sub = 2 * nb * nkb;
   cudaStream_t st = as_stream(stream);
   uint32_t* totals = scratch_u32;
-  uint32_t* out = scratch_u32 + n_sub;
+  unsigned long long* out = reinterpret_cast<unsigned long long*>(scratch_u32 + ((n_sub + 1) & ~1));
   stage_lists_kernel<false><<<n_sub, 128, 0, st>>>(*s, nkb, nullptr, counts, totals, ranges, nullptr);
   MTC_CHECK_LAUNCH("mtc_repack_stage_plan: count");
   stage_scan_kernel<<<1, 1024, 0, st>>>(totals, n_sub, ranges, offsets, out);
   MTC_CHECK_LAUNCH("mtc_repack_stage_plan: scan");
-  uint32_t back[2];
-  MTC_CHECK_CUDA(cudaMemcpyAsync(back, out, 8, cudaMemcpyDeviceToHost, st), "mtc_repack_stage_plan: copy back");
+  unsigned long long back[2];
+  MTC_CHECK_CUDA(cudaMemcpyAsync(back, out, 16, cudaMemcpyDeviceToHost, st), "mtc_repack_stage_plan: copy back");
   MTC_CHECK_CUDA(cudaStreamSynchronize(st), "mtc_repack_stage_plan: sync");
+  MTC_REQUIRE(back[0] < (1ull << 32), "mtc_repack_stage_plan: %llu bytes of sub-stage images exceed 32-bit offsets",
+              back[0]);
   out_host[0] = back[0];
   out_host[1] = back[1];
   return MTC_OK;
 }
 
-extern "C" int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint64_t* lists,
+extern "C" int mtc_repack_stage_fill(const mtc_stream_desc* s, const uint32_t* offsets, uint8_t* images,
                                      void* stream) {
   clear_error();
-  MTC_REQUIRE(s && offsets && lists && s->tiles && s->row_off && s->records, "mtc_repack_stage_fill: null pointer");
+  MTC_REQUIRE(s && offsets && images && s->tiles && s->row_off && s->records, "mtc_repack_stage_fill: null pointer");
+  MTC_REQUIRE((reinterpret_cast<uintptr_t>(images) & 15) == 0, "mtc_repack_stage_fill: images not 16-byte aligned");
   const int nkb = (s->tk + 1) / 2;
   const int nb = (s->tn + s->band_tiles - 1) / s->band_tiles;
   stage_lists_kernel<true><<<2 * nb * nkb, 128, 0, as_stream(stream)>>>(*s, nkb, offsets, nullptr, nullptr, nullptr,
-                                                                        lists);
+                                                                        images);
   MTC_CHECK_LAUNCH("mtc_repack_stage_fill");
   return MTC_OK;
 }

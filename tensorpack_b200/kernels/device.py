@@ -73,22 +73,22 @@ class DeviceStream:
             _lib.check(lib.mtc_repack_fill(d_arena.data_ptr(), arena.nbytes, d_leaves.data_ptr(),
                                            d_begin.data_ptr(), ctypes.byref(self.desc), self.records.data_ptr(),
                                            scratch.data_ptr(), st), "repack fill")
-            # class-sorted work lists of every prefill sub-stage (half a band, two
-            # k-tile rows): CSR counts, offsets, entries, plus record ranges
+            # sub-stage images for the tensor-core kernels (half a band, two k-tile
+            # rows each): descriptors, class-sorted work list, a copy of the records
             n_sub = 2 * self.n_bands * ((tk + 1) // 2)
             self.stage_counts = torch.empty(n_sub, dtype=torch.int32, device=dev)
             self.stage_offsets = torch.empty(n_sub + 1, dtype=torch.int32, device=dev)
             self.stage_ranges = torch.empty(4 * n_sub, dtype=torch.int32, device=dev)
-            st_scratch = torch.empty(n_sub + 2, dtype=torch.int32, device=dev)
+            st_scratch = torch.empty(n_sub + 8, dtype=torch.int32, device=dev)
             _lib.check(lib.mtc_repack_stage_plan(ctypes.byref(self.desc), self.stage_counts.data_ptr(),
                                                  self.stage_offsets.data_ptr(), self.stage_ranges.data_ptr(),
                                                  st_scratch.data_ptr(), out, st),
                        "repack stage plan")
-            self.stage_lists = torch.zeros(max(int(out[0]), 2), dtype=torch.int64, device=dev)
+            self.stage_images = torch.zeros(max(int(out[0]), 16), dtype=torch.uint8, device=dev)
             self.max_stage_bytes = int(out[1])
             _lib.check(lib.mtc_repack_stage_fill(ctypes.byref(self.desc), self.stage_offsets.data_ptr(),
-                                                 self.stage_lists.data_ptr(), st), "repack stage fill")
-            self.desc.stage_lists = self.stage_lists.data_ptr()
+                                                 self.stage_images.data_ptr(), st), "repack stage fill")
+            self.desc.stage_images = self.stage_images.data_ptr()
             self.desc.stage_counts = self.stage_counts.data_ptr()
             self.desc.stage_offsets = self.stage_offsets.data_ptr()
             self.desc.stage_ranges = self.stage_ranges.data_ptr()
