@@ -40,12 +40,15 @@ constexpr int kMmaWarp = 5;
 constexpr int kPackWarp = 6;
 constexpr int kDeqWarp0 = 7;
 constexpr int kDeqWarps = kSubWarps;
-constexpr int kDeqGroups = 2;
+#ifndef MTC_DECODE_GROUPS
+#define MTC_DECODE_GROUPS 2
+#endif
+constexpr int kDeqGroups = MTC_DECODE_GROUPS;
 constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
 constexpr uint32_t kXBytes = kTok * BK * 2;     // 2 KB
 constexpr uint32_t kWBytes = kFeat * BK * 2;    // 16 KB
-constexpr int kMaxS = 8;
-constexpr int kRingSlots = 8;
+constexpr int kMaxS = 16;
+constexpr int kRingSlots = 16;
 constexpr int kMetaChunk = 32;
 constexpr uint32_t kTmemCols = 64;              // two accumulators of 32 columns
 
@@ -60,6 +63,7 @@ struct DecodeParams {
   uint32_t* status;
   int n_hb, nkb, n_kr, R, n_units;
   int SX, SW;
+  uint32_t x_box_bytes;  // bytes one X load brings: 64 k x M rows (rows M..15 of the tile are never read back)
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
@@ -89,8 +93,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort, [1] last unit
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
   uint32_t* pmeta = tmem_slot + 4;                  // [kRingSlots][4]
-  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1024);
-  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1536);  // [2][kMetaChunk][2]
+  uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1280);
+  uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1792);  // [2][kMetaChunk][2]
+  static_assert((4 * kMaxS + 2 * kRingSlots + 5) * 8 + 32 + 16 * kRingSlots <= 1280, "barrier region");
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (flags[0]) break;
-          mbar_expect_tx(&full_x[sx], kXBytes);
+          mbar_expect_tx(&full_x[sx], p.x_box_bytes);
           tc::tma_load_2d(sX + sx * kXBytes, &tmap_x, kb * BK, 0, &full_x[sx]);
         }
       }
@@ -394,10 +399,10 @@ bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
   pl->n_kr = (pl->nkb + pl->R - 1) / pl->R;
   pl->n_units = pl->n_hb * pl->n_kr;
   pl->grid = pl->n_units < sms ? pl->n_units : sms;
-  pl->SX = 4;
+  pl->SX = 16;  // X loads queue behind the packed copies on the copy engine: keep them far ahead
   pl->SW = 4;
   const size_t cap = 227 * 1024;
-  const size_t fixed = 1024 /*align*/ + 1536 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
+  const size_t fixed = 1024 /*align*/ + 1792 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
   const size_t xb = ((size_t)pl->SX * kXBytes + 1023) & ~(size_t)1023;
   const size_t used = fixed + xb + (size_t)pl->SW * kWBytes;
   const size_t ring = (cap - used) & ~(size_t)127;
@@ -446,7 +451,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   int rc = launch_gather_x(X, ldx, s->K, pl.Kp, row_perm, M, Xp, status, st);
   if (rc != MTC_OK) return rc;
   CUtensorMap tmap;
-  rc = encode_xp_map(&tmap, Xp, pl.Kp, M, kTok, "mtc_decode");
+  rc = encode_xp_map(&tmap, Xp, pl.Kp, M, M, "mtc_decode");
   if (rc != MTC_OK) return rc;
   DecodeParams p;
   p.s = *s;
@@ -463,6 +468,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   p.R = pl.R;
   p.n_units = pl.n_units;
   p.SX = pl.SX;
+  p.x_box_bytes = (uint32_t)(BK * 2 * M);
   p.SW = pl.SW;
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
