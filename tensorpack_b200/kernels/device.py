@@ -20,6 +20,11 @@ from ..core import layout
 
 BAND_TILES = 8  # tiles per column band = 256 output features (one per consumer warp)
 DECODE_MAX_M = 16  # largest M served by the split-K decode kernel
+# Version of the device tile stream layout (tile descriptors, records, row
+# offsets, sub-stage images).  A stream saved by another version is rebuilt
+# from the host layout instead of uploaded.
+STREAM_FORMAT_VERSION = 3
+_STREAM_ARRAYS = ("tiles", "row_off", "records", "stage_counts", "stage_offsets", "stage_ranges", "stage_images")
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -28,6 +33,48 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def stream_compatible(meta: dict, mat) -> bool:
+    """Whether a saved stream was made by this device format for ``mat``."""
+    K, N = mat.shape
+    try:
+        return (int(meta["version"]) == STREAM_FORMAT_VERSION and int(meta["band_tiles"]) == BAND_TILES
+                and int(meta["K"]) == K and int(meta["N"]) == N and int(meta["tk"]) == -(-K // layout.TILE)
+                and int(meta["tn"]) == -(-N // layout.TILE) and int(meta["exp2"]) == layout.choose_exp2(mat.leaf_set)
+                and int(meta["scale_words"]) == (1 if layout.bf16_exact(np.asarray(mat.scales)) else 2))
+    except (KeyError, TypeError, ValueError):
+        return False
+
+
+def check_stream_buffers(meta: dict, arrs: dict) -> None:
+    """Host-side consistency checks of a saved stream before it is uploaded:
+    sizes, monotone offsets, sub-stage images inside their buffer."""
+    try:
+        tk, tn = int(meta["tk"]), int(meta["tn"])
+        n_bands = -(-tn // BAND_TILES)
+        n_sub = 2 * n_bands * ((tk + 1) // 2)
+        rb = int(meta["record_bytes"])
+        a = {k: np.asarray(arrs[k]) for k in _STREAM_ARRAYS}
+    except (KeyError, TypeError, ValueError):
+        raise ValueError("saved device stream: metadata or arrays missing") from None
+    want = {"tiles": (np.uint8, tk * tn * 16), "row_off": (np.int32, n_bands * (tk + 1)),
+            "records": (np.uint8, max(rb, 16)), "stage_counts": (np.int32, n_sub),
+            "stage_offsets": (np.int32, n_sub + 1), "stage_ranges": (np.int32, 4 * n_sub)}
+    for k, (dt, n) in want.items():
+        if a[k].dtype != dt or a[k].size != n:
+            raise ValueError(f"saved device stream: {k} has {a[k].size} x {a[k].dtype}, expected {n} x {np.dtype(dt)}")
+    if a["stage_images"].dtype != np.uint8:
+        raise ValueError("saved device stream: stage_images must be bytes")
+    ro = a["row_off"].reshape(n_bands, tk + 1).astype(np.int64)
+    if (np.diff(ro, axis=1) < 0).any() or ro.min(initial=0) < 0 or ro.max(initial=0) > rb:
+        raise ValueError("saved device stream: row offsets not monotone or beyond the records")
+    offs = a["stage_offsets"].view(np.uint32).astype(np.int64)
+    sizes = a["stage_ranges"].view(np.uint32).astype(np.int64).reshape(n_sub, 4)[:, 0]
+    if (offs % 16).any() or (np.diff(offs) < sizes).any() or offs[-1] > a["stage_images"].size:
+        raise ValueError("saved device stream: sub-stage images overlap or lie outside their buffer")
+    if sizes.max(initial=0) > int(meta["max_stage_bytes"]):
+        raise ValueError("saved device stream: a sub-stage image exceeds the recorded maximum")
 
 
 class DeviceStream:
@@ -88,6 +135,13 @@ class DeviceStream:
             self.max_stage_bytes = int(out[1])
             _lib.check(lib.mtc_repack_stage_fill(ctypes.byref(self.desc), self.stage_offsets.data_ptr(),
                                                  self.stage_images.data_ptr(), st), "repack stage fill")
+            self._finish(mat, len(ls))
+
+    def _finish(self, mat, n_leaves: int):
+        """Descriptor fields of the sub-stage images, permutations and the
+        per-stream counters (shared by the repack and the upload paths)."""
+        dev = self.device
+        with torch.cuda.device(dev):
             self.desc.stage_images = self.stage_images.data_ptr()
             self.desc.stage_counts = self.stage_counts.data_ptr()
             self.desc.stage_offsets = self.stage_offsets.data_ptr()
@@ -106,7 +160,49 @@ class DeviceStream:
             self.decode_counters = torch.zeros(2 * self.n_bands, dtype=torch.int32, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ws = {}
-        self.n_leaves = len(ls)
+        self.n_leaves = n_leaves
+
+    # ------------------------------------------------------------------ saving / loading
+    def export_buffers(self):
+        """(metadata, name -> numpy array) of the device stream, for the
+        on-disk format (tensorpack_b200.core.fileformat)."""
+        meta = {"version": STREAM_FORMAT_VERSION, "band_tiles": BAND_TILES, "K": self.K, "N": self.N,
+                "tk": self.tk, "tn": self.tn, "exp2": self.exp2, "scale_words": self.scale_words,
+                "record_bytes": self.record_bytes, "max_row_bytes": self.max_row_bytes,
+                "max_stage_bytes": self.max_stage_bytes}
+        arrs = {name: getattr(self, name).cpu().numpy() for name in _STREAM_ARRAYS}
+        return meta, arrs
+
+    @classmethod
+    def from_buffers(cls, mat, device, meta: dict, arrs: dict) -> "DeviceStream":
+        """Upload a saved stream (checked by ``stream_compatible`` and
+        ``check_stream_buffers``) instead of repacking."""
+        if not torch.cuda.is_available():
+            raise RuntimeError("the MTC GEMM path needs a CUDA device (B200, sm_100a); none is available")
+        _lib.load()
+        check_stream_buffers(meta, arrs)
+        self = cls.__new__(cls)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError(f"DeviceStream needs a CUDA device, got {self.device}")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.K, self.N = int(meta["K"]), int(meta["N"])
+        self.tk, self.tn = int(meta["tk"]), int(meta["tn"])
+        self.n_bands = -(-self.tn // BAND_TILES)
+        self.exp2, self.scale_words = int(meta["exp2"]), int(meta["scale_words"])
+        self.record_bytes, self.max_row_bytes = int(meta["record_bytes"]), int(meta["max_row_bytes"])
+        self.max_stage_bytes = int(meta["max_stage_bytes"])
+        with torch.cuda.device(self.device):
+            for name in _STREAM_ARRAYS:
+                a = np.ascontiguousarray(arrs[name])
+                setattr(self, name, torch.from_numpy(a.copy()).to(self.device))
+        self.desc = _lib.StreamDesc(
+            records=self.records.data_ptr(), tiles=self.tiles.data_ptr(), row_off=self.row_off.data_ptr(),
+            K=self.K, N=self.N, tk=self.tk, tn=self.tn, band_tiles=BAND_TILES, exp2=self.exp2,
+            record_bytes=self.record_bytes, max_row_bytes=self.max_row_bytes, scale_words=self.scale_words)
+        self._finish(mat, mat.num_leaves)
+        return self
 
     # ------------------------------------------------------------------
     @property

@@ -248,6 +248,30 @@ class MTCMatrix:
             self._device[key] = ds
         return ds
 
+    def attach_device_stream(self, ds) -> None:
+        """Use an already built device stream (e.g. uploaded from a file)."""
+        self._device[str(ds.device)] = ds
+
+    # ------------------------------------------------------------------ files
+    def save(self, path, *, include_stream: bool = False, device=None) -> None:
+        """Write this matrix to a versioned ``.mtcpk`` file
+        (tensorpack_b200.core.fileformat); ``include_stream`` also stores the
+        device tile stream so that loading skips the repack."""
+        from ..core.fileformat import save_mtc
+
+        save_mtc(path, self, include_stream=include_stream, device=device)
+
+    @classmethod
+    def load(cls, path, *, device=None, use_stream: bool = True, mmap: bool = False) -> "MTCMatrix":
+        """Read a matrix written by ``save`` (raises ValueError on a corrupt,
+        truncated or foreign file)."""
+        from ..core.fileformat import load_mtc
+
+        mat = load_mtc(path, device=device, use_stream=use_stream, mmap=mmap)
+        if not isinstance(mat, cls):
+            raise ValueError(f"{path} holds a bundle of {len(mat)} matrices; use fileformat.load_mtc")
+        return mat
+
     def to_tensor(self, device=None):
         """Exact fp32 dequantisation on the GPU, original channel order."""
         return self.device_stream(device).dequant(original_order=True)
