@@ -331,7 +331,7 @@ def main():
                                   None if ds.row_perm is None else ds.row_perm.data_ptr(),
                                   None if ds.col_perm is None else ds.col_perm.data_ptr(), y1.data_ptr(),
                                   y1.stride(0), ws.data_ptr(), ws.numel(), ds.decode_counters.data_ptr(),
-                                  ds.status.data_ptr(), stream.cuda_stream), "decode")
+                                  ds.status.data_ptr(), None, stream.cuda_stream), "decode")
 
     for i in range(max(args.warmup, copies)):
         decode(i)

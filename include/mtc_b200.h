@@ -37,7 +37,7 @@ extern "C" {
 #define MTC_API
 #endif
 
-#define MTC_ABI_VERSION 1
+#define MTC_ABI_VERSION 2
 
 enum {
   MTC_OK = 0,
@@ -53,6 +53,24 @@ enum {
   MTC_STATUS_X_RANGE = 2u,       /* |x| beyond the fp16 range of the tensor path */
   MTC_STATUS_BAD_STREAM = 4u     /* a tile record failed a bounds check       */
 };
+
+/* Output epilogue fused into the kernel that writes Y (pass NULL for none):
+ *   Y[m][j] = act(acc[m][j] + bias[j])
+ * where j is the column of Y as written (the original column for calls that
+ * take a column permutation; the stored column when the output is left in
+ * stored order) and acc the product.  bias may be NULL.  Replaces the
+ * separate bias add of LinearMTCAdaptive.forward (mtc/nn/layers.py:146-151)
+ * and the activation that follows the layer.
+ *   MTC_ACT_RELU       max(x, 0)  (NaN stays NaN)
+ *   MTC_ACT_SILU       x / (1 + exp(-x))
+ *   MTC_ACT_GELU_TANH  0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) */
+enum { MTC_ACT_NONE = 0, MTC_ACT_RELU = 1, MTC_ACT_SILU = 2, MTC_ACT_GELU_TANH = 3 };
+
+typedef struct mtc_epilogue {
+  const float* bias; /* device, one per output column, or NULL */
+  int32_t act;       /* MTC_ACT_* */
+  int32_t pad_;
+} mtc_epilogue;
 
 /* One quadtree leaf as handed to the GPU repack (host builds, device reads).
  * Leaves are grouped by 32x32 tile (tile-major, grid order kt*tn+nt) and
@@ -222,7 +240,8 @@ MTC_API int mtc_gemv_static(const mtc_stream_desc* s, const float* X, int32_t M,
 MTC_API size_t mtc_decode_workspace_bytes(const mtc_stream_desc* s, int32_t M);
 MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                        const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy, void* ws,
-                       size_t ws_bytes, uint32_t* counters, uint32_t* status, void* stream);
+                       size_t ws_bytes, uint32_t* counters, uint32_t* status, const mtc_epilogue* ep,
+                       void* stream);
 
 /* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
  * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,
@@ -235,22 +254,26 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
 MTC_API size_t mtc_prefill_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t permuted);
 MTC_API int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                              const int32_t* row_perm, const int32_t* col_perm_inv, float* Y,
-                             int64_t ldy, void* ws, size_t ws_bytes, uint32_t* status, void* stream);
+                             int64_t ldy, void* ws, size_t ws_bytes, uint32_t* status,
+                             const mtc_epilogue* ep, void* stream);
 
 /* The three stages mtc_gemm_prefill runs, for callers that fuse or time them
  * separately (same workspace):
  *   gather:  ws <- fp16 X[:, row_perm] (padded to tk*32 columns)
  *   gemm:    fused dequant + tcgen05 GEMM of that; writes Y directly
- *            (permuted_output = 0) or the permuted-column product into ws
- *   scatter: Y[:, col_perm] <- the permuted-column product in ws */
+ *            (permuted_output = 0; the epilogue `ep` is applied there) or the
+ *            permuted-column product into ws (permuted_output = 1; `ep` must
+ *            then be NULL and is given to the scatter instead)
+ *   scatter: Y[:, col_perm] <- epilogue of the permuted-column product in ws */
 MTC_API int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                                const int32_t* row_perm, void* ws, size_t ws_bytes, uint32_t* status,
                                void* stream);
 MTC_API int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, int64_t ldy,
                              int32_t permuted_output, void* ws, size_t ws_bytes, uint32_t* status,
-                             void* stream);
+                             const mtc_epilogue* ep, void* stream);
 MTC_API int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32_t* col_perm_inv,
-                                float* Y, int64_t ldy, void* ws, size_t ws_bytes, void* stream);
+                                float* Y, int64_t ldy, void* ws, size_t ws_bytes, const mtc_epilogue* ep,
+                                void* stream);
 
 /* Row-wise column gather: Y[m][j] = row_m[pos[j]] with row_m the
  * concatenation of nseg segments src[g*seg_stride + m*ldp + (0..seg_len-1)]
@@ -258,7 +281,7 @@ MTC_API int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32
  * of a multi-GPU GEMM in original column order. */
 MTC_API int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ldp, int32_t nseg,
                              int32_t seg_len, const int32_t* pos, int32_t N, int32_t M, float* Y,
-                             int64_t ldy, void* stream);
+                             int64_t ldy, const mtc_epilogue* ep, void* stream);
 
 /* GPU candidate search of the rate-distortion allocators (replaces the Numba
  * _search_kernel / _search_mode, mtc/core/allocation.py:106-160, used by

@@ -47,6 +47,18 @@ class StreamDesc(ctypes.Structure):
 
 assert ctypes.sizeof(StreamDesc) == 104
 
+
+class Epilogue(ctypes.Structure):
+    """struct mtc_epilogue: Y = act(acc + bias[col])."""
+
+    _fields_ = [("bias", c_p), ("act", c_i32), ("pad_", c_i32)]
+
+
+assert ctypes.sizeof(Epilogue) == 16
+ACT_NONE, ACT_RELU, ACT_SILU, ACT_GELU_TANH = 0, 1, 2, 3
+ACTIVATIONS = {None: ACT_NONE, "none": ACT_NONE, "relu": ACT_RELU, "silu": ACT_SILU, "gelu_tanh": ACT_GELU_TANH}
+_EP = ctypes.POINTER(Epilogue)
+
 # name -> (restype, argtypes); every symbol declared in include/mtc_b200.h.
 SIGNATURES = {
     "mtc_abi_version": (c_i32, []),
@@ -65,14 +77,15 @@ SIGNATURES = {
     "mtc_gemv_static": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_p]),
     "mtc_decode_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32]),
     "mtc_decode": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_size, c_p,
-                           c_p, c_p]),
+                           c_p, _EP, c_p]),
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemm_prefill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64,
-                                 c_p, c_size, c_p, c_p]),
+                                 c_p, c_size, c_p, _EP, c_p]),
     "mtc_prefill_gather": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_size, c_p, c_p]),
-    "mtc_prefill_gemm": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_i64, c_i32, c_p, c_size, c_p, c_p]),
-    "mtc_prefill_scatter": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_p, c_i64, c_p, c_size, c_p]),
-    "mtc_permute_rows": (c_i32, [c_p, c_i64, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_p, c_i64, c_p]),
+    "mtc_prefill_gemm": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_i64, c_i32, c_p, c_size, c_p, _EP,
+                                 c_p]),
+    "mtc_prefill_scatter": (c_i32, [ctypes.POINTER(StreamDesc), c_i32, c_p, c_p, c_i64, c_p, c_size, _EP, c_p]),
+    "mtc_permute_rows": (c_i32, [c_p, c_i64, c_i64, c_i32, c_i32, c_p, c_i32, c_i32, c_p, c_i64, _EP, c_p]),
 }
 
 _lock = threading.Lock()
@@ -96,7 +109,7 @@ def load(path: str = LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.mtc_abi_version() != 1:
+        if lib.mtc_abi_version() != 2:
             raise NativeLibraryError("libmtc_b200.so ABI version mismatch")
         _lib = lib
         return lib

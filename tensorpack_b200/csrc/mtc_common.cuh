@@ -607,6 +607,35 @@ __device__ __forceinline__ void decode_group_w16(const uint8_t* rec, uint16_t n_
 // mbarrier / bulk-copy / mma wrappers
 // ---------------------------------------------------------------------------
 
+// ---------------------------------------------------------------------------
+// Output epilogue (mtc_epilogue of the C ABI): y = act(x + bias[j]).
+// ---------------------------------------------------------------------------
+struct Epi {
+  const float* bias;  // nullable
+  int act;            // MTC_ACT_*
+};
+
+__device__ __forceinline__ float epi_act(float x, int act) {
+  switch (act) {
+    case MTC_ACT_RELU:
+      return x < 0.0f ? 0.0f : x;  // NaN passes through, as in torch.relu
+    case MTC_ACT_SILU:
+      return x / (1.0f + expf(-x));
+    case MTC_ACT_GELU_TANH: {
+      // GELU, tanh form (Hendrycks & Gimpel): sqrt(2/pi) and 0.044715
+      const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+      return 0.5f * x * (1.0f + tanhf(u));
+    }
+    default:
+      return x;
+  }
+}
+
+__device__ __forceinline__ float epi_apply(const Epi& e, float x, long long j) {
+  if (e.bias) x += __ldg(e.bias + j);
+  return e.act ? epi_act(x, e.act) : x;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -67,6 +67,7 @@ struct DecodeParams {
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
+  Epi ep;              // bias / activation applied to Y
 };
 
 __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float sum = 0.0f;
             for (int r = 0; r < p.n_kr; ++r)
               sum += __ldcg(p.part + ((size_t)(hb * p.n_kr + r) * kTok + t) * kFeat + f);
-            p.Y[(long long)t * p.ldy + col] = sum * p.inv_pow2e;
+            p.Y[(long long)t * p.ldy + col] = epi_apply(p.ep, sum * p.inv_pow2e, col);
           }
         }
         if (tid == 0) p.counters[hb] = 0u;
@@ -427,8 +428,13 @@ extern "C" size_t mtc_decode_workspace_bytes(const mtc_stream_desc* s, int32_t M
 
 extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx, const int32_t* row_perm,
                           const int32_t* col_perm, float* Y, int64_t ldy, void* ws, size_t ws_bytes,
-                          uint32_t* counters, uint32_t* status, void* stream) {
+                          uint32_t* counters, uint32_t* status, const mtc_epilogue* ep, void* stream) {
   clear_error();
+  EpiArg epa;
+  {
+    const int rc = read_epilogue(ep, &epa, "mtc_decode");
+    if (rc != MTC_OK) return rc;
+  }
   MTC_REQUIRE(s && X && Y && ws && counters && s->records && s->tiles && s->row_off,
               "mtc_decode: null pointer argument");
   MTC_REQUIRE(M >= 1 && M <= kTok, "mtc_decode: M=%d outside 1..%d (use mtc_gemm_prefill)", M, kTok);
@@ -474,6 +480,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
   p.timeout_ns = 2000000000ull;
+  p.ep = Epi{epa.bias, epa.act};
   MTC_CHECK_CUDA(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
                  "mtc_decode: smem attribute");
   decode_kernel<<<pl.grid, kThreads, pl.smem, st>>>(tmap, p);

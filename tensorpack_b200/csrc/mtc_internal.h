@@ -44,6 +44,28 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
     }                                                               \
   } while (0)
 
+// The epilogue argument of the C ABI, checked (act in range) and flattened
+// for kernel parameters; NULL means none.
+struct EpiArg {
+  const float* bias = nullptr;
+  int act = MTC_ACT_NONE;
+};
+inline int read_epilogue(const mtc_epilogue* ep, EpiArg* out, const char* who) {
+  *out = EpiArg();
+  if (!ep) return MTC_OK;
+  if (ep->act < MTC_ACT_NONE || ep->act > MTC_ACT_GELU_TANH) {
+    set_error("%s: unknown activation %d", who, ep->act);
+    return MTC_ERR_INVALID;
+  }
+  if (ep->bias && (reinterpret_cast<uintptr_t>(ep->bias) & 3)) {
+    set_error("%s: bias not 4-byte aligned", who);
+    return MTC_ERR_INVALID;
+  }
+  out->bias = ep->bias;
+  out->act = ep->act;
+  return MTC_OK;
+}
+
 // Shared launch helpers (mtc_prefill.cu): the X row gather into fp16 Xp and
 // the TMA descriptor of Xp used by the prefill and decode kernels.
 int launch_gather_x(const float* X, long long ldx, int K, int Kp, const int32_t* row_perm, int M, __half* Xp,

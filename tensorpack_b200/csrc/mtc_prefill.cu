@@ -77,6 +77,7 @@ struct PrefillParams {
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
+  Epi ep;             // bias / activation applied to Y (direct output only)
 };
 
 __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
@@ -86,6 +87,9 @@ __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
 
 // Launched as clusters of two CTAs; cluster c takes pair tiles c, c + G, ...
 // (G = number of clusters), each 512 tokens x one band of 256 features.
+// EPI: the output epilogue (bias / activation) is applied in the store loop;
+// the plain instance keeps the epilogue warps' registers for the main loop.
+template <bool EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -362,10 +366,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int lb = 0; lb < 32; lb += 16) {
           const int m0 = mblk * CBM + 256 * (int)rank + 128 * half + 32 * warp + lb + (lane >> 2);
+          // (the epilogue instance loads 32 columns at a time: fewer live
+          // registers next to the activation's)
+          constexpr int RW = EPI ? 4 : 8;
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 64) {
-            uint32_t v[32];
-            tc::tmem_ld_16x256b_x8(tmem + ((uint32_t)(32 * warp + lb) << 16) + half * 256 + c, v);
+          for (int c = 0; c < BN; c += 8 * RW) {
+            uint32_t v[4 * RW];
+            if constexpr (EPI)
+              tc::tmem_ld_16x256b_x4(tmem + ((uint32_t)(32 * warp + lb) << 16) + half * 256 + c, v);
+            else
+              tc::tmem_ld_16x256b_x8(tmem + ((uint32_t)(32 * warp + lb) << 16) + half * 256 + c, v);
             const int nb = band * BN + c + 2 * (lane & 3);
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
@@ -373,10 +383,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (m >= p.M) continue;
               float* y = p.Y + (long long)m * p.ldy;
 #pragma unroll
-              for (int r = 0; r < 8; ++r) {
+              for (int r = 0; r < RW; ++r) {
                 const int n = nb + 8 * r;
-                const float a = __uint_as_float(v[4 * r + 2 * hr]) * p.inv_pow2e;
-                const float b = __uint_as_float(v[4 * r + 2 * hr + 1]) * p.inv_pow2e;
+                float a = __uint_as_float(v[4 * r + 2 * hr]) * p.inv_pow2e;
+                float b = __uint_as_float(v[4 * r + 2 * hr + 1]) * p.inv_pow2e;
+                if constexpr (EPI) {
+                  if (n < s.N) a = epi_apply(p.ep, a, n);
+                  if (n + 1 < s.N) b = epi_apply(p.ep, b, n + 1);
+                }
                 if (p.vec2 && n + 1 < s.N) {
                   *reinterpret_cast<float2*>(y + n) = make_float2(a, b);
                 } else {
@@ -437,7 +451,7 @@ __global__ void __launch_bounds__(256) gather_x_kernel(const float* __restrict__
 __global__ void __launch_bounds__(512) permute_rows_kernel(const float* __restrict__ src, long long seg_stride,
                                                            long long ldp, int nseg, int seg_len,
                                                            const int32_t* __restrict__ pos, int N,
-                                                           float* __restrict__ Y, long long ldy) {
+                                                           float* __restrict__ Y, long long ldy, const Epi ep) {
   extern __shared__ float row[];
   const int m = blockIdx.x;
   for (int g = 0; g < nseg; ++g) {
@@ -446,7 +460,7 @@ __global__ void __launch_bounds__(512) permute_rows_kernel(const float* __restri
   }
   __syncthreads();
   float* dst = Y + (long long)m * ldy;
-  for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = row[pos[j]];
+  for (int j = threadIdx.x; j < N; j += blockDim.x) dst[j] = epi_apply(ep, row[pos[j]], j);
 }
 
 // Persistent row kernels for the HBM-bound gather / scatter around the GEMM:
@@ -466,7 +480,7 @@ template <int NJ>
 __global__ void __launch_bounds__(kRowThreads)
     permute_rows_bulk_kernel(const float* __restrict__ src, long long seg_stride, long long ldp, int nseg,
                              int seg_len, const int32_t* __restrict__ pos, int N, int M, float* __restrict__ Y,
-                             long long ldy, int buf_floats, uint32_t* status) {
+                             long long ldy, int buf_floats, const Epi ep, uint32_t* status) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   float* buf = reinterpret_cast<float*>(smem_raw);  // [2][buf_floats]
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf + 2 * buf_floats);
@@ -509,10 +523,18 @@ __global__ void __launch_bounds__(kRowThreads)
     }
     const float* row = buf + b * buf_floats;
     float* dst = Y + (long long)m * ldy;
+    if (ep.bias || ep.act) {
 #pragma unroll
-    for (int i = 0; i < NJ; ++i) {
-      const int j = tid + i * kRowThreads;
-      if (j < N) dst[j] = row[pj[i]];
+      for (int i = 0; i < NJ; ++i) {
+        const int j = tid + i * kRowThreads;
+        if (j < N) dst[j] = epi_apply(ep, row[pj[i]], j);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NJ; ++i) {
+        const int j = tid + i * kRowThreads;
+        if (j < N) dst[j] = row[pj[i]];
+      }
     }
     __syncthreads();
   }
@@ -588,8 +610,9 @@ int row_grid(const void* kernel, size_t smem, int M) {
 }
 
 int launch_permute_rows(const float* src, long long seg_stride, long long ldp, int nseg, int seg_len,
-                        const int32_t* pos, int N, int M, float* Y, long long ldy, uint32_t* status,
-                        cudaStream_t st) {
+                        const int32_t* pos, int N, int M, float* Y, long long ldy, const EpiArg& epa,
+                        uint32_t* status, cudaStream_t st) {
+  const Epi ep{epa.bias, epa.act};
   const size_t row = (size_t)nseg * seg_len * 4;
   const size_t buf_floats = ((size_t)nseg * seg_len + 31) & ~(size_t)31;
   const size_t sm2 = 2 * buf_floats * 4 + 64;
@@ -601,7 +624,7 @@ int launch_permute_rows(const float* src, long long seg_stride, long long ldp, i
                      "permute: smem attribute");
       const int grid = row_grid(reinterpret_cast<const void*>(kernel), sm2, M);
       kernel<<<grid, kRowThreads, sm2, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, (int)buf_floats,
-                                             status);
+                                             ep, status);
       MTC_CHECK_LAUNCH("permute_rows");
       return MTC_OK;
     };
@@ -614,7 +637,7 @@ int launch_permute_rows(const float* src, long long seg_stride, long long ldp, i
   if (row > 48 * 1024)
     MTC_CHECK_CUDA(cudaFuncSetAttribute(permute_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row),
                    "permute: smem attribute");
-  permute_rows_kernel<<<M, 512, row, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, Y, ldy);
+  permute_rows_kernel<<<M, 512, row, st>>>(src, seg_stride, ldp, nseg, seg_len, pos, N, Y, ldy, ep);
   MTC_CHECK_LAUNCH("permute_rows");
   return MTC_OK;
 }
@@ -783,42 +806,57 @@ extern "C" int mtc_prefill_gather(const mtc_stream_desc* s, const float* X, int3
 }
 
 extern "C" int mtc_prefill_scatter(const mtc_stream_desc* s, int32_t M, const int32_t* col_perm_inv, float* Y,
-                                   int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+                                   int64_t ldy, void* ws, size_t ws_bytes, const mtc_epilogue* ep, void* stream) {
   clear_error();
   PrefillPlan pl;
   int rc = check_prefill(s, M, true, ws, ws_bytes, &pl, "mtc_prefill_scatter");
   if (rc != MTC_OK) return rc;
   MTC_REQUIRE(Y && col_perm_inv && ldy >= s->N, "mtc_prefill_scatter: bad output");
+  EpiArg epa;
+  rc = read_epilogue(ep, &epa, "mtc_prefill_scatter");
+  if (rc != MTC_OK) return rc;
   const float* Yp = reinterpret_cast<const float*>(static_cast<const uint8_t*>(ws) + pl.xp_bytes);
-  return launch_permute_rows(Yp, 0, pl.Np, 1, s->N, col_perm_inv, s->N, M, Y, ldy, nullptr, as_stream(stream));
+  return launch_permute_rows(Yp, 0, pl.Np, 1, s->N, col_perm_inv, s->N, M, Y, ldy, epa, nullptr, as_stream(stream));
 }
 
 extern "C" int mtc_permute_rows(const float* src, int64_t seg_stride, int64_t ldp, int32_t nseg, int32_t seg_len,
-                                const int32_t* pos, int32_t N, int32_t M, float* Y, int64_t ldy, void* stream) {
+                                const int32_t* pos, int32_t N, int32_t M, float* Y, int64_t ldy,
+                                const mtc_epilogue* ep, void* stream) {
   clear_error();
   MTC_REQUIRE(src && pos && Y && nseg >= 1 && seg_len >= 1 && N >= 1 && M >= 1 && ldy >= N,
               "mtc_permute_rows: bad arguments");
-  return launch_permute_rows(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, nullptr, as_stream(stream));
+  EpiArg epa;
+  const int rc = read_epilogue(ep, &epa, "mtc_permute_rows");
+  if (rc != MTC_OK) return rc;
+  return launch_permute_rows(src, seg_stride, ldp, nseg, seg_len, pos, N, M, Y, ldy, epa, nullptr, as_stream(stream));
 }
 
 extern "C" int mtc_gemm_prefill(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                                 const int32_t* row_perm, const int32_t* col_perm_inv, float* Y, int64_t ldy,
-                                void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
+                                void* ws, size_t ws_bytes, uint32_t* status, const mtc_epilogue* ep, void* stream) {
   clear_error();
-  int rc = mtc_prefill_gather(s, X, M, ldx, row_perm, ws, ws_bytes, status, stream);
+  EpiArg epa;
+  int rc = read_epilogue(ep, &epa, "mtc_gemm_prefill");
   if (rc != MTC_OK) return rc;
-  rc = mtc_prefill_gemm(s, M, Y, ldy, col_perm_inv != nullptr ? 1 : 0, ws, ws_bytes, status, stream);
+  rc = mtc_prefill_gather(s, X, M, ldx, row_perm, ws, ws_bytes, status, stream);
   if (rc != MTC_OK) return rc;
-  if (col_perm_inv) return mtc_prefill_scatter(s, M, col_perm_inv, Y, ldy, ws, ws_bytes, stream);
+  rc = mtc_prefill_gemm(s, M, Y, ldy, col_perm_inv != nullptr ? 1 : 0, ws, ws_bytes, status,
+                        col_perm_inv != nullptr ? nullptr : ep, stream);
+  if (rc != MTC_OK) return rc;
+  if (col_perm_inv) return mtc_prefill_scatter(s, M, col_perm_inv, Y, ldy, ws, ws_bytes, ep, stream);
   return MTC_OK;
 }
 
 extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, int64_t ldy, int32_t permuted_output,
-                                void* ws, size_t ws_bytes, uint32_t* status, void* stream) {
+                                void* ws, size_t ws_bytes, uint32_t* status, const mtc_epilogue* ep, void* stream) {
   clear_error();
   PrefillPlan pl;
   int rc = check_prefill(s, M, permuted_output != 0, ws, ws_bytes, &pl, "mtc_prefill_gemm");
   if (rc != MTC_OK) return rc;
+  EpiArg epa;
+  rc = read_epilogue(ep, &epa, "mtc_prefill_gemm");
+  if (rc != MTC_OK) return rc;
+  MTC_REQUIRE(!(permuted_output && ep), "mtc_prefill_gemm: the epilogue of a permuted output goes to the scatter");
   MTC_REQUIRE(s->stage_images && s->stage_counts && s->stage_offsets && s->stage_ranges && s->max_stage_bytes,
               "mtc_prefill_gemm: stage work lists missing (run mtc_repack_stage_plan and mtc_repack_stage_fill)");
   MTC_REQUIRE(permuted_output || (Y && ldy >= s->N), "mtc_prefill_gemm: bad output");
@@ -845,7 +883,10 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
   p.timeout_ns = 2000000000ull;
-  MTC_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
+  p.ep = Epi{epa.bias, epa.act};
+  const bool with_ep = epa.bias || epa.act;
+  auto kernel = with_ep ? prefill_kernel<true> : prefill_kernel<false>;
+  MTC_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
                  "mtc_prefill_gemm: smem attribute");
   // CTA pairs: one cluster of two CTAs per pair tile, as many clusters as
   // can be resident at once (persistent; each loops over tiles)
@@ -862,12 +903,12 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   cfg.numAttrs = 1;
   int max_clusters = 0;
   cfg.gridDim = dim3(2, 1, 1);
-  MTC_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, prefill_kernel, &cfg),
+  MTC_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg),
                  "mtc_prefill_gemm: cluster occupancy");
   MTC_REQUIRE(max_clusters >= 1, "mtc_prefill_gemm: no CTA pair of %zu bytes of shared memory fits", pl.smem);
   const int clusters = pl.n_tiles < max_clusters ? pl.n_tiles : max_clusters;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  MTC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, prefill_kernel, tmap, p), "mtc_prefill_gemm: launch");
+  MTC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p), "mtc_prefill_gemm: launch");
   MTC_CHECK_LAUNCH("mtc_prefill_gemm");
   return MTC_OK;
 }

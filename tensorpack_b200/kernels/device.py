@@ -35,6 +35,27 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def epilogue(bias: Optional[torch.Tensor] = None, activation=None) -> Optional[_lib.Epilogue]:
+    """The fused output epilogue Y = act(acc + bias[col]) of the kernels, or
+    None for a plain product.  ``bias`` is a contiguous fp32 CUDA tensor with
+    one value per output column of Y as written; ``activation`` is None,
+    "relu", "silu" or "gelu_tanh".  The caller keeps ``bias`` alive until
+    the kernel has run (the returned struct holds its device pointer)."""
+    if activation not in _lib.ACTIVATIONS:
+        raise ValueError(f"unknown activation {activation!r} (one of relu, silu, gelu_tanh)")
+    act = _lib.ACTIVATIONS[activation]
+    if bias is None and act == _lib.ACT_NONE:
+        return None
+    if bias is not None:
+        if bias.dtype != torch.float32 or not bias.is_cuda or not bias.is_contiguous() or bias.dim() != 1:
+            raise ValueError("bias must be a contiguous 1-D float32 CUDA tensor")
+    return _lib.Epilogue(bias=None if bias is None else bias.data_ptr(), act=act)
+
+
+def _ep(e: Optional[_lib.Epilogue]):
+    return None if e is None else ctypes.byref(e)
+
+
 def stream_compatible(meta: dict, mat) -> bool:
     """Whether a saved stream was made by this device format for ``mat``."""
     K, N = mat.shape
@@ -161,6 +182,32 @@ class DeviceStream:
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ws = {}
         self.n_leaves = n_leaves
+        self.source = getattr(self, "source", "repack")  # "repack" or "file" (uploaded by from_buffers)
+
+    def with_perms(self, row_perm, col_perm) -> "DeviceStream":
+        """The same packed stream (buffers shared, nothing repacked) with other
+        row / column permutations (numpy int arrays or None), e.g. after
+        folding a permutation into a neighbouring layer."""
+        import copy
+
+        new = copy.copy(self)
+        new.desc = _lib.StreamDesc.from_buffer_copy(self.desc)
+        dev = self.device
+        with torch.cuda.device(dev):
+            new.row_perm = None if row_perm is None else torch.from_numpy(
+                np.asarray(row_perm, dtype=np.int32)).to(dev)
+            new.col_perm = None if col_perm is None else torch.from_numpy(
+                np.asarray(col_perm, dtype=np.int32)).to(dev)
+            new.col_perm_inv = None
+            if col_perm is not None:
+                inv = np.empty(self.N, dtype=np.int32)
+                inv[np.asarray(col_perm)] = np.arange(self.N, dtype=np.int32)
+                new.col_perm_inv = torch.from_numpy(inv).to(dev)
+            new.counters = torch.zeros_like(self.counters)
+            new.decode_counters = torch.zeros_like(self.decode_counters)
+            new.status = torch.zeros_like(self.status)
+        new._ws = {}
+        return new
 
     # ------------------------------------------------------------------ saving / loading
     def export_buffers(self):
@@ -182,6 +229,7 @@ class DeviceStream:
         _lib.load()
         check_stream_buffers(meta, arrs)
         self = cls.__new__(cls)
+        self.source = "file"
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError(f"DeviceStream needs a CUDA device, got {self.device}")
@@ -243,8 +291,9 @@ class DeviceStream:
                                 _stream(self.device)), "gemv")
         return Y
 
-    def decode(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
-        """Y[:M] = X @ W for M <= 16 (tensor-core decode kernel)."""
+    def decode(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
+        """Y[:M] = X @ W for M <= 16 (tensor-core decode kernel); ``ep`` from
+        ``epilogue()`` fuses a bias and activation into the output."""
         lib = _lib.load()
         M = X.shape[0]
         need = int(lib.mtc_decode_workspace_bytes(ctypes.byref(self.desc), M))
@@ -254,8 +303,8 @@ class DeviceStream:
             self._ws["decode"] = ws
         _lib.check(lib.mtc_decode(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
                                   _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), ws.data_ptr(), ws.numel(),
-                                  self.decode_counters.data_ptr(), self.status.data_ptr(), _stream(self.device)),
-                   "decode")
+                                  self.decode_counters.data_ptr(), self.status.data_ptr(), _ep(ep),
+                                  _stream(self.device)), "decode")
         return Y
 
     def prefill_workspace(self, M: int) -> torch.Tensor:
@@ -268,14 +317,15 @@ class DeviceStream:
             self._ws["prefill"] = ws
         return ws
 
-    def prefill(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
+    def prefill(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
         """Y = X @ W for any M (fused dequant + tcgen05 kernel; used for M > 16)."""
         lib = _lib.load()
         M = X.shape[0]
         ws = self.prefill_workspace(M)
         _lib.check(lib.mtc_gemm_prefill(ctypes.byref(self.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
                                         _ptr(self.col_perm_inv), Y.data_ptr(), Y.stride(0), ws.data_ptr(),
-                                        ws.numel(), self.status.data_ptr(), _stream(self.device)), "prefill")
+                                        ws.numel(), self.status.data_ptr(), _ep(ep), _stream(self.device)),
+                   "prefill")
         return Y
 
     # The three prefill stages, for callers that time or fuse them separately.
@@ -286,29 +336,29 @@ class DeviceStream:
                                           _ptr(self.row_perm), ws.data_ptr(), ws.numel(), self.status.data_ptr(),
                                           _stream(self.device)), "prefill gather")
 
-    def prefill_gemm(self, M: int, Y: torch.Tensor):
+    def prefill_gemm(self, M: int, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None):
         lib = _lib.load()
         ws = self.prefill_workspace(M)
         permuted = 1 if self.col_perm_inv is not None else 0
         _lib.check(lib.mtc_prefill_gemm(ctypes.byref(self.desc), M, Y.data_ptr(), Y.stride(0), permuted,
-                                        ws.data_ptr(), ws.numel(), self.status.data_ptr(), _stream(self.device)),
-                   "prefill gemm")
+                                        ws.data_ptr(), ws.numel(), self.status.data_ptr(),
+                                        None if permuted else _ep(ep), _stream(self.device)), "prefill gemm")
 
-    def prefill_scatter(self, M: int, Y: torch.Tensor):
+    def prefill_scatter(self, M: int, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None):
         if self.col_perm_inv is None:
             return
         lib = _lib.load()
         ws = self.prefill_workspace(M)
         _lib.check(lib.mtc_prefill_scatter(ctypes.byref(self.desc), M, self.col_perm_inv.data_ptr(), Y.data_ptr(),
-                                           Y.stride(0), ws.data_ptr(), ws.numel(), _stream(self.device)),
+                                           Y.stride(0), ws.data_ptr(), ws.numel(), _ep(ep), _stream(self.device)),
                    "prefill scatter")
 
-    def matmul(self, X: torch.Tensor, Y: torch.Tensor) -> torch.Tensor:
-        """Y = X @ W, picking the decode kernel for M <= 16 and the tensor-core
-        prefill kernel above."""
+    def matmul(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
+        """Y = X @ W (+ the fused epilogue ``ep``), picking the decode kernel
+        for M <= 16 and the tensor-core prefill kernel above."""
         if X.shape[0] <= DECODE_MAX_M:
-            return self.decode(X, Y)
-        return self.prefill(X, Y)
+            return self.decode(X, Y, ep)
+        return self.prefill(X, Y, ep)
 
     def check_status(self):
         """Raise if a kernel reported a runtime problem (synchronises)."""

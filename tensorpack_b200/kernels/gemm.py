@@ -301,6 +301,35 @@ def gemm_into(X, W: MTCMatrix, Y):
     return W.device_stream(X.device).matmul(X, Y)
 
 
+def gemm_fused(X, W: MTCMatrix, bias=None, activation: Optional[str] = None, Y=None):
+    """Y = act(X @ W + bias) with the bias add and activation fused into the
+    kernel that writes Y (the decode reduction, the prefill epilogue or the
+    column scatter of a permuted matrix): one pass over the output.
+
+    X: (M, K) CUDA tensor (fp32, or converted); bias: None or N floats (numpy
+    or tensor) in the column order of Y; activation: None, "relu", "silu" or
+    "gelu_tanh".  Returns Y (CUDA fp32)."""
+    import torch
+
+    from .device import epilogue
+
+    dev = X.device if isinstance(X, torch.Tensor) else torch.device("cuda", torch.cuda.current_device())
+    Xd, _ = _as_cuda_f32(X, dev)
+    M, K = Xd.shape
+    K2, N = W.shape
+    assert K == K2, f"Shape mismatch: {tuple(Xd.shape)} vs {W.shape}"
+    b = None
+    if bias is not None:
+        b = torch.as_tensor(bias, dtype=torch.float32, device=dev).reshape(-1).contiguous()
+        if b.numel() != N:
+            raise ValueError(f"bias has {b.numel()} values, the output {N} columns")
+    if Y is None:
+        Y = torch.empty(M, N, dtype=torch.float32, device=dev)
+    if M:
+        W.device_stream(dev).matmul(Xd, Y, epilogue(b, activation))
+    return Y
+
+
 def mtc_gemm(A, B):
     """GEMM with a packed right operand (gemm.py:541-574).
 

@@ -16,13 +16,28 @@ import numpy as np
 import torch
 
 from ..core.arena import MemoryArena
-from ..kernels.gemm import MTCMatrix, mtc_gemm
+from ..kernels.gemm import MTCMatrix, gemm_fused, mtc_gemm
+
+_NP_ACT = {
+    None: lambda y: y,
+    "relu": lambda y: np.where(y < 0, np.float32(0), y),
+    "silu": lambda y: y / (np.float32(1) + np.exp(-y)),
+    "gelu_tanh": lambda y: np.float32(0.5) * y * (np.float32(1) + np.tanh(
+        np.float32(0.7978845608028654) * (y + np.float32(0.044715) * y * y * y))),
+}
 
 
 class LinearMTCAdaptive(torch.nn.Module):
+    """``activation`` (None, "relu", "silu", "gelu_tanh") is applied after the
+    bias, fused into the GEMM's output pass on the GPU."""
+
     def __init__(self, in_features: int, out_features: int, block_size: int = 16, epsilon: float = 0.05,
-                 seed: int = 42, *, W_mtc: Optional[MTCMatrix] = None, bias: Optional[np.ndarray] = None):
+                 seed: int = 42, *, W_mtc: Optional[MTCMatrix] = None, bias: Optional[np.ndarray] = None,
+                 activation: Optional[str] = None):
         super().__init__()
+        if activation not in _NP_ACT:
+            raise ValueError(f"unknown activation {activation!r}")
+        self.activation = activation
         self.block_size = block_size
         self.in_features = in_features
         self.out_features = out_features
@@ -42,10 +57,11 @@ class LinearMTCAdaptive(torch.nn.Module):
         self._bias_dev = {}
 
     @classmethod
-    def from_mtc(cls, W_mtc: MTCMatrix, bias: Optional[np.ndarray] = None) -> "LinearMTCAdaptive":
+    def from_mtc(cls, W_mtc: MTCMatrix, bias: Optional[np.ndarray] = None,
+                 activation: Optional[str] = None) -> "LinearMTCAdaptive":
         """Wrap an already packed matrix (e.g. from ``MTCMatrix.from_qt_allocation``)."""
         K, N = W_mtc.shape
-        return cls(K, N, block_size=W_mtc.block_size, W_mtc=W_mtc, bias=bias)
+        return cls(K, N, block_size=W_mtc.block_size, W_mtc=W_mtc, bias=bias, activation=activation)
 
     @property
     def weight_bytes(self) -> int:
@@ -53,11 +69,24 @@ class LinearMTCAdaptive(torch.nn.Module):
 
     def forward(self, X):
         if isinstance(X, np.ndarray):
-            return mtc_gemm(X, self.W_mtc) + self.b
-        Y = mtc_gemm(X, self.W_mtc)
-        key = str(Y.device)
+            return _NP_ACT[self.activation](mtc_gemm(X, self.W_mtc) + self.b)
+        if X.device.type != "cuda":
+            raise ValueError("LinearMTCAdaptive: activations must be a CUDA tensor (no CPU path)")
+        key = str(X.device)
         bd = self._bias_dev.get(key)
         if bd is None:
-            bd = torch.from_numpy(self.b).to(Y.device)
+            bd = torch.from_numpy(self.b).to(X.device)
             self._bias_dev[key] = bd
-        return Y.add_(bd)
+        return gemm_fused(X, self.W_mtc, bd, self.activation)
+
+
+def fold_layers(a: LinearMTCAdaptive, b: LinearMTCAdaptive):
+    """(a', b') computing b(a(X)) with a's output left in its stored column
+    order and b's input permutation absorbing it (tensorpack_b200.kernels.
+    fold): no column scatter after a, and a' outputs act(Y_a)[:, pc_a]."""
+    from ..kernels.fold import fold_permutation
+
+    wa, wb = fold_permutation(a.W_mtc, b.W_mtc)
+    pc = a.W_mtc.col_perm
+    bias_a = a.b if pc is None else a.b[np.asarray(pc)]
+    return (LinearMTCAdaptive.from_mtc(wa, bias_a, a.activation), LinearMTCAdaptive.from_mtc(wb, b.b, b.activation))

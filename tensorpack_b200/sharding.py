@@ -137,6 +137,6 @@ class ShardedMTCMatrix:
             Y = torch.empty(M, self.N, dtype=torch.float32, device=self.device)
         lib = _lib.load()
         _lib.check(lib.mtc_permute_rows(src.data_ptr(), M * wmax, wmax, self.world, wmax, self.pos.data_ptr(),
-                                        self.N, M, Y.data_ptr(), Y.stride(0),
+                                        self.N, M, Y.data_ptr(), Y.stride(0), None,
                                         torch.cuda.current_stream(self.device).cuda_stream), "shard assembly")
         return Y

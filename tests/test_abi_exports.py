@@ -35,7 +35,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_error_text(lib):
-    assert lib.mtc_abi_version() == 1
+    assert lib.mtc_abi_version() == 2
     assert isinstance(lib.mtc_last_error(), bytes)
 
 

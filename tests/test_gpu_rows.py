@@ -44,7 +44,7 @@ def permute(dev, segs, pos, M, ldy, seg_stride, ldp, seg_len):
     Y = torch.full((M, ldy), -7.0, dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(lib.mtc_permute_rows(src.data_ptr(), seg_stride, ldp, segs.shape[0], seg_len, p.data_ptr(), N, M,
-                                    Y.data_ptr(), ldy, st), "permute_rows")
+                                    Y.data_ptr(), ldy, None, st), "permute_rows")
     torch.cuda.synchronize()
     return Y.cpu().numpy()
 
