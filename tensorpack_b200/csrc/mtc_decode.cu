@@ -8,20 +8,30 @@
 // x X^T tile (16 tokens x 64 k, fp16, TMA).  The SMs' issue slots go to the
 // dequantisation alone.
 //
-//  * work unit = (half band: 4 tiles = 128 features, range of k stages of
-//    64); persistent CTAs, one per SM, take units u = blockIdx.x, + grid, ...
-//  * warp roles (as in the prefill kernel):
+//  * work unit = (half band: 4 tiles = 128 features, range of at most 16
+//    k stages of 64); persistent CTAs, one per SM, take units
+//    u = blockIdx.x, + grid, ...
+//  * warp roles:
 //      warps 0-3  epilogue: TMEM -> partial sums of the unit -> workspace;
 //                 the last unit of a half band (atomic ticket) reduces the
 //                 partials in a fixed order and scatters Y[:, pc]
-//      warp  4    X producer: TMA of the Xp tile of each stage
-//      warp  5    TMEM allocator + single-thread tcgen05.mma issuer
-//      warp  6    packed producer: sub-stage descriptors, work list and
-//                 records into a shared-memory byte ring (cp.async.bulk)
-//      warps 7-22 dequant, two groups taking alternate stages
-//                 (dequant_substage, shared with the prefill)
-//  * two TMEM accumulators (32 columns each) alternate between units, so a
-//    unit's epilogue overlaps the next unit's MMAs.
+//      warp  4    X producer: TMA of all of a unit's X tiles at once, into
+//                 one of two unit buffers
+//      warp  5    packed producer: sub-stage images into a shared-memory
+//                 byte ring (cp.async.bulk)
+//      warps 6-7  MMA issuers, one per dequant group: when the group's
+//                 eight warps have written a W tile (mbarrier), one thread
+//                 issues that stage's four MMAs into the group's own
+//                 accumulator and commits them to the W buffer's release
+//                 barrier
+//      warps 8-23 dequant, two groups of eight; group g takes the stages
+//                 j = g, g + 2, ... of each unit (dequant_substage, shared
+//                 with the prefill).  A warp never waits for the other
+//                 warps of its group except through the W buffers (two per
+//                 group), so per-stage differences between warps average
+//                 out instead of adding up.
+//  * accumulators: 2 units in flight x 2 groups x 16 columns; the epilogue
+//    adds the two groups' partial products of a unit.
 // Every mbarrier wait is bounded; a timeout sets MTC_STATUS_TIMEOUT.
 #include "mtc_common.cuh"
 #include "mtc_internal.h"
@@ -36,21 +46,20 @@ constexpr int BK = 64;          // K per stage (two k-tile rows)
 constexpr int kFeat = 128;      // features per unit (MMA M)
 constexpr int kEpiWarps = 4;
 constexpr int kXWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kPackWarp = 6;
-constexpr int kDeqWarp0 = 7;
+constexpr int kPackWarp = 5;
+constexpr int kIssWarp0 = 6;
+constexpr int kDeqWarp0 = 8;
 constexpr int kDeqWarps = kSubWarps;
-#ifndef MTC_DECODE_GROUPS
-#define MTC_DECODE_GROUPS 2
-#endif
-constexpr int kDeqGroups = MTC_DECODE_GROUPS;
+constexpr int kDeqGroups = 2;
 constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
 constexpr uint32_t kXBytes = kTok * BK * 2;     // 2 KB
 constexpr uint32_t kWBytes = kFeat * BK * 2;    // 16 KB
-constexpr int kMaxS = 16;
+constexpr int kMaxR = 16;                       // stages per unit at most
+constexpr int kWBufs = 2;                       // W tiles per group
 constexpr int kRingSlots = 16;
 constexpr int kMetaChunk = 32;
-constexpr uint32_t kTmemCols = 64;              // two accumulators of 32 columns
+constexpr uint32_t kTmemCols = 64;              // [unit buffer d][group g] -> column 32 d + 16 g
+constexpr int kEpiBar = 1;                      // named barrier of the epilogue warps
 
 struct DecodeParams {
   mtc_stream_desc s;
@@ -62,7 +71,6 @@ struct DecodeParams {
   uint32_t* counters;  // [half bands] tickets, zero between calls
   uint32_t* status;
   int n_hb, nkb, n_kr, R, n_units;
-  int SX, SW;
   uint32_t x_box_bytes;  // bytes one X load brings: 64 k x M rows (rows M..15 of the tile are never read back)
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
@@ -74,56 +82,68 @@ __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
   if (st) atomicOr(st, bits);
 }
 
+// AND of `v` over the `n` threads meeting at named barrier `id` (all of them
+// take part, so the group decides together whether to go on).
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_x, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sX = smem;                               // [SX][2 KB], 1024-byte aligned
-  uint8_t* sW = sX + ((p.SX * kXBytes + 1023u) & ~1023u);  // [SW][16 KB]
-  uint8_t* sP = sW + p.SW * kWBytes;                // packed byte ring
+  uint8_t* sX = smem;                                         // [2][kMaxR][2 KB], 1024-byte aligned
+  uint8_t* sW = sX + 2 * kMaxR * kXBytes;                     // [2 groups][kWBufs][16 KB]
+  uint8_t* sP = sW + kDeqGroups * kWBufs * kWBytes;           // packed byte ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
-  uint64_t* full_x = bars;
-  uint64_t* empty_x = full_x + kMaxS;
-  uint64_t* full_w = empty_x + kMaxS;
-  uint64_t* empty_w = full_w + kMaxS;
-  uint64_t* pfull = empty_w + kMaxS;
+  uint64_t* x_full = bars;                                    // [2]
+  uint64_t* w_empty = x_full + 2;                             // [groups * kWBufs]
+  uint64_t* w_full = w_empty + kDeqGroups * kWBufs;           // [groups * kWBufs]
+  uint64_t* pfull = w_full + kDeqGroups * kWBufs;             // [kRingSlots]
   uint64_t* pempty = pfull + kRingSlots;
-  uint64_t* acc_full = pempty + kRingSlots;         // [2]
-  uint64_t* acc_empty = acc_full + 2;               // [2]
-  uint64_t* drain = acc_empty + 2;
-  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + 1);  // [0] abort, [1] last unit
+  uint64_t* acc_full = pempty + kRingSlots;                   // [2]
+  uint64_t* acc_empty = acc_full + 2;                         // [2]
+  uint64_t* drain = acc_empty + 2;                            // [groups]
+  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + kDeqGroups);  // [0] abort, [1] last unit
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
-  uint32_t* pmeta = tmem_slot + 4;                  // [kRingSlots][4]
+  uint32_t* pmeta = tmem_slot + 4;                            // [kRingSlots][4]
   uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1280);
   uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1792);  // [2][kMetaChunk][2]
-  static_assert((4 * kMaxS + 2 * kRingSlots + 5) * 8 + 32 + 16 * kRingSlots <= 1280, "barrier region");
+  static_assert((2 + 2 * kDeqGroups * kWBufs + 2 * kRingSlots + 4 + kDeqGroups) * 8 + 32 + 16 * kRingSlots <= 1280,
+                "barrier region");
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < p.SX; ++i) {
-      mbar_init(&full_x[i], 1);
-      mbar_init(&empty_x[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&acc_full[i], kDeqGroups);  // one commit (or arrive) per group
+      mbar_init(&acc_empty[i], kEpiWarps);
     }
-    for (int i = 0; i < p.SW; ++i) {
-      mbar_init(&full_w[i], kDeqWarps);
-      mbar_init(&empty_w[i], 1);
+    for (int i = 0; i < kDeqGroups * kWBufs; ++i) {
+      mbar_init(&w_empty[i], 1);
+      mbar_init(&w_full[i], kDeqWarps);
     }
     for (int i = 0; i < kRingSlots; ++i) {
       mbar_init(&pfull[i], 1);
       mbar_init(&pempty[i], kDeqWarps);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiWarps);
-    }
-    mbar_init(drain, 1);
+    for (int i = 0; i < kDeqGroups; ++i) mbar_init(&drain[i], 1);
     flags[0] = 0;
     fence_barrier_init();
   }
-  if (warp == 0) load_dec_table(dtab, lane);
-  if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) load_dec_table(dtab, lane);
+  if (warp == 0) tc::tmem_alloc(tmem_slot, kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -138,27 +158,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kXWarp) {
     // ---------------------------------------------------------------- X producer
+    // All X tiles of a unit in one go, into unit buffer d = ucount & 1 once
+    // the unit two back (same buffer) has finished its MMAs.
     if (lane == 0) {
-      uint32_t it = 0;
-      for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x) {
+      uint32_t ucount = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ucount) {
         int hb, kb0, kb1;
         unit_range(u, hb, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int sx = it % p.SX;
-          if (it >= (uint32_t)p.SX && !mbar_wait(&empty_x[sx], ((it / p.SX) & 1) ^ 1, p.timeout_ns)) {
-            flags[0] = 1;
-            break;
-          }
-          if (flags[0]) break;
-          mbar_expect_tx(&full_x[sx], p.x_box_bytes);
-          tc::tma_load_2d(sX + sx * kXBytes, &tmap_x, kb * BK, 0, &full_x[sx]);
+        const int d = ucount & 1;
+        if (ucount >= 2 && !mbar_wait(&acc_full[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
+          ok = false;
+          break;
         }
+        if (flags[0]) break;
+        mbar_expect_tx(&x_full[d], (uint32_t)(kb1 - kb0) * p.x_box_bytes);
+        for (int kb = kb0; kb < kb1; ++kb)
+          tc::tma_load_2d(sX + (d * kMaxR + (kb - kb0)) * kXBytes, &tmap_x, kb * BK, 0, &x_full[d]);
       }
-      if (flags[0]) {
-        for (uint32_t j = it > (uint32_t)p.SX ? it - p.SX : 0u; j < it; ++j)
-          (void)mbar_wait(&full_x[j % p.SX], (j / p.SX) & 1, 10000000ull);
+      if (!ok) {
+        flags[0] = 1;
         flag(p.status, MTC_STATUS_TIMEOUT);
       }
+      // let the last loads land before the CTA can exit
+      for (uint32_t q = ucount > 2 ? ucount - 2 : 0u; q < ucount; ++q)
+        (void)mbar_wait(&x_full[q & 1], (q >> 1) & 1, 10000000ull);
     }
   } else if (warp == kPackWarp) {
     // ---------------------------------------------------------------- packed producer
@@ -255,90 +279,112 @@ __global__ void __launch_bounds__(kThreads, 1)
         (void)mbar_wait(&pfull[j % kRingSlots], (j / kRingSlots) & 1, 10000000ull);
       flag(p.status, MTC_STATUS_TIMEOUT);
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16_f32(kFeat, kTok);
-      uint32_t it = 0, ucount = 0;
-      for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x, ++ucount) {
-        int hb, kb0, kb1;
-        unit_range(u, hb, kb0, kb1);
-        const int d = ucount & 1;
-        if (ucount >= 2 && !mbar_wait(&acc_empty[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
-          flags[0] = 1;
-          break;
-        }
-        tc::fence_after();
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int sx = it % p.SX, sw = it % p.SW;
-          if (!mbar_wait(&full_x[sx], (it / p.SX) & 1, p.timeout_ns) ||
-              !mbar_wait(&full_w[sw], (it / p.SW) & 1, p.timeout_ns)) {
-            flags[0] = 1;
-            break;
-          }
-          tc::fence_after();
-          const uint32_t w0 = smem_u32(sW + sw * kWBytes);
-          const uint32_t x0 = smem_u32(sX + sx * kXBytes);
-#pragma unroll
-          for (int j = 0; j < BK / 16; ++j)
-            tc::mma_f16_ss(tmem + 32u * d, tc::smem_desc_k_sw128(w0 + 32 * j), tc::smem_desc_k_sw128(x0 + 32 * j),
-                           idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-          tc::commit(&empty_x[sx]);
-          tc::commit(&empty_w[sw]);
-        }
-        if (flags[0]) break;
-        tc::commit(&acc_full[d]);
-      }
-      tc::commit(drain);
-      (void)mbar_wait(drain, 0, 100000000ull);
-      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
-    }
   } else if (warp >= kDeqWarp0) {
     // ---------------------------------------------------------------- dequant
     const int grp = (warp - kDeqWarp0) / kDeqWarps;
     const int dw = (warp - kDeqWarp0) % kDeqWarps;
-    uint32_t it = 0;
-    for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x) {
+    uint32_t it = 0, sg = 0;
+    bool go = true;
+    for (int u = blockIdx.x; u < p.n_units && go; u += gridDim.x) {
       int hb, kb0, kb1;
       unit_range(u, hb, kb0, kb1);
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        if ((int)(it % kDeqGroups) != grp) continue;
-        const int sw = it % p.SW, ps = it % kRingSlots;
-        if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
+      const int L = kb1 - kb0;
+      for (int j = 0; j < L; ++j, ++it) {
+        if ((j & 1) != grp) continue;
+        const int kb = kb0 + j;
+        const int b = grp * kWBufs + (sg & 1);
+        const int ps = it % kRingSlots;
+        bool ok = !flags[0] && mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
+        if (ok && sg >= (uint32_t)kWBufs) ok = mbar_wait(&w_empty[b], ((sg >> 1) - 1) & 1, p.timeout_ns);
+        ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the dequant uses whole-warp shuffles
+        if (!ok) {
           flags[0] = 1;
+          go = false;
           break;
         }
-        if (it >= (uint32_t)p.SW && !mbar_wait(&empty_w[sw], ((it / p.SW) & 1) ^ 1, p.timeout_ns)) {
-          flags[0] = 1;
-          break;
-        }
-        dequant_substage(sW + sw * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
+        dequant_substage(sW + b * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
                          pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
-                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32);
+                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32, (int)(sg * 3u));
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full_w[sw]);
           mbar_arrive(&pempty[ps]);
+          mbar_arrive(&w_full[b]);
         }
+        ++sg;
       }
+    }
+  } else if (warp >= kIssWarp0) {
+    // ---------------------------------------------------------------- MMA issuers
+    const int grp = warp - kIssWarp0;
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16_f32(kFeat, kTok);
+      uint32_t sg = 0, ucount = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ucount) {
+        int hb, kb0, kb1;
+        unit_range(u, hb, kb0, kb1);
+        const int L = kb1 - kb0, d = ucount & 1;
+        // the accumulator (and X buffer) of the unit two back must be free
+        if (ucount >= 2 && !mbar_wait(&acc_empty[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        if (L <= grp) {
+          mbar_arrive(&acc_full[d]);  // no stage of this unit: the accumulator is not read
+          continue;
+        }
+        if (!mbar_wait(&x_full[d], (ucount >> 1) & 1, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const uint32_t acc = tmem + 32u * d + 16u * grp;
+        for (int j = grp; j < L; j += 2, ++sg) {
+          const int b = grp * kWBufs + (sg & 1);
+          if (flags[0] || !mbar_wait(&w_full[b], (sg >> 1) & 1, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t w0 = smem_u32(sW + b * kWBytes);
+          const uint32_t x0 = smem_u32(sX + (d * kMaxR + j) * kXBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::mma_f16_ss(acc, tc::smem_desc_k_sw128(w0 + 32 * kk), tc::smem_desc_k_sw128(x0 + 32 * kk), idesc,
+                           (j > grp || kk > 0) ? 1u : 0u);
+          tc::commit(&w_empty[b]);
+        }
+        if (!ok) break;
+        tc::commit(&acc_full[d]);
+      }
+      if (!ok) flags[0] = 1;
+      tc::commit(&drain[grp]);
+      (void)mbar_wait(&drain[grp], 0, 100000000ull);
+      if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 0-3)
     // Thread (warp w, lane l) owns feature 32 w + l of the unit.
     const int f = 32 * warp + lane;
     uint32_t ucount = 0;
-    for (int u = blockIdx.x; u < p.n_units && !flags[0]; u += gridDim.x, ++ucount) {
+    for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ucount) {
       int hb, kb0, kb1;
       unit_range(u, hb, kb0, kb1);
       const int d = ucount & 1;
-      if (!mbar_wait(&acc_full[d], (ucount >> 1) & 1, p.timeout_ns)) {
+      const bool ok = !flags[0] && mbar_wait(&acc_full[d], (ucount >> 1) & 1, p.timeout_ns);
+      if (!bar_and(kEpiBar, kEpiWarps * 32, ok)) {
         flags[0] = 1;
         break;
       }
       tc::fence_after();
-      uint32_t v[16];
-      tc::tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * warp) << 16) + 32u * d, v);
+      uint32_t v[16], w[16];
+      const uint32_t row = tmem + ((uint32_t)(32 * warp) << 16) + 32u * d;
+      tc::tmem_ld_32x32b_x16(row, v);
+      if (kb1 - kb0 >= 2) {
+        tc::tmem_ld_32x32b_x16(row + 16u, w);
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) + __uint_as_float(w[t]));
+      }
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[d]);
@@ -348,9 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t < p.M) part[t * kFeat + f] = __uint_as_float(v[t]);
       // ticket: the last unit of the half band reduces in a fixed order
       __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(kEpiBar), "r"(kEpiWarps * 32) : "memory");
       if (tid == 0) flags[1] = atomicAdd(&p.counters[hb], 1u) == (uint32_t)(p.n_kr - 1) ? 1u : 0u;
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(kEpiBar), "r"(kEpiWarps * 32) : "memory");
       if (flags[1]) {
         __threadfence();
         const int n = hb * kFeat + f;
@@ -365,21 +411,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tid == 0) p.counters[hb] = 0u;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(kEpiBar), "r"(kEpiWarps * 32) : "memory");
     }
     if (flags[0]) flag(p.status, MTC_STATUS_TIMEOUT);
   }
 
   tc::fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == 0) {
     tc::fence_after();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 struct DecodePlan {
-  int Kp, nkb, n_hb, R, n_kr, n_units, SX, SW, grid;
+  int Kp, nkb, n_hb, R, n_kr, n_units, grid;
   uint32_t ring_bytes;
   size_t smem, xp_bytes, part_bytes;
 };
@@ -392,20 +438,17 @@ bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
   pl->n_hb = 2 * n_bands;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // about four units per SM, at least four stages each
+  // about four units per SM, four to kMaxR stages each
   const long long total = (long long)pl->n_hb * pl->nkb;
   long long R = (total + 4LL * sms - 1) / (4LL * sms);
-  R = R < 4 ? 4 : R;
+  R = R < 4 ? 4 : (R > kMaxR ? kMaxR : R);
   pl->R = (int)(R < pl->nkb ? R : pl->nkb);
   pl->n_kr = (pl->nkb + pl->R - 1) / pl->R;
   pl->n_units = pl->n_hb * pl->n_kr;
   pl->grid = pl->n_units < sms ? pl->n_units : sms;
-  pl->SX = 16;  // X loads queue behind the packed copies on the copy engine: keep them far ahead
-  pl->SW = 4;
   const size_t cap = 227 * 1024;
   const size_t fixed = 1024 /*align*/ + 1792 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
-  const size_t xb = ((size_t)pl->SX * kXBytes + 1023) & ~(size_t)1023;
-  const size_t used = fixed + xb + (size_t)pl->SW * kWBytes;
+  const size_t used = fixed + 2 * (size_t)kMaxR * kXBytes + (size_t)kDeqGroups * kWBufs * kWBytes;
   const size_t ring = (cap - used) & ~(size_t)127;
   if (s->max_stage_bytes == 0 || ring < s->max_stage_bytes) return false;
   pl->ring_bytes = (uint32_t)ring;
@@ -473,9 +516,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   p.n_kr = pl.n_kr;
   p.R = pl.R;
   p.n_units = pl.n_units;
-  p.SX = pl.SX;
   p.x_box_bytes = (uint32_t)(BK * 2 * M);
-  p.SW = pl.SW;
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);

@@ -326,17 +326,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.nkb; ++kb, ++it) {
         if ((int)(it % kDeqGroups) != grp) continue;  // the other group's stage
         const int sb = it % p.SB, ps = it % kRingSlots;
-        if (!mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns)) {
-          flags[0] = 1;
-          break;
-        }
-        if (it >= (uint32_t)p.SB && !mbar_wait(&empty_b[sb], ((it / p.SB) & 1) ^ 1, p.timeout_ns)) {
+        bool ok = mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
+        if (ok && it >= (uint32_t)p.SB) ok = mbar_wait(&empty_b[sb], ((it / p.SB) & 1) ^ 1, p.timeout_ns);
+        if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform: the dequant uses whole-warp shuffles
           flags[0] = 1;
           break;
         }
         dequant_substage(sB + sb * kBBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
                          pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
-                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32);
+                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32, (int)((it >> 1) * 3u));
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {

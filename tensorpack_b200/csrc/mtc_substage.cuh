@@ -15,16 +15,19 @@ namespace mtc {
 // The sub-stage's work list holds group entries (one 8x8 leaf group, 4
 // micro-blocks) and micro-block entries (split groups), each run sorted by
 // decode class.  Warp dw (of kSubWarps) takes an equal contiguous slice of
-// each run, so every warp does the same work: one pass over at most 16
-// group entries, then one micro-block entry per lane pair per pass; lane
-// pair (2e, 2e + 1) decodes the two column halves of its entry.  Sorted runs
+// the group run: one pass over at most 16 group entries, lane pair
+// (2e, 2e + 1) decoding the two column halves of its entry.  Sorted runs
 // make most warps mode-uniform, so they take one specialised path; the
-// others use the branch-free table decoder.
+// others use the branch-free table decoder.  Micro-block entries go one per
+// lane, 32 to a pass, to rotating warps.
 //   sl      staged sub-stage: [128 B descriptors][list (lbytes)][records]
 //   cnt     group entries | micro-block entries << 16
 //   part0   bytes of the row-0 records (the row-1 records follow)
 //   tid_d   thread index among the kSubWarps warps; zero_row1: the stage's
 //           second k-tile row lies beyond the matrix (zero it)
+//   rot     rotation of the micro-block chunks over the warps (any value
+//           that advances from one sub-stage to the next, the same for all
+//           warps of the group)
 constexpr int kSubWarps = 8;
 constexpr uint32_t kSubDescBytes = 128;
 constexpr int kClassGeneric = 7;
@@ -36,7 +39,8 @@ __device__ __forceinline__ uint32_t sw128_off(int n, int k) {
 
 __device__ __forceinline__ void dequant_substage(uint8_t* Bt, const uint8_t* sl, uint32_t cnt, uint32_t lbytes,
                                                  uint32_t part0, bool zero_row1, const uint32_t* dtab,
-                                                 int scale_words, float pow2e, int dw, int lane, int tid_d) {
+                                                 int scale_words, float pow2e, int dw, int lane, int tid_d,
+                                                 int rot) {
   const int h = lane & 1;
   const uint64_t* list = reinterpret_cast<const uint64_t*>(sl + kSubDescBytes);
   const uint8_t* payload = sl + kSubDescBytes + lbytes;
@@ -100,41 +104,53 @@ __device__ __forceinline__ void dequant_substage(uint8_t* Bt, const uint8_t* sl,
       }
     }
   }
-  // ---- micro-block entries (split groups): each warp takes an equal
-  // contiguous slice, one entry per lane pair per pass.  P0..P8 go through
-  // the branch-free table decoder; generic entries (P16, inexact fp16
-  // scales) through a per-lane path when present ----
+  // ---- micro-block entries (split groups): one entry (both column halves)
+  // per lane, in chunks of 32.  Chunk c goes to warp (c + rot) mod 8: most
+  // sub-stages have one or two chunks, so only those warps make a pass, and
+  // the rotation spreads the passes evenly over the warps across
+  // consecutive sub-stages.  P0..P8 go through the branch-free table
+  // decoder; generic entries (P16, inexact fp16 scales) through a per-lane
+  // path when present ----
   {
-    const int m0 = (dw * n_mb) / kSubWarps, m1 = ((dw + 1) * n_mb) / kSubWarps;
+    const int n_chunks = (n_mb + 31) >> 5;
 #pragma unroll 1
-    for (int base = m0; base < m1; base += 16) {  // warp-uniform
-      const int j = base + pair;
-      const bool ok = j < m1;
+    for (int c = (dw - rot) & (kSubWarps - 1); c < n_chunks; c += kSubWarps) {  // warp-uniform
+      const int j = 32 * c + lane;
+      const bool ok = j < n_mb;
       const uint64_t e = ok ? list[n_group + j] : 0ull;
       const int cls = (int)((e >> 48) & 15u);
       const bool dec = ok && cls != kClassGeneric;
       const uint64_t ed = dec ? e : 0ull;
-      uint32_t r[4];
-      decode_half_class(dtab, dec ? cls : 0, payload + (uint32_t)(ed & 0xffffu),
-                        payload + (uint32_t)((ed >> 16) & 0xffffu), h, h2const((uint16_t)((ed >> 32) & 0xffffu)), r);
+      const uint8_t* prim = payload + (uint32_t)(ed & 0xffffu);
+      const uint8_t* sec = payload + (uint32_t)((ed >> 16) & 0xffffu);
+      const uint32_t s2 = h2const((uint16_t)((ed >> 32) & 0xffffu));
+      uint32_t r0[4], r1[4];
+      decode_half_class(dtab, dec ? cls : 0, prim, sec, 0, s2, r0);
+      decode_half_class(dtab, dec ? cls : 0, prim, sec, 1, s2, r1);
       const bool gen = ok && cls == kClassGeneric;
+      const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
       if (__any_sync(0xffffffffu, gen) && gen) {
-        const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
         const uint32_t* ltab = reinterpret_cast<const uint32_t*>(tile_record(ti));
         const int L = leaf_of(descs[ti].leaf_start, 4 * G + mk);
-        decode_half_w16(lt_entry(ltab, L, scale_words), lt_scale_of(ltab, L, scale_words),
-                        payload + (uint32_t)(e & 0xffffu), payload + (uint32_t)((e >> 16) & 0xffffu), h, pow2e, r);
+        const uint32_t le = lt_entry(ltab, L, scale_words);
+        const float ls = lt_scale_of(ltab, L, scale_words);
+        const uint8_t* gp = payload + (uint32_t)(e & 0xffffu);
+        const uint8_t* gs = payload + (uint32_t)((e >> 16) & 0xffffu);
+        decode_half_w16(le, ls, gp, gs, 0, pow2e, r0);
+        decode_half_w16(le, ls, gp, gs, 1, pow2e, r1);
       }
       if (ok) {
-        // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1
-        const int ti = (int)((e >> 52) & 15u), G = (int)((e >> 56) & 15u), mk = (int)((e >> 60) & 3u);
+        // micro-block (2t + di, 2jj + dj) of group G, di = mk >> 1, dj = mk & 1;
+        // half 0 holds features f, f + 1, half 1 features f + 2, f + 3
         const int rr = ti >> 2, col = ti & 3;
         const int t = ((G >> 3) & 1) << 1 | ((G >> 1) & 1);
         const int jj = ((G >> 2) & 1) << 1 | (G & 1);
-        const int f = 32 * col + 4 * (2 * jj + (mk & 1)) + 2 * h;
+        const int f = 32 * col + 4 * (2 * jj + (mk & 1));
         const int k0 = 32 * rr + 8 * t + 4 * (mk >> 1);
-        *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r[0], r[1]);
-        *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r[2], r[3]);
+        *reinterpret_cast<uint2*>(Bt + sw128_off(f, k0)) = make_uint2(r0[0], r0[1]);
+        *reinterpret_cast<uint2*>(Bt + sw128_off(f + 1, k0)) = make_uint2(r0[2], r0[3]);
+        *reinterpret_cast<uint2*>(Bt + sw128_off(f + 2, k0)) = make_uint2(r1[0], r1[1]);
+        *reinterpret_cast<uint2*>(Bt + sw128_off(f + 3, k0)) = make_uint2(r1[2], r1[3]);
       }
     }
   }
