@@ -8,28 +8,27 @@
 // x X^T tile (16 tokens x 64 k, fp16, TMA).  The SMs' issue slots go to the
 // dequantisation alone.
 //
-//  * work unit = (half band: 4 tiles = 128 features, range of at most 16
-//    k stages of 64); persistent CTAs, one per SM, take units
-//    u = blockIdx.x, + grid, ...
+//  * work unit = (half band: 4 tiles = 128 features, range of k stages of
+//    64); persistent CTAs, one per SM, take units u = blockIdx.x, + grid, ...
+//    The stages of a unit go in pairs (2p, 2p + 1) to the two dequant
+//    groups in turn: pair p to group p mod 2.
 //  * warp roles:
 //      warps 0-3  epilogue: TMEM -> partial sums of the unit -> workspace;
 //                 the last unit of a half band (atomic ticket) reduces the
 //                 partials in a fixed order and scatters Y[:, pc]
-//      warp  4    X producer: TMA of all of a unit's X tiles at once, into
-//                 one of two unit buffers
+//      warp  4    X producer: TMA of each stage's X tile into a ring
 //      warp  5    packed producer: sub-stage images into a shared-memory
 //                 byte ring (cp.async.bulk)
 //      warps 6-7  MMA issuers, one per dequant group: when the group's
-//                 eight warps have written a W tile (mbarrier), one thread
-//                 issues that stage's four MMAs into the group's own
-//                 accumulator and commits them to the W buffer's release
-//                 barrier
-//      warps 8-23 dequant, two groups of eight; group g takes the stages
-//                 j = g, g + 2, ... of each unit (dequant_substage, shared
+//                 eight warps have written the two W tiles of a pair
+//                 (mbarrier), one thread issues the pair's eight MMAs into
+//                 the group's own accumulator and commits them to the W
+//                 buffer's release barrier
+//      warps 8-23 dequant, two groups of eight (dequant_substage, shared
 //                 with the prefill).  A warp never waits for the other
-//                 warps of its group except through the W buffers (two per
-//                 group), so per-stage differences between warps average
-//                 out instead of adding up.
+//                 warps of its group except through the W buffers (two
+//                 pairs per group), and it pays the waits, proxy fence and
+//                 arrivals once per pair of sub-stages.
 //  * accumulators: 2 units in flight x 2 groups x 16 columns; the epilogue
 //    adds the two groups' partial products of a unit.
 // Every mbarrier wait is bounded; a timeout sets MTC_STATUS_TIMEOUT.
@@ -54,8 +53,9 @@ constexpr int kDeqGroups = 2;
 constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
 constexpr uint32_t kXBytes = kTok * BK * 2;     // 2 KB
 constexpr uint32_t kWBytes = kFeat * BK * 2;    // 16 KB
-constexpr int kMaxR = 16;                       // stages per unit at most
-constexpr int kWBufs = 2;                       // W tiles per group
+constexpr int kMaxS = 16;                       // X ring slots
+constexpr int kWBufs = 2;                       // W buffers (two tiles each) per group
+constexpr uint32_t kWPair = 2 * kWBytes;
 constexpr int kRingSlots = 16;
 constexpr int kMetaChunk = 32;
 constexpr uint32_t kTmemCols = 64;              // [unit buffer d][group g] -> column 32 d + 16 g
@@ -101,12 +101,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_x, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sX = smem;                                         // [2][kMaxR][2 KB], 1024-byte aligned
-  uint8_t* sW = sX + 2 * kMaxR * kXBytes;                     // [2 groups][kWBufs][16 KB]
-  uint8_t* sP = sW + kDeqGroups * kWBufs * kWBytes;           // packed byte ring
+  uint8_t* sX = smem;                                         // [kMaxS][2 KB], 1024-byte aligned
+  uint8_t* sW = sX + kMaxS * kXBytes;                         // [2 groups][kWBufs][2][16 KB]
+  uint8_t* sP = sW + kDeqGroups * kWBufs * kWPair;            // packed byte ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
-  uint64_t* x_full = bars;                                    // [2]
-  uint64_t* w_empty = x_full + 2;                             // [groups * kWBufs]
+  uint64_t* x_full = bars;                                    // [kMaxS]
+  uint64_t* x_empty = x_full + kMaxS;                         // [kMaxS]
+  uint64_t* w_empty = x_empty + kMaxS;                        // [groups * kWBufs]
   uint64_t* w_full = w_empty + kDeqGroups * kWBufs;           // [groups * kWBufs]
   uint64_t* pfull = w_full + kDeqGroups * kWBufs;             // [kRingSlots]
   uint64_t* pempty = pfull + kRingSlots;
@@ -118,15 +119,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* pmeta = tmem_slot + 4;                            // [kRingSlots][4]
   uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1280);
   uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1792);  // [2][kMetaChunk][2]
-  static_assert((2 + 2 * kDeqGroups * kWBufs + 2 * kRingSlots + 4 + kDeqGroups) * 8 + 32 + 16 * kRingSlots <= 1280,
+  static_assert((2 * kMaxS + 2 * kDeqGroups * kWBufs + 2 * kRingSlots + 4 + kDeqGroups) * 8 + 32 + 16 * kRingSlots <=
+                    1280,
                 "barrier region");
 
   const mtc_stream_desc& s = p.s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kMaxS; ++i) {
       mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], kDeqGroups);  // one commit (or arrive) per group
       mbar_init(&acc_empty[i], kEpiWarps);
     }
@@ -158,31 +163,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kXWarp) {
     // ---------------------------------------------------------------- X producer
-    // All X tiles of a unit in one go, into unit buffer d = ucount & 1 once
-    // the unit two back (same buffer) has finished its MMAs.
+    // One TMA per stage into a ring of kMaxS tiles, released by the MMAs'
+    // commits; the loads run far ahead of the MMAs.
     if (lane == 0) {
-      uint32_t ucount = 0;
+      uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ucount) {
+      for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
         int hb, kb0, kb1;
         unit_range(u, hb, kb0, kb1);
-        const int d = ucount & 1;
-        if (ucount >= 2 && !mbar_wait(&acc_full[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
-          ok = false;
-          break;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int sx = it % kMaxS;
+          if (it >= (uint32_t)kMaxS && !mbar_wait(&x_empty[sx], ((it / kMaxS) & 1) ^ 1, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          if (flags[0]) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&x_full[sx], p.x_box_bytes);
+          tc::tma_load_2d(sX + sx * kXBytes, &tmap_x, kb * BK, 0, &x_full[sx]);
         }
-        if (flags[0]) break;
-        mbar_expect_tx(&x_full[d], (uint32_t)(kb1 - kb0) * p.x_box_bytes);
-        for (int kb = kb0; kb < kb1; ++kb)
-          tc::tma_load_2d(sX + (d * kMaxR + (kb - kb0)) * kXBytes, &tmap_x, kb * BK, 0, &x_full[d]);
       }
       if (!ok) {
         flags[0] = 1;
         flag(p.status, MTC_STATUS_TIMEOUT);
       }
-      // let the last loads land before the CTA can exit
-      for (uint32_t q = ucount > 2 ? ucount - 2 : 0u; q < ucount; ++q)
-        (void)mbar_wait(&x_full[q & 1], (q >> 1) & 1, 10000000ull);
+      // let the loads in flight land before the CTA can exit
+      for (uint32_t q = it > (uint32_t)kMaxS ? it - kMaxS : 0u; q < it; ++q)
+        (void)mbar_wait(&x_full[q % kMaxS], (q / kMaxS) & 1, 10000000ull);
     }
   } else if (warp == kPackWarp) {
     // ---------------------------------------------------------------- packed producer
@@ -283,75 +292,89 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- dequant
     const int grp = (warp - kDeqWarp0) / kDeqWarps;
     const int dw = (warp - kDeqWarp0) % kDeqWarps;
-    uint32_t it = 0, sg = 0;
+    uint32_t it0 = 0, sp = 0;
     bool go = true;
     for (int u = blockIdx.x; u < p.n_units && go; u += gridDim.x) {
       int hb, kb0, kb1;
       unit_range(u, hb, kb0, kb1);
       const int L = kb1 - kb0;
-      for (int j = 0; j < L; ++j, ++it) {
-        if ((j & 1) != grp) continue;
-        const int kb = kb0 + j;
-        const int b = grp * kWBufs + (sg & 1);
-        const int ps = it % kRingSlots;
-        bool ok = !flags[0] && mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
-        if (ok && sg >= (uint32_t)kWBufs) ok = mbar_wait(&w_empty[b], ((sg >> 1) - 1) & 1, p.timeout_ns);
-        ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the dequant uses whole-warp shuffles
+      for (int pr = grp; 2 * pr < L && go; pr += kDeqGroups, ++sp) {
+        const int b = grp * kWBufs + (sp & 1);
+        const int n = min(2, L - 2 * pr);
+        bool ok = !flags[0];
+        if (ok && sp >= (uint32_t)kWBufs) ok = mbar_wait(&w_empty[b], ((sp >> 1) - 1) & 1, p.timeout_ns);
+        for (int h = 0; h < n; ++h) {
+          const uint32_t it = it0 + 2 * pr + h;
+          const int ps = it % kRingSlots;
+          ok = ok && mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
+          ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the dequant uses whole-warp shuffles
+          if (!ok) break;
+          const int kb = kb0 + 2 * pr + h;
+          dequant_substage(sW + b * kWPair + h * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
+                           pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
+                           tid - (kDeqWarp0 + grp * kDeqWarps) * 32, (int)((2 * sp + h) * 3u));
+        }
         if (!ok) {
           flags[0] = 1;
           go = false;
           break;
         }
-        dequant_substage(sW + b * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
-                         pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
-                         tid - (kDeqWarp0 + grp * kDeqWarps) * 32, (int)(sg * 3u));
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&pempty[ps]);
+          for (int h = 0; h < n; ++h) mbar_arrive(&pempty[(it0 + 2 * pr + h) % kRingSlots]);
           mbar_arrive(&w_full[b]);
         }
-        ++sg;
       }
+      it0 += L;
     }
   } else if (warp >= kIssWarp0) {
     // ---------------------------------------------------------------- MMA issuers
     const int grp = warp - kIssWarp0;
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(kFeat, kTok);
-      uint32_t sg = 0, ucount = 0;
+      uint32_t sp = 0, ucount = 0, it0 = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ucount) {
         int hb, kb0, kb1;
         unit_range(u, hb, kb0, kb1);
         const int L = kb1 - kb0, d = ucount & 1;
-        // the accumulator (and X buffer) of the unit two back must be free
+        const uint32_t ubase = it0;
+        it0 += L;
+        // the accumulator of the unit two back must have been read out
         if (ucount >= 2 && !mbar_wait(&acc_empty[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
           ok = false;
           break;
         }
-        if (L <= grp) {
-          mbar_arrive(&acc_full[d]);  // no stage of this unit: the accumulator is not read
+        if (2 * grp >= L) {
+          mbar_arrive(&acc_full[d]);  // no pair of this unit: the accumulator is not read
           continue;
         }
-        if (!mbar_wait(&x_full[d], (ucount >> 1) & 1, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
         const uint32_t acc = tmem + 32u * d + 16u * grp;
-        for (int j = grp; j < L; j += 2, ++sg) {
-          const int b = grp * kWBufs + (sg & 1);
-          if (flags[0] || !mbar_wait(&w_full[b], (sg >> 1) & 1, p.timeout_ns)) {
+        for (int pr = grp; 2 * pr < L; pr += kDeqGroups, ++sp) {
+          const int b = grp * kWBufs + (sp & 1);
+          const int n = min(2, L - 2 * pr);
+          if (flags[0] || !mbar_wait(&w_full[b], (sp >> 1) & 1, p.timeout_ns)) {
             ok = false;
             break;
           }
-          tc::fence_after();
-          const uint32_t w0 = smem_u32(sW + b * kWBytes);
-          const uint32_t x0 = smem_u32(sX + (d * kMaxR + j) * kXBytes);
+          for (int h = 0; h < n; ++h) {
+            const uint32_t it = ubase + 2 * pr + h;
+            const int sx = it % kMaxS;
+            if (!mbar_wait(&x_full[sx], (it / kMaxS) & 1, p.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after();
+            const uint32_t w0 = smem_u32(sW + b * kWPair + h * kWBytes);
+            const uint32_t x0 = smem_u32(sX + sx * kXBytes);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_f16_ss(acc, tc::smem_desc_k_sw128(w0 + 32 * kk), tc::smem_desc_k_sw128(x0 + 32 * kk), idesc,
-                           (j > grp || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk)
+              tc::mma_f16_ss(acc, tc::smem_desc_k_sw128(w0 + 32 * kk), tc::smem_desc_k_sw128(x0 + 32 * kk), idesc,
+                             (pr > grp || h > 0 || kk > 0) ? 1u : 0u);
+            tc::commit(&x_empty[sx]);
+          }
+          if (!ok) break;
           tc::commit(&w_empty[b]);
         }
         if (!ok) break;
@@ -380,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t v[16], w[16];
       const uint32_t row = tmem + ((uint32_t)(32 * warp) << 16) + 32u * d;
       tc::tmem_ld_32x32b_x16(row, v);
-      if (kb1 - kb0 >= 2) {
+      if (kb1 - kb0 >= 3) {  // the second group has a pair in this unit
         tc::tmem_ld_32x32b_x16(row + 16u, w);
 #pragma unroll
         for (int t = 0; t < kTok; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) + __uint_as_float(w[t]));
@@ -438,17 +461,17 @@ bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
   pl->n_hb = 2 * n_bands;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // about four units per SM, four to kMaxR stages each
+  // about four units per SM, at least four stages each
   const long long total = (long long)pl->n_hb * pl->nkb;
   long long R = (total + 4LL * sms - 1) / (4LL * sms);
-  R = R < 4 ? 4 : (R > kMaxR ? kMaxR : R);
+  R = R < 4 ? 4 : R;
   pl->R = (int)(R < pl->nkb ? R : pl->nkb);
   pl->n_kr = (pl->nkb + pl->R - 1) / pl->R;
   pl->n_units = pl->n_hb * pl->n_kr;
   pl->grid = pl->n_units < sms ? pl->n_units : sms;
   const size_t cap = 227 * 1024;
   const size_t fixed = 1024 /*align*/ + 1792 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
-  const size_t used = fixed + 2 * (size_t)kMaxR * kXBytes + (size_t)kDeqGroups * kWBufs * kWBytes;
+  const size_t used = fixed + (size_t)kMaxS * kXBytes + (size_t)kDeqGroups * kWBufs * kWPair;
   const size_t ring = (cap - used) & ~(size_t)127;
   if (s->max_stage_bytes == 0 || ring < s->max_stage_bytes) return false;
   pl->ring_bytes = (uint32_t)ring;
