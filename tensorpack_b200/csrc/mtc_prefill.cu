@@ -311,15 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kDeqWarp0) {
     // ---------------------------------------------------------------- dequant
-    // The sub-stage's work list holds group entries (one 8x8 leaf group, 4
-    // micro-blocks) and micro-block entries (split groups), each run sorted by
-    // decode class.  Work unit = one group entry or four micro-block entries;
-    // warp w takes units 16w .. 16w + 15, lane pair (2e, 2e + 1) decodes the
-    // two column halves of unit e.  Sorted runs make most warps mode-uniform,
-    // so they take one specialised path; others use the table decoder.
+    // Two groups of eight warps take alternate sub-stages; each dequantises
+    // its CTA's half band into a W tile (dequant_substage).
     const int grp = (warp - kDeqWarp0) / kDeqWarps;
     const int dw = (warp - kDeqWarp0) % kDeqWarps;
-    const int h = lane & 1;
     const uint32_t full_b_remote = tc::mapa(full_b, 0);
     uint32_t it = 0;
     for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters) {

@@ -127,3 +127,40 @@ def test_mtc_gemm_dispatch_large_m(dev):
     Y = mtc_gemm(X, m)
     ref = X.double().cpu().numpy() @ deq.astype(np.float64)
     assert O.relative_frobenius_error(ref, Y.cpu().numpy()) < TOL_REF
+
+
+@pytest.mark.parametrize("K,N,M,permuted", [(256, 4096, 3000, False), (160, 4096, 2600, True), (64, 8192, 4400, False)])
+def test_prefill_many_tiles(dev, K, N, M, permuted):
+    """More pair tiles than CTA pairs (96, 96 and 288 tiles): persistent
+    pairs take several tiles each, with the fused epilogue too; the result
+    within the GEMM tolerance of the oracle, and the epilogue applied to the
+    same sums as the plain call."""
+    import torch
+
+    from tensorpack_b200.kernels.device import epilogue
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    W, sizes, leaf, modes, scales = inputs.forced_mode_allocation(K, N, seed=K + M, p_split=0.3)
+    inner = O.QuadtreeAllocation(sizes, leaf, modes, scales, None, 0)
+    if permuted:
+        rng = np.random.default_rng(K)
+        pr, pc = rng.permutation(K), rng.permutation(N)
+        m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, 0))
+        deq = O.permuted_quadtree_dequant(W, pr, pc, sizes, leaf, modes, scales)
+    else:
+        m = MTCMatrix.from_qt_allocation(W, inner)
+        deq = O.quadtree_dequant(W, sizes, leaf, modes, scales)
+    X = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+    ref = X.astype(np.float64) @ deq.astype(np.float64)
+    Y = prefill(m, X, dev)
+    assert O.relative_frobenius_error(ref, Y) < TOL_REF
+    ds = m.device_stream(dev)
+    b = torch.randn(N, device=dev)
+    Xt = torch.from_numpy(X).to(dev)
+    Ye = torch.empty(M, N, device=dev)
+    ds.prefill(Xt, Ye, epilogue(b, "relu"))
+    torch.cuda.synchronize()
+    ds.check_status()
+    refe = np.maximum(ref + b.double().cpu().numpy(), 0.0)
+    assert O.relative_frobenius_error(refe, Ye.cpu().numpy()) < TOL_REF
+    assert torch.equal(Ye, torch.relu(torch.from_numpy(Y).to(dev) + b))
