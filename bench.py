@@ -15,8 +15,11 @@ tensorpack_b200.quant.
   decode    M = 1 through the tensor-core decode kernel, GB/s of accounted packed
             bytes (payload + scales + modes + split flags + permutation
             indices), rotating over copies of the stream totalling > 4x L2
-  e2e       the prefill metric through the public API (mtc_gemm) with pinned
-            host X and Y: host->device copy, GEMM, device->host copy per step
+  e2e       the prefill metric through the public API with pinned host X and
+            Y: host->device copy, GEMM, device->host copy per step (one GPU:
+            tensorpack_b200.kernels.gemm.HostGemm, which overlaps the copies
+            and the GEMM of row chunks; several: the sharded GEMM between
+            whole-matrix copies)
   roofline  the prefill kernel alone (CUDA events on its stream) against the
             measured dense bf16 peak; the decode kernel against measured HBM
   cpu_baseline  the reference's packed Numba GEMM algorithm (oracle port,
@@ -217,7 +220,7 @@ def main():
 
     build.build()
     from tensorpack_b200 import _lib
-    from tensorpack_b200.kernels.gemm import MTCMatrix, mtc_gemm
+    from tensorpack_b200.kernels.gemm import HostGemm, MTCMatrix
     from tensorpack_b200.quant import PermutedQuadtreeRD
     from tensorpack_b200.sharding import ShardedMTCMatrix
 
@@ -356,21 +359,29 @@ def main():
         return
 
     # --- end to end through the public API with pinned host buffers ---
+    # One GPU: HostGemm (host X in, host Y out; copies in, GEMM and copies out
+    # of row chunks overlapped).  Several: copy in, sharded GEMM, copy out.
     Xh = torch.from_numpy(X_host).pin_memory()
     Yh = torch.empty(M_PREFILL, N_OUT, dtype=torch.float32).pin_memory()
     Xd = torch.empty_like(X)
-    for _ in range(2):
+    host_gemm = HostGemm(mat, dev) if sharded is None else None
+
+    def e2e_step():
+        if host_gemm is not None:
+            host_gemm(Xh, Yh)
+            return
         Xd.copy_(Xh, non_blocking=True)
-        gemm(Xd, Y) if sharded is not None else mtc_gemm(Xd, mat)
+        gemm(Xd, Y)
         Yh.copy_(Y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = max(3, args.steps // 4)
     e0.record(stream)
     for _ in range(e2e_steps):
-        Xd.copy_(Xh, non_blocking=True)
-        Yd = gemm(Xd, Y) if sharded is not None else mtc_gemm(Xd, mat)
-        Yh.copy_(Yd, non_blocking=True)
+        e2e_step()
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)

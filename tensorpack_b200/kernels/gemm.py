@@ -330,6 +330,86 @@ def gemm_fused(X, W: MTCMatrix, bias=None, activation: Optional[str] = None, Y=N
     return Y
 
 
+class HostGemm:
+    """Y = X @ W for activations and results in (pinned) host memory, with
+    the host->device copy, the GEMM and the device->host copy of consecutive
+    row chunks overlapped on three CUDA streams: the PCIe copies in both
+    directions and the kernels run at the same time instead of one after the
+    other.  Device buffers (two chunks) are allocated once per shape and
+    reused across calls; ``__call__`` returns once Yh holds the result.
+
+    A chunk is ``chunk_rows`` rows (a multiple of the prefill kernel's 512-row
+    pair tile by default); M <= chunk_rows runs as one chunk."""
+
+    def __init__(self, W: MTCMatrix, device=None, chunk_rows: int = 1024):
+        import torch
+
+        self.W = W
+        self.device = torch.device(device if device is not None else "cuda")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.chunk_rows = int(chunk_rows)
+        self.ds = W.device_stream(self.device)
+        with torch.cuda.device(self.device):
+            self.s_in, self.s_mm, self.s_out = (torch.cuda.Stream(self.device) for _ in range(3))
+        self._bufs = None
+
+    def _buffers(self, rows: int):
+        import torch
+
+        K, N = self.W.shape
+        if self._bufs is None or self._bufs[0][0].shape[0] < rows:
+            self._bufs = [(torch.empty(rows, K, dtype=torch.float32, device=self.device),
+                           torch.empty(rows, N, dtype=torch.float32, device=self.device)) for _ in range(2)]
+        return self._bufs
+
+    def __call__(self, Xh, Yh=None, ep=None):
+        import torch
+
+        K, N = self.W.shape
+        if Xh.device.type != "cpu" or Xh.dtype != torch.float32 or Xh.dim() != 2 or Xh.shape[1] != K:
+            raise ValueError(f"HostGemm: X must be a host float32 (M, {K}) tensor")
+        M = Xh.shape[0]
+        if Yh is None:
+            Yh = torch.empty(M, N, dtype=torch.float32, pin_memory=True)
+        if Yh.shape != (M, N) or Yh.device.type != "cpu" or Yh.dtype != torch.float32:
+            raise ValueError(f"HostGemm: Y must be a host float32 ({M}, {N}) tensor")
+        if M == 0:
+            return Yh
+        cr = min(self.chunk_rows, M)
+        bufs = self._buffers(cr)
+        cur = torch.cuda.current_stream(self.device)
+        ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("in", "mm", "out")}
+        started = [False, False]
+        for s in (self.s_in, self.s_mm, self.s_out):
+            s.wait_stream(cur)
+        for i, r0 in enumerate(range(0, M, cr)):
+            r1 = min(M, r0 + cr)
+            b = i & 1
+            Xd, Yd = bufs[b]
+            with torch.cuda.stream(self.s_in):
+                if started[b]:
+                    self.s_in.wait_event(ev["mm"][b])        # the chunk two back has read Xd
+                Xd[:r1 - r0].copy_(Xh[r0:r1], non_blocking=True)
+                ev["in"][b].record(self.s_in)
+            with torch.cuda.stream(self.s_mm):
+                self.s_mm.wait_event(ev["in"][b])
+                if started[b]:
+                    self.s_mm.wait_event(ev["out"][b])       # ... and its result left Yd
+                self.ds.matmul(Xd[:r1 - r0], Yd[:r1 - r0], ep)
+                ev["mm"][b].record(self.s_mm)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(ev["mm"][b])
+                Yh[r0:r1].copy_(Yd[:r1 - r0], non_blocking=True)
+                ev["out"][b].record(self.s_out)
+            started[b] = True
+        cur.wait_stream(self.s_out)
+        cur.wait_stream(self.s_mm)
+        cur.synchronize()
+        self.ds.check_status()
+        return Yh
+
+
 def mtc_gemm(A, B):
     """GEMM with a packed right operand (gemm.py:541-574).
 

@@ -164,3 +164,29 @@ def test_prefill_many_tiles(dev, K, N, M, permuted):
     refe = np.maximum(ref + b.double().cpu().numpy(), 0.0)
     assert O.relative_frobenius_error(refe, Ye.cpu().numpy()) < TOL_REF
     assert torch.equal(Ye, torch.relu(torch.from_numpy(Y).to(dev) + b))
+
+
+@pytest.mark.parametrize("M,chunk", [(3000, 1024), (1030, 1024), (10, 1024), (700, 256)])
+def test_host_gemm_pipeline(dev, M, chunk):
+    """HostGemm: pinned host X in, host Y out, row chunks overlapped.  Rows
+    are independent in the GEMM, so chunks of the prefill kernel give the
+    whole-matrix call's values exactly; a chunk of <= 16 rows goes to the
+    decode kernel (another summation order), held to the tolerance."""
+    import torch
+
+    from tensorpack_b200.kernels.gemm import HostGemm
+
+    m, deq = forced(256, 640, seed=9)
+    X = np.random.default_rng(M).standard_normal((M, 256)).astype(np.float32)
+    hg = HostGemm(m, dev, chunk_rows=chunk)
+    Xh = torch.from_numpy(X).pin_memory()
+    Yh = hg(Xh)
+    Yh2 = hg(Xh, torch.empty(M, 640).pin_memory())  # buffers reused
+    assert torch.equal(Yh, Yh2)
+    ref = X.astype(np.float64) @ deq.astype(np.float64)
+    assert O.relative_frobenius_error(ref, Yh.numpy()) < TOL_REF
+    whole = prefill(m, X, dev) if M > 16 else None
+    if whole is not None and (M % chunk == 0 or M % chunk > 16):
+        np.testing.assert_array_equal(Yh.numpy(), whole)
+    with pytest.raises(ValueError):
+        hg(torch.zeros(4, 255))
