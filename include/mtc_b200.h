@@ -135,7 +135,8 @@ typedef struct mtc_stream_desc {
   const uint32_t* stage_offsets; /* [n_sub + 1]: byte offset of each image (last = total) */
   const uint32_t* stage_ranges;  /* [n_sub][4]: image bytes, work-list bytes, row-0 record bytes, row-1 record bytes */
   uint32_t max_stage_bytes;      /* largest image */
-  uint32_t pad_;
+  uint32_t max_sms;              /* at most this many SMs for the prefill kernel (0: all); leaves SMs free for
+                                    work that overlaps it, such as a collective on another stream */
 } mtc_stream_desc;
 
 MTC_API int mtc_abi_version(void);

@@ -41,7 +41,7 @@ class StreamDesc(ctypes.Structure):
         ("band_tiles", c_i32), ("exp2", c_i32),
         ("record_bytes", c_u64), ("max_row_bytes", c_u32), ("scale_words", c_i32),
         ("stage_images", c_p), ("stage_counts", c_p), ("stage_offsets", c_p), ("stage_ranges", c_p),
-        ("max_stage_bytes", c_u32), ("pad_", c_u32),
+        ("max_stage_bytes", c_u32), ("max_sms", c_u32),
     ]
 
 

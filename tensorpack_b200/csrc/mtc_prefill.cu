@@ -899,7 +899,8 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   MTC_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg),
                  "mtc_prefill_gemm: cluster occupancy");
   MTC_REQUIRE(max_clusters >= 1, "mtc_prefill_gemm: no CTA pair of %zu bytes of shared memory fits", pl.smem);
-  const int clusters = pl.n_tiles < max_clusters ? pl.n_tiles : max_clusters;
+  int clusters = pl.n_tiles < max_clusters ? pl.n_tiles : max_clusters;
+  if (s->max_sms >= 2 && clusters > (int)(s->max_sms / 2)) clusters = (int)(s->max_sms / 2);
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   MTC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p), "mtc_prefill_gemm: launch");
   MTC_CHECK_LAUNCH("mtc_prefill_gemm");

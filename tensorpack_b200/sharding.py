@@ -6,7 +6,9 @@ matrix, cut on 32-column tile boundaries and balanced by payload bytes
 unequal bytes).  Every GPU receives the full activations, gathers X[:, pr]
 and computes its slice of the permuted output; one all-gather over NCCL
 (NVLink/NVSwitch) collects the slices, and one row-permute kernel writes the
-original column order Y[:, pc].  No other communication: the reference has
+original column order Y[:, pc].  For large M the rows go in two chunks: the
+second chunk's GEMM (held to all but 16 SMs) runs while the first chunk is
+all-gathered and assembled on a side stream.  No other communication: the reference has
 no distributed path (it is a single-process Numba package), so this is the
 B200-side scale-out of mtc_gemm (mtc/kernels/gemm.py:541-574 and the
 gather/scatter of mtc/core/permutation.py:15-21).
@@ -113,6 +115,10 @@ class ShardedMTCMatrix:
         self.stream = self.local.device_stream(self.device)
         self.pos = torch.from_numpy(self.plan.pos).to(self.device)
         self._buf = {}
+        self.side = torch.cuda.Stream(self.device)
+        self.pipeline_min_rows = 1024
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.limit_sms = max(2, sms - 16)  # 16 SMs left to the collective while the prefill runs
 
     def matmul(self, X, Y: Optional["torch.Tensor"] = None):
         import torch
@@ -122,21 +128,41 @@ class ShardedMTCMatrix:
 
         M = X.shape[0]
         w, wmax = self.local.shape[1], self.plan.wmax
-        key = M
-        if key not in self._buf:
-            self._buf[key] = (torch.zeros(M, wmax, dtype=torch.float32, device=self.device),
-                              torch.empty(self.world, M, wmax, dtype=torch.float32, device=self.device))
-        part, gathered = self._buf[key]
-        self.stream.matmul(X, part[:, :w])
-        if self.world > 1:
-            dist.all_gather_into_tensor(gathered, part, group=self.group)
-            src = gathered
-        else:
-            src = part
         if Y is None:
             Y = torch.empty(M, self.N, dtype=torch.float32, device=self.device)
         lib = _lib.load()
-        _lib.check(lib.mtc_permute_rows(src.data_ptr(), M * wmax, wmax, self.world, wmax, self.pos.data_ptr(),
-                                        self.N, M, Y.data_ptr(), Y.stride(0), None,
-                                        torch.cuda.current_stream(self.device).cuda_stream), "shard assembly")
+        # Large M on several GPUs: two row chunks, the second chunk's GEMM
+        # overlapping the first chunk's all-gather and assembly on a side
+        # stream.  The prefill then leaves `reserve_sms` SMs to the collective.
+        chunks = [(0, M)]
+        if self.world > 1 and M >= self.pipeline_min_rows:
+            h = (M // 2 + 511) // 512 * 512
+            chunks = [(0, h), (h, M)] if h < M else [(0, M)]
+        key = (M, len(chunks))
+        if key not in self._buf:
+            self._buf[key] = (torch.zeros(M, wmax, dtype=torch.float32, device=self.device),
+                              [torch.empty(self.world, r1 - r0, wmax, dtype=torch.float32, device=self.device)
+                               for r0, r1 in chunks])
+        part, gathered = self._buf[key]
+        main = torch.cuda.current_stream(self.device)
+        self.stream.desc.max_sms = self.limit_sms if len(chunks) > 1 else 0
+        for c, (r0, r1) in enumerate(chunks):
+            self.stream.matmul(X[r0:r1], part[r0:r1, :w])
+            done = torch.cuda.Event()
+            done.record(main)
+            side = self.side if len(chunks) > 1 else main
+            with torch.cuda.stream(side):
+                side.wait_event(done)
+                src = part[r0:r1]
+                if self.world > 1:
+                    work = dist.all_gather_into_tensor(gathered[c], src, group=self.group, async_op=True)
+                    work.wait()
+                    src = gathered[c]
+                rows = r1 - r0
+                _lib.check(lib.mtc_permute_rows(src.data_ptr(), rows * wmax, wmax, self.world, wmax,
+                                                self.pos.data_ptr(), self.N, rows, Y[r0:r1].data_ptr(), Y.stride(0),
+                                                None, side.cuda_stream), "shard assembly")
+        if len(chunks) > 1:
+            main.wait_stream(self.side)
+        self.stream.desc.max_sms = 0
         return Y

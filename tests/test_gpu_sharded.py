@@ -59,7 +59,7 @@ def _worker(rank, world, port, golden_dir, out_q):
         ref_w = O.permuted_quadtree_dequant(W, pr, pc, sizes, leaf, modes, scales).astype(np.float64)
         sh = ShardedMTCMatrix(mat, device=dev)
         full = mat.device_stream(dev)
-        for M in (1, 16, 300):
+        for M in (1, 16, 300, 1200):  # 1200: two row chunks, GEMM overlapping the first chunk's all-gather
             X = torch.from_numpy(inputs.llm_activations(M, 256, seed=M, outlier_seed=2)).to(dev)
             Y = sh.matmul(X)
             Y1 = torch.empty(M, 1024, dtype=torch.float32, device=dev)
