@@ -360,7 +360,9 @@ def main():
 
     # --- end to end through the public API with pinned host buffers ---
     # One GPU: HostGemm (host X in, host Y out; copies in, GEMM and copies out
-    # of row chunks overlapped).  Several: copy in, sharded GEMM, copy out.
+    # of row chunks overlapped).  Several: every rank copies X in (each GPU
+    # needs all of it), runs the sharded GEMM, and rank 0 copies the result
+    # out (it is the same on every rank; the host needs it once).
     Xh = torch.from_numpy(X_host).pin_memory()
     Yh = torch.empty(M_PREFILL, N_OUT, dtype=torch.float32).pin_memory()
     Xd = torch.empty_like(X)
@@ -372,7 +374,8 @@ def main():
             return
         Xd.copy_(Xh, non_blocking=True)
         gemm(Xd, Y)
-        Yh.copy_(Y, non_blocking=True)
+        if rank == 0:
+            Yh.copy_(Y, non_blocking=True)
 
     for _ in range(2):
         e2e_step()

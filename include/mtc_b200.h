@@ -143,6 +143,13 @@ MTC_API int mtc_abi_version(void);
 MTC_API const char* mtc_last_error(void);
 MTC_API int mtc_device_sm_count(int device);
 
+/* Byte copy by the copy engines (cudaMemcpyAsync, device to device) on
+ * `stream`; dst or src may be a peer GPU's memory mapped into this process
+ * (symmetric memory), in which case the bytes cross NVLink without using
+ * SMs.  Used to move column shards of a multi-GPU GEMM into the peers'
+ * buffers while the GEMM runs.  Both pointers 16-byte aligned. */
+MTC_API int mtc_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Repack step 1 (replaces the per-block offset computation of
  * MTCMatrix.from_allocation, mtc/kernels/gemm.py:449-454): measures every
  * tile record, lays the records out band-major, fills `tiles`

@@ -64,6 +64,7 @@ SIGNATURES = {
     "mtc_abi_version": (c_i32, []),
     "mtc_last_error": (ctypes.c_char_p, []),
     "mtc_device_sm_count": (c_i32, [c_i32]),
+    "mtc_copy_async": (c_i32, [c_p, c_p, c_size, c_p]),
     "mtc_repack_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p,
                                 ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_fill": (c_i32, [c_p, c_u64, c_p, c_p, ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),

@@ -33,3 +33,14 @@ extern "C" int mtc_device_sm_count(int device) {
   }
   return n;
 }
+
+extern "C" int mtc_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  mtc::clear_error();
+  MTC_REQUIRE(dst && src, "mtc_copy_async: null pointer");
+  MTC_REQUIRE(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0,
+              "mtc_copy_async: pointers not 16-byte aligned");
+  if (bytes == 0) return MTC_OK;
+  MTC_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, mtc::as_stream(stream)),
+                 "mtc_copy_async");
+  return MTC_OK;
+}

@@ -118,7 +118,30 @@ class ShardedMTCMatrix:
         self.side = torch.cuda.Stream(self.device)
         self.pipeline_min_rows = 1024
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.limit_sms = max(2, sms - 16)  # 16 SMs left to the collective while the prefill runs
+        self.limit_sms = max(2, sms - 16)  # 16 SMs left to the exchange while the prefill runs
+        # "nccl": one all-gather per chunk (default); "copy": slices pushed
+        # into the peers' symmetric-memory buffers by the copy engines
+        self.transport = "nccl"
+        self._calls = 0
+
+    def _peer_buffers(self, M: int, idx: int):
+        """[world][M][wmax] gather buffer in symmetric memory (every rank's
+        slice lands in every rank's buffer) and the peers' views of it.  Calls
+        alternate between two such buffers: a rank may push the next call's
+        slices while a slower peer still assembles this call's."""
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        key = ("peer", M, idx)
+        if key not in self._buf:
+            wmax = self.plan.wmax
+            buf = symm.empty(self.world, M, wmax, dtype=torch.float32, device=self.device)
+            hdl = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+            peers = [buf if r == self.rank else hdl.get_buffer(r, (self.world, M, wmax), torch.float32)
+                     for r in range(self.world)]
+            self._buf[key] = (buf, peers, hdl, torch.zeros(1, dtype=torch.float32, device=self.device))
+        return self._buf[key]
 
     def matmul(self, X, Y: Optional["torch.Tensor"] = None):
         import torch
@@ -132,37 +155,63 @@ class ShardedMTCMatrix:
             Y = torch.empty(M, self.N, dtype=torch.float32, device=self.device)
         lib = _lib.load()
         # Large M on several GPUs: two row chunks, the second chunk's GEMM
-        # overlapping the first chunk's all-gather and assembly on a side
-        # stream.  The prefill then leaves `reserve_sms` SMs to the collective.
+        # overlapping the first chunk's exchange and assembly on a side
+        # stream.  The prefill then leaves 16 SMs to the exchange.
         chunks = [(0, M)]
         if self.world > 1 and M >= self.pipeline_min_rows:
             h = (M // 2 + 511) // 512 * 512
             chunks = [(0, h), (h, M)] if h < M else [(0, M)]
-        key = (M, len(chunks))
-        if key not in self._buf:
-            self._buf[key] = (torch.zeros(M, wmax, dtype=torch.float32, device=self.device),
-                              [torch.empty(self.world, r1 - r0, wmax, dtype=torch.float32, device=self.device)
-                               for r0, r1 in chunks])
-        part, gathered = self._buf[key]
+        peer = None
+        if self.world > 1 and self.transport == "copy":
+            try:
+                peer = self._peer_buffers(M, self._calls & 1)
+            except Exception:  # no symmetric memory here: exchange through NCCL instead
+                self.transport = "nccl"
+        if peer is None:
+            key = (M, len(chunks))
+            if key not in self._buf:
+                self._buf[key] = (torch.zeros(M, wmax, dtype=torch.float32, device=self.device),
+                                  [torch.empty(self.world, r1 - r0, wmax, dtype=torch.float32, device=self.device)
+                                   for r0, r1 in chunks])
+            part, gathered = self._buf[key]
+        else:
+            gbuf, peers, _, token = peer
+            part = gbuf[self.rank]
+        self._calls += 1
         main = torch.cuda.current_stream(self.device)
         self.stream.desc.max_sms = self.limit_sms if len(chunks) > 1 else 0
         for c, (r0, r1) in enumerate(chunks):
             self.stream.matmul(X[r0:r1], part[r0:r1, :w])
             done = torch.cuda.Event()
             done.record(main)
-            side = self.side if len(chunks) > 1 else main
+            side = self.side if (len(chunks) > 1 or peer is not None) else main
+            rows = r1 - r0
             with torch.cuda.stream(side):
                 side.wait_event(done)
-                src = part[r0:r1]
-                if self.world > 1:
-                    work = dist.all_gather_into_tensor(gathered[c], src, group=self.group, async_op=True)
+                if self.world == 1:
+                    src, seg_stride = part[r0:r1], rows * wmax
+                elif peer is None:
+                    work = dist.all_gather_into_tensor(gathered[c], part[r0:r1], group=self.group, async_op=True)
                     work.wait()
-                    src = gathered[c]
-                rows = r1 - r0
-                _lib.check(lib.mtc_permute_rows(src.data_ptr(), rows * wmax, wmax, self.world, wmax,
+                    src, seg_stride = gathered[c], rows * wmax
+                else:
+                    # this rank's rows go straight into every peer's buffer
+                    # (copy engines over NVLink, no SMs); a one-element
+                    # all-reduce after the copies tells every rank that all
+                    # slices of the chunk have landed in its own buffer
+                    nbytes = rows * wmax * 4
+                    for r in range(self.world):
+                        if r != self.rank:
+                            _lib.check(lib.mtc_copy_async(peers[r][self.rank, r0].data_ptr(),
+                                                          part[r0].data_ptr(), nbytes, side.cuda_stream),
+                                       "shard exchange")
+                    work = dist.all_reduce(token, group=self.group, async_op=True)
+                    work.wait()
+                    src, seg_stride = gbuf[0, r0:], M * wmax
+                _lib.check(lib.mtc_permute_rows(src.data_ptr(), seg_stride, wmax, self.world, wmax,
                                                 self.pos.data_ptr(), self.N, rows, Y[r0:r1].data_ptr(), Y.stride(0),
                                                 None, side.cuda_stream), "shard assembly")
-        if len(chunks) > 1:
+        if side is not main:
             main.wait_stream(self.side)
         self.stream.desc.max_sms = 0
         return Y

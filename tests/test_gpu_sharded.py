@@ -3,7 +3,9 @@
 Each rank packs the same MTC-QT-P matrix, keeps its byte-balanced column
 slice (tensorpack_b200.sharding), runs the decode (M <= 16) or prefill
 kernel on it, all-gathers the permuted output slices over NCCL and assembles
-Y[:, pc] with mtc_permute_rows.  Every rank must hold the full product:
+Y[:, pc] with mtc_permute_rows; the exchange goes through NCCL or through
+copy-engine copies into the peers' symmetric-memory buffers.  Every rank
+must hold the full product:
 within the GEMM tolerance of the oracle's fp64 product of the exact dequant.
 The prefill result must also be bit-identical to the unsharded single-GPU
 result (each output tile sums the same k stages in the same order); the
@@ -32,7 +34,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, golden_dir, out_q):
+def _worker(rank, world, port, golden_dir, out_q, transport):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, golden_dir)
     import torch
@@ -58,6 +60,7 @@ def _worker(rank, world, port, golden_dir, out_q):
         mat = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, 0))
         ref_w = O.permuted_quadtree_dequant(W, pr, pc, sizes, leaf, modes, scales).astype(np.float64)
         sh = ShardedMTCMatrix(mat, device=dev)
+        sh.transport = transport
         full = mat.device_stream(dev)
         for M in (1, 16, 300, 1200):  # 1200: two row chunks, GEMM overlapping the first chunk's all-gather
             X = torch.from_numpy(inputs.llm_activations(M, 256, seed=M, outlier_seed=2)).to(dev)
@@ -76,7 +79,8 @@ def _worker(rank, world, port, golden_dir, out_q):
         dist.destroy_process_group()
 
 
-def test_sharded_gemm_on_two_gpus(golden_dir):
+@pytest.mark.parametrize("transport", ["nccl", "copy"])
+def test_sharded_gemm_on_two_gpus(golden_dir, transport):
     import torch
     import torch.multiprocessing as mp
 
@@ -91,7 +95,7 @@ def test_sharded_gemm_on_two_gpus(golden_dir):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, golden_dir, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, golden_dir, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
