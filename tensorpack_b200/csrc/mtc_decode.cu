@@ -425,12 +425,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = hb * kFeat + f;
         if (n < s.N) {
           const int col = p.pc ? p.pc[n] : n;
-          for (int t = 0; t < p.M; ++t) {
-            float sum = 0.0f;
-            for (int r = 0; r < p.n_kr; ++r)
-              sum += __ldcg(p.part + ((size_t)(hb * p.n_kr + r) * kTok + t) * kFeat + f);
-            p.Y[(long long)t * p.ldy + col] = epi_apply(p.ep, sum * p.inv_pow2e, col);
+          // partials r = 0, 1, ... summed in that order for every token; the
+          // loads of one partial are issued together
+          float acc[kTok];
+#pragma unroll
+          for (int t = 0; t < kTok; ++t) acc[t] = 0.0f;
+          for (int r = 0; r < p.n_kr; ++r) {
+            const float* pr = p.part + (size_t)(hb * p.n_kr + r) * kTok * kFeat + f;
+#pragma unroll
+            for (int t = 0; t < kTok; ++t)
+              if (t < p.M) acc[t] += __ldcg(pr + t * kFeat);
           }
+#pragma unroll
+          for (int t = 0; t < kTok; ++t)
+            if (t < p.M) p.Y[(long long)t * p.ldy + col] = epi_apply(p.ep, acc[t] * p.inv_pow2e, col);
         }
         if (tid == 0) p.counters[hb] = 0u;
       }
