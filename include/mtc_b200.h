@@ -125,10 +125,11 @@ typedef struct mtc_stream_desc {
   int32_t scale_words;           /* 1: bf16 scale in the entry, 2: extra fp32 scale word */
   /* Sub-stage images for the tensor-core kernels (NULL until
    * mtc_repack_stage_plan / _fill build them), one per sub-stage q =
-   * 2 * (band * n_kb + kb) + half: the four tiles 4 * half .. 4 * half + 3
-   * of a band in k-tile rows 2 kb and 2 kb + 1 (n_kb = (tk + 1) / 2).  An
-   * image is what the kernels stage in shared memory, read with one bulk
-   * copy: [128 B tile descriptors (4 of row 2 kb, 4 of row 2 kb + 1)][work
+   * (2 * band + half) * n_kb + kb: the four tiles 4 * half .. 4 * half + 3
+   * of a band in k-tile rows 2 kb and 2 kb + 1 (n_kb = (tk + 1) / 2).  The
+   * images of one half band are consecutive, so neighbouring k stages can be
+   * read with one copy.  An image is what the kernels stage in shared
+   * memory: [128 B tile descriptors (4 of row 2 kb, 4 of row 2 kb + 1)][work
    * list][records of row 2 kb][records of row 2 kb + 1]. */
   const uint8_t* stage_images;   /* all images, each 16-byte aligned */
   const uint32_t* stage_counts;  /* [n_sub]: group entries | micro-block entries << 16 */

@@ -16,9 +16,11 @@
 //      warps 0-3  epilogue: TMEM -> partial sums of the unit -> workspace;
 //                 the last unit of a half band (atomic ticket) reduces the
 //                 partials in a fixed order and scatters Y[:, pc]
-//      warp  4    X producer: TMA of each stage's X tile into a ring
-//      warp  5    packed producer: sub-stage images into a shared-memory
-//                 byte ring (cp.async.bulk)
+//      warp  4    X producer: one TMA per stage pair (a 3-d box of two
+//                 64-k blocks of Xp) into a ring of pair slots
+//      warp  5    packed producer: the two images of a stage pair (adjacent
+//                 in the half-band-major image order) with one cp.async.bulk
+//                 into a shared-memory byte ring
 //      warps 6-7  MMA issuers, one per dequant group: when the group's
 //                 eight warps have written the two W tiles of a pair
 //                 (mbarrier), one thread issues the pair's eight MMAs into
@@ -53,10 +55,11 @@ constexpr int kDeqGroups = 2;
 constexpr int kThreads = (kDeqWarp0 + kDeqGroups * kDeqWarps) * 32;
 constexpr uint32_t kXBytes = kTok * BK * 2;     // 2 KB
 constexpr uint32_t kWBytes = kFeat * BK * 2;    // 16 KB
-constexpr int kMaxS = 16;                       // X ring slots
+constexpr int kXPairs = 8;                      // X ring slots, one stage pair each
+constexpr uint32_t kXPair = 2 * kXBytes;
 constexpr int kWBufs = 2;                       // W buffers (two tiles each) per group
 constexpr uint32_t kWPair = 2 * kWBytes;
-constexpr int kRingSlots = 16;
+constexpr int kRingSlots = 8;                   // stage pairs in the byte ring at most
 constexpr int kMetaChunk = 32;
 constexpr uint32_t kTmemCols = 64;              // [unit buffer d][group g] -> column 32 d + 16 g
 constexpr int kEpiBar = 1;                      // named barrier of the epilogue warps
@@ -71,7 +74,6 @@ struct DecodeParams {
   uint32_t* counters;  // [half bands] tickets, zero between calls
   uint32_t* status;
   int n_hb, nkb, n_kr, R, n_units;
-  uint32_t x_box_bytes;  // bytes one X load brings: 64 k x M rows (rows M..15 of the tile are never read back)
   uint32_t ring_bytes;
   float pow2e, inv_pow2e;
   unsigned long long timeout_ns;
@@ -101,13 +103,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_x, const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sX = smem;                                         // [kMaxS][2 KB], 1024-byte aligned
-  uint8_t* sW = sX + kMaxS * kXBytes;                         // [2 groups][kWBufs][2][16 KB]
+  uint8_t* sX = smem;                                         // [kXPairs][2][2 KB], 1024-byte aligned
+  uint8_t* sW = sX + kXPairs * kXPair;                        // [2 groups][kWBufs][2][16 KB]
   uint8_t* sP = sW + kDeqGroups * kWBufs * kWPair;            // packed byte ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + p.ring_bytes);
-  uint64_t* x_full = bars;                                    // [kMaxS]
-  uint64_t* x_empty = x_full + kMaxS;                         // [kMaxS]
-  uint64_t* w_empty = x_empty + kMaxS;                        // [groups * kWBufs]
+  uint64_t* x_full = bars;                                    // [kXPairs]
+  uint64_t* x_empty = x_full + kXPairs;                       // [kXPairs]
+  uint64_t* w_empty = x_empty + kXPairs;                      // [groups * kWBufs]
   uint64_t* w_full = w_empty + kDeqGroups * kWBufs;           // [groups * kWBufs]
   uint64_t* pfull = w_full + kDeqGroups * kWBufs;             // [kRingSlots]
   uint64_t* pempty = pfull + kRingSlots;
@@ -116,10 +118,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;                            // [groups]
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(drain + kDeqGroups);  // [0] abort, [1] last unit
   uint32_t* tmem_slot = const_cast<uint32_t*>(flags) + 4;
-  uint32_t* pmeta = tmem_slot + 4;                            // [kRingSlots][4]
+  uint32_t* pmeta = tmem_slot + 4;                            // [kRingSlots][2 stages][4]
   uint32_t* dtab = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 1280);
   uint4* smeta = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bars) + 1792);  // [2][kMetaChunk][2]
-  static_assert((2 * kMaxS + 2 * kDeqGroups * kWBufs + 2 * kRingSlots + 4 + kDeqGroups) * 8 + 32 + 16 * kRingSlots <=
+  static_assert((2 * kXPairs + 2 * kDeqGroups * kWBufs + 2 * kRingSlots + 4 + kDeqGroups) * 8 + 32 + 32 * kRingSlots <=
                     1280,
                 "barrier region");
 
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < kMaxS; ++i) {
+    for (int i = 0; i < kXPairs; ++i) {
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
     }
@@ -163,17 +165,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kXWarp) {
     // ---------------------------------------------------------------- X producer
-    // One TMA per stage into a ring of kMaxS tiles, released by the MMAs'
-    // commits; the loads run far ahead of the MMAs.
+    // One TMA per stage pair (16 rows of Xp x two 64-k blocks) into a ring
+    // of kXPairs slots, released by the MMAs' commits.
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t ip = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
         int hb, kb0, kb1;
         unit_range(u, hb, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int sx = it % kMaxS;
-          if (it >= (uint32_t)kMaxS && !mbar_wait(&x_empty[sx], ((it / kMaxS) & 1) ^ 1, p.timeout_ns)) {
+        const int P = (kb1 - kb0 + 1) / 2;
+        for (int pr = 0; pr < P; ++pr, ++ip) {
+          const int sx = ip % kXPairs;
+          if (ip >= (uint32_t)kXPairs && !mbar_wait(&x_empty[sx], ((ip / kXPairs) & 1) ^ 1, p.timeout_ns)) {
             ok = false;
             break;
           }
@@ -181,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&x_full[sx], p.x_box_bytes);
-          tc::tma_load_2d(sX + sx * kXBytes, &tmap_x, kb * BK, 0, &x_full[sx]);
+          mbar_expect_tx(&x_full[sx], kXPair);
+          tc::tma_load_3d(sX + sx * kXPair, &tmap_x, 0, 0, kb0 + 2 * pr, &x_full[sx]);
         }
       }
       if (!ok) {
@@ -190,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         flag(p.status, MTC_STATUS_TIMEOUT);
       }
       // let the loads in flight land before the CTA can exit
-      for (uint32_t q = it > (uint32_t)kMaxS ? it - kMaxS : 0u; q < it; ++q)
-        (void)mbar_wait(&x_full[q % kMaxS], (q / kMaxS) & 1, 10000000ull);
+      for (uint32_t q = ip > (uint32_t)kXPairs ? ip - kXPairs : 0u; q < ip; ++q)
+        (void)mbar_wait(&x_full[q % kXPairs], (q / kXPairs) & 1, 10000000ull);
     }
   } else if (warp == kPackWarp) {
     // ---------------------------------------------------------------- packed producer
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_range(blockIdx.x + (q / chunks_per_unit) * gridDim.x, hb, kb0, kb1);
       const int kb = kb0 + (q % chunks_per_unit) * kMetaChunk + lane;
       if (kb < kb1) {
-        const size_t sub = 2 * ((size_t)(hb >> 1) * p.nkb + kb) + (hb & 1);
+        const size_t sub = (size_t)hb * p.nkb + kb;
         nxt0 = *reinterpret_cast<const uint4*>(s.stage_ranges + 4 * sub);
         nxt1 = make_uint4(s.stage_counts[sub], s.stage_offsets[sub], 0u, 0u);
       }
@@ -232,12 +235,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_range(blockIdx.x + (q / chunks_per_unit) * gridDim.x, hb, kb0, kb1);
         const int c0 = kb0 + (q % chunks_per_unit) * kMetaChunk;
         const int c1 = min(kb1, c0 + kMetaChunk);
-        for (int kb = c0; kb < c1 && !flags[0]; ++kb, ++it) {
+        // stage pairs (c0 - kb0 is even): the two images are adjacent
+        for (int kb = c0; kb < c1 && !flags[0]; kb += 2, ++it) {
+          const bool two = kb + 1 < c1;
           const uint4 rg = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0))];  // bytes: image, list, row 0, row 1
           const uint4 mc = smeta[2 * ((q & 1) * kMetaChunk + (kb - c0)) + 1];  // counts, image offset
-          const uint32_t cnt = mc.x;
-          const uint32_t need = rg.x;
-          if (need > p.ring_bytes || ((need | mc.y) & 15u)) {
+          const uint4 rg1 = two ? smeta[2 * ((q & 1) * kMetaChunk + (kb + 1 - c0))] : make_uint4(0u, 0u, 0u, 0u);
+          const uint4 mc1 = two ? smeta[2 * ((q & 1) * kMetaChunk + (kb + 1 - c0)) + 1] : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t need = rg.x + rg1.x;
+          if (need > p.ring_bytes || ((need | mc.y) & 15u) || (two && mc1.y != mc.y + rg.x)) {
             flag(p.status, MTC_STATUS_BAD_STREAM);
             flags[0] = 1;
             break;
@@ -269,11 +275,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ring_start[ps] = pos;
           ring_head = pos + need;
           head_off = start + need;
-          pmeta[4 * ps + 0] = start;
-          pmeta[4 * ps + 1] = cnt;
-          pmeta[4 * ps + 2] = rg.y;
-          pmeta[4 * ps + 3] = rg.z;
-          // the whole sub-stage image in one bulk copy
+          pmeta[8 * ps + 0] = start;
+          pmeta[8 * ps + 1] = mc.x;
+          pmeta[8 * ps + 2] = rg.y;
+          pmeta[8 * ps + 3] = rg.z;
+          pmeta[8 * ps + 4] = start + rg.x;
+          pmeta[8 * ps + 5] = mc1.x;
+          pmeta[8 * ps + 6] = rg1.y;
+          pmeta[8 * ps + 7] = rg1.z;
+          // both images of the pair in one bulk copy
           mbar_expect_tx(&pfull[ps], need);
           bulk_g2s(sP + start, s.stage_images + mc.y, need, &pfull[ps]);
         }
@@ -292,89 +302,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- dequant
     const int grp = (warp - kDeqWarp0) / kDeqWarps;
     const int dw = (warp - kDeqWarp0) % kDeqWarps;
-    uint32_t it0 = 0, sp = 0;
+    uint32_t ip = 0, sp = 0;
     bool go = true;
     for (int u = blockIdx.x; u < p.n_units && go; u += gridDim.x) {
       int hb, kb0, kb1;
       unit_range(u, hb, kb0, kb1);
-      const int L = kb1 - kb0;
-      for (int pr = grp; 2 * pr < L && go; pr += kDeqGroups, ++sp) {
+      const int L = kb1 - kb0, P = (L + 1) / 2;
+      for (int pr = 0; pr < P && go; ++pr, ++ip) {
+        if ((pr & 1) != grp) continue;
         const int b = grp * kWBufs + (sp & 1);
         const int n = min(2, L - 2 * pr);
+        const int ps = ip % kRingSlots;
         bool ok = !flags[0];
         if (ok && sp >= (uint32_t)kWBufs) ok = mbar_wait(&w_empty[b], ((sp >> 1) - 1) & 1, p.timeout_ns);
-        for (int h = 0; h < n; ++h) {
-          const uint32_t it = it0 + 2 * pr + h;
-          const int ps = it % kRingSlots;
-          ok = ok && mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
-          ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the dequant uses whole-warp shuffles
-          if (!ok) break;
-          const int kb = kb0 + 2 * pr + h;
-          dequant_substage(sW + b * kWPair + h * kWBytes, sP + pmeta[4 * ps], pmeta[4 * ps + 1], pmeta[4 * ps + 2],
-                           pmeta[4 * ps + 3], 2 * kb + 1 >= s.tk, dtab, s.scale_words, p.pow2e, dw, lane,
-                           tid - (kDeqWarp0 + grp * kDeqWarps) * 32, (int)((2 * sp + h) * 3u));
-        }
+        ok = ok && mbar_wait(&pfull[ps], (ip / kRingSlots) & 1, p.timeout_ns);
+        ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the dequant uses whole-warp shuffles
         if (!ok) {
           flags[0] = 1;
           go = false;
           break;
         }
+        for (int h = 0; h < n; ++h) {
+          const int kb = kb0 + 2 * pr + h;
+          const uint32_t* pm = pmeta + 8 * ps + 4 * h;
+          dequant_substage(sW + b * kWPair + h * kWBytes, sP + pm[0], pm[1], pm[2], pm[3], 2 * kb + 1 >= s.tk, dtab,
+                           s.scale_words, p.pow2e, dw, lane, tid - (kDeqWarp0 + grp * kDeqWarps) * 32,
+                           (int)((2 * sp + h) * 3u));
+        }
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          for (int h = 0; h < n; ++h) mbar_arrive(&pempty[(it0 + 2 * pr + h) % kRingSlots]);
+          mbar_arrive(&pempty[ps]);
           mbar_arrive(&w_full[b]);
         }
+        ++sp;
       }
-      it0 += L;
     }
   } else if (warp >= kIssWarp0) {
     // ---------------------------------------------------------------- MMA issuers
     const int grp = warp - kIssWarp0;
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(kFeat, kTok);
-      uint32_t sp = 0, ucount = 0, it0 = 0;
+      uint32_t sp = 0, ucount = 0, ip = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ucount) {
         int hb, kb0, kb1;
         unit_range(u, hb, kb0, kb1);
-        const int L = kb1 - kb0, d = ucount & 1;
-        const uint32_t ubase = it0;
-        it0 += L;
+        const int L = kb1 - kb0, P = (L + 1) / 2, d = ucount & 1;
+        const uint32_t ipu = ip;
+        ip += (uint32_t)P;
         // the accumulator of the unit two back must have been read out
         if (ucount >= 2 && !mbar_wait(&acc_empty[d], ((ucount >> 1) - 1) & 1, p.timeout_ns)) {
           ok = false;
           break;
         }
-        if (2 * grp >= L) {
+        if (P <= grp) {
           mbar_arrive(&acc_full[d]);  // no pair of this unit: the accumulator is not read
           continue;
         }
         const uint32_t acc = tmem + 32u * d + 16u * grp;
-        for (int pr = grp; 2 * pr < L; pr += kDeqGroups, ++sp) {
+        for (int pr = grp; pr < P; pr += kDeqGroups, ++sp) {
           const int b = grp * kWBufs + (sp & 1);
           const int n = min(2, L - 2 * pr);
-          if (flags[0] || !mbar_wait(&w_full[b], (sp >> 1) & 1, p.timeout_ns)) {
+          const uint32_t ipp = ipu + pr;
+          const int sx = ipp % kXPairs;
+          if (flags[0] || !mbar_wait(&w_full[b], (sp >> 1) & 1, p.timeout_ns) ||
+              !mbar_wait(&x_full[sx], (ipp / kXPairs) & 1, p.timeout_ns)) {
             ok = false;
             break;
           }
+          tc::fence_after();
           for (int h = 0; h < n; ++h) {
-            const uint32_t it = ubase + 2 * pr + h;
-            const int sx = it % kMaxS;
-            if (!mbar_wait(&x_full[sx], (it / kMaxS) & 1, p.timeout_ns)) {
-              ok = false;
-              break;
-            }
-            tc::fence_after();
             const uint32_t w0 = smem_u32(sW + b * kWPair + h * kWBytes);
-            const uint32_t x0 = smem_u32(sX + sx * kXBytes);
+            const uint32_t x0 = smem_u32(sX + sx * kXPair + h * kXBytes);
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
               tc::mma_f16_ss(acc, tc::smem_desc_k_sw128(w0 + 32 * kk), tc::smem_desc_k_sw128(x0 + 32 * kk), idesc,
                              (pr > grp || h > 0 || kk > 0) ? 1u : 0u);
-            tc::commit(&x_empty[sx]);
           }
-          if (!ok) break;
+          tc::commit(&x_empty[sx]);
           tc::commit(&w_empty[b]);
         }
         if (!ok) break;
@@ -463,7 +469,7 @@ struct DecodePlan {
 
 bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
   if (M < 1 || M > kTok) return false;
-  pl->Kp = s->tk * kTile;
+  pl->Kp = (s->tk + 1) / 2 * BK;  // whole 64-k blocks: a block never runs into the next Xp row
   pl->nkb = (s->tk + 1) / 2;
   const int n_bands = (s->tn + s->band_tiles - 1) / s->band_tiles;
   pl->n_hb = 2 * n_bands;
@@ -479,12 +485,12 @@ bool plan_decode(const mtc_stream_desc* s, int M, DecodePlan* pl) {
   pl->grid = pl->n_units < sms ? pl->n_units : sms;
   const size_t cap = 227 * 1024;
   const size_t fixed = 1024 /*align*/ + 1792 /*barriers, flags, decoder table*/ + 64 * kMetaChunk;
-  const size_t used = fixed + (size_t)kMaxS * kXBytes + (size_t)kDeqGroups * kWBufs * kWPair;
+  const size_t used = fixed + (size_t)kXPairs * kXPair + (size_t)kDeqGroups * kWBufs * kWPair;
   const size_t ring = (cap - used) & ~(size_t)127;
   if (s->max_stage_bytes == 0 || ring < s->max_stage_bytes) return false;
   pl->ring_bytes = (uint32_t)ring;
   pl->smem = used + ring;
-  pl->xp_bytes = ((size_t)kTok * pl->Kp * 2 + 255) & ~(size_t)255;
+  pl->xp_bytes = ((size_t)kTok * pl->Kp * 2 + 255) & ~(size_t)255;  // 16 rows (the MMA's N) x Kp
   pl->part_bytes = (size_t)pl->n_units * kTok * kFeat * sizeof(float);
   return true;
 }
@@ -531,7 +537,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   int rc = launch_gather_x(X, ldx, s->K, pl.Kp, row_perm, M, Xp, status, st);
   if (rc != MTC_OK) return rc;
   CUtensorMap tmap;
-  rc = encode_xp_map(&tmap, Xp, pl.Kp, M, M, "mtc_decode");
+  rc = encode_xp_blocks_map(&tmap, Xp, pl.Kp, kTok, 2, "mtc_decode");
   if (rc != MTC_OK) return rc;
   DecodeParams p;
   p.s = *s;
@@ -547,7 +553,6 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   p.n_kr = pl.n_kr;
   p.R = pl.R;
   p.n_units = pl.n_units;
-  p.x_box_bytes = (uint32_t)(BK * 2 * M);
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);

@@ -71,5 +71,6 @@ inline int read_epilogue(const mtc_epilogue* ep, EpiArg* out, const char* who) {
 int launch_gather_x(const float* X, long long ldx, int K, int Kp, const int32_t* row_perm, int M, __half* Xp,
                     uint32_t* status, cudaStream_t st);
 int encode_xp_map(CUtensorMap* map, const __half* Xp, int Kp, int M, int box_rows, const char* who);
+int encode_xp_blocks_map(CUtensorMap* map, const __half* Xp, int Kp, int rows, int nblk, const char* who);
 
 }  // namespace mtc

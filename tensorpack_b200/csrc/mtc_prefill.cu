@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       nxt0 = make_uint4(0u, 0u, 0u, 0u);
       nxt1 = make_uint4(0u, 0u, 0u, 0u);
       if (q < n_chunks && kb < p.nkb) {
-        const size_t sub = 2 * ((size_t)band * p.nkb + kb) + rank;
+        const size_t sub = (size_t)(2 * band + (int)rank) * p.nkb + kb;
         nxt0 = *reinterpret_cast<const uint4*>(s.stage_ranges + 4 * sub);
         nxt1 = make_uint4(s.stage_counts[sub], s.stage_offsets[sub], 0u, 0u);
       }
@@ -753,6 +753,33 @@ int encode_xp_map(CUtensorMap* map, const __half* Xp, int Kp, int M, int box_row
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("%s: cuTensorMapEncodeTiled failed (%d)", who, (int)r);
+    return MTC_ERR_CUDA;
+  }
+  return MTC_OK;
+}
+
+// TMA descriptor of Xp (fp16 [rows][Kp], Kp a multiple of 64) as 64-k blocks:
+// dims (k in block, row, k block); a box of (64, rows, nblk) lands as nblk
+// consecutive (rows x 128 B) SWIZZLE_128B tiles.
+int encode_xp_blocks_map(CUtensorMap* map, const __half* Xp, int Kp, int rows, int nblk, const char* who) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) {
+    set_error("%s: cuTensorMapEncodeTiled unavailable from the driver", who);
+    return MTC_ERR_CUDA;
+  }
+  if (Kp % 64) {
+    set_error("%s: Xp row length %d is not a multiple of 64", who, Kp);
+    return MTC_ERR_INVALID;
+  }
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(Kp / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)Kp * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)rows, (cuuint32_t)nblk};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(Xp), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled (3-d) failed (%d)", who, (int)r);
     return MTC_ERR_CUDA;
   }
   return MTC_OK;

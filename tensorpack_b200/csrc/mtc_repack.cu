@@ -315,9 +315,9 @@ __global__ void __launch_bounds__(128) stage_lists_kernel(mtc_stream_desc s, int
                                                           uint8_t* __restrict__ images) {
   __shared__ uint32_t cnt[16];   // [0, 8) group classes, [8, 16) micro-block classes
   __shared__ uint32_t base[16];
-  const int q = blockIdx.x;
-  const int half = q & 1, stage = q >> 1;
-  const int band = stage / nkb, kb = stage % nkb;
+  const int q = blockIdx.x;  // half-band major: q = (2 band + half) nkb + kb
+  const int hb = q / nkb, kb = q % nkb;
+  const int band = hb >> 1, half = hb & 1;
   const int i = threadIdx.x;
   const int t8 = i >> 4, G = i & 15;
   const int r = t8 >> 2, colh = t8 & 3;

@@ -23,7 +23,7 @@ DECODE_MAX_M = 16  # largest M served by the split-K decode kernel
 # Version of the device tile stream layout (tile descriptors, records, row
 # offsets, sub-stage images).  A stream saved by another version is rebuilt
 # from the host layout instead of uploaded.
-STREAM_FORMAT_VERSION = 3
+STREAM_FORMAT_VERSION = 4
 _STREAM_ARRAYS = ("tiles", "row_off", "records", "stage_counts", "stage_offsets", "stage_ranges", "stage_images")
 
 
