@@ -212,7 +212,8 @@ MTC_API int mtc_dequant(const mtc_stream_desc* s, const int32_t* row_perm, const
  * tensor cores, fp32 accumulation.  `ws` / `ws_bytes` is scratch for the
  * split-K partial sums (size from mtc_gemv_workspace_bytes); `counters`
  * points at n_bands u32 that are zero before the first call and are left
- * zero by every successful call.  `status` (nullable) receives MTC_STATUS_*
+ * zero by every successful call; after a call that set a status bit the
+ * caller zeroes them again.  `status` (nullable) receives MTC_STATUS_*
  * bits. */
 MTC_API size_t mtc_gemv_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t rows_per_unit);
 MTC_API int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
@@ -245,7 +246,8 @@ MTC_API int mtc_gemv_static(const mtc_stream_desc* s, const float* X, int32_t M,
  * (256-byte aligned, size from mtc_decode_workspace_bytes) holds the fp16
  * gathered activations and the split-K partial sums; `counters` points at
  * 2 * n_bands u32 that are zero before the first call and are left zero by
- * every successful call.  `status` (nullable) receives MTC_STATUS_* bits. */
+ * every successful call; after a call that set a status bit the caller
+ * zeroes them again.  `status` (nullable) receives MTC_STATUS_* bits. */
 MTC_API size_t mtc_decode_workspace_bytes(const mtc_stream_desc* s, int32_t M);
 MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int64_t ldx,
                        const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy, void* ws,

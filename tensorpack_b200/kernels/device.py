@@ -361,11 +361,16 @@ class DeviceStream:
         return self.prefill(X, Y, ep)
 
     def check_status(self):
-        """Raise if a kernel reported a runtime problem (synchronises)."""
+        """Raise if a kernel reported a runtime problem (synchronises).
+
+        A call that gave up part-way can leave split-K tickets counted, so
+        both ticket arrays are cleared with the status word: the next call
+        starts from the zero state the kernels expect."""
         v = int(self.status.item())
         if v:
             self.status.zero_()
             self.counters.zero_()
+            self.decode_counters.zero_()
             bits = []
             if v & _lib.STATUS_TIMEOUT:
                 bits.append("pipeline wait timed out")
