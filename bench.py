@@ -194,6 +194,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--decode-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-kernel", default="tensor", choices=["tensor", "strip"],
+                    help="decode M = 1 through the tcgen05 kernel over the sub-stage images (tensor) or the "
+                         "mma.sync kernel over the strip stream (strip)")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
                     help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
@@ -310,31 +313,51 @@ def main():
 
     # --- decode M = 1 over rotating copies of the stream (> 4x L2) ---
     # Every buffer the decode kernel streams is copied: the sub-stage images
-    # and their metadata.
-    stream_bytes = ds.stage_images.numel()
-    copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
-    descs, keep = [], []
-    for _ in range(copies):
-        bufs = [ds.stage_images.clone(), ds.stage_counts.clone(), ds.stage_offsets.clone(),
-                ds.stage_ranges.clone()]
-        keep += bufs
-        d = _lib.StreamDesc.from_buffer_copy(ds.desc)
-        d.stage_images, d.stage_counts, d.stage_offsets, d.stage_ranges = [b.data_ptr() for b in bufs]
-        descs.append(d)
+    # and their metadata (tensor), or the batch records and their offsets (strip).
     lib = _lib.load()
     import ctypes
 
     x1 = X[:1].contiguous()
     y1 = torch.empty(1, ds.N, dtype=torch.float32, device=dev)
-    ws = torch.empty(max(int(lib.mtc_decode_workspace_bytes(ctypes.byref(ds.desc), 1)), 256), dtype=torch.uint8,
-                     device=dev)
+    descs, keep = [], []
+    pr_ptr = None if ds.row_perm is None else ds.row_perm.data_ptr()
+    pc_ptr = None if ds.col_perm is None else ds.col_perm.data_ptr()
+    if args.decode_kernel == "strip":
+        sp = ds.strip()
+        stream_bytes = sp.stream.numel()
+        copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
+        for _ in range(copies):
+            bufs = [sp.stream.clone(), sp.batch_off.clone(), sp.strip_batch.clone()]
+            keep += bufs
+            d = _lib.StripDesc.from_buffer_copy(sp.desc)
+            d.stream, d.batch_off, d.strip_batch = [b.data_ptr() for b in bufs]
+            descs.append(d)
+        ws = torch.empty(max(int(lib.mtc_strip_workspace_bytes(ctypes.byref(sp.desc), 1)), 256), dtype=torch.uint8,
+                         device=dev)
 
-    def decode(i):
-        _lib.check(lib.mtc_decode(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0),
-                                  None if ds.row_perm is None else ds.row_perm.data_ptr(),
-                                  None if ds.col_perm is None else ds.col_perm.data_ptr(), y1.data_ptr(),
-                                  y1.stride(0), ws.data_ptr(), ws.numel(), ds.decode_counters.data_ptr(),
-                                  ds.status.data_ptr(), None, stream.cuda_stream), "decode")
+        def decode(i):
+            _lib.check(lib.mtc_strip_decode(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0), pr_ptr,
+                                            pc_ptr, y1.data_ptr(), y1.stride(0), ws.data_ptr(), ws.numel(),
+                                            sp.counters.data_ptr(), ds.status.data_ptr(), None, stream.cuda_stream),
+                       "strip decode")
+    else:
+        stream_bytes = ds.stage_images.numel()
+        copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
+        for _ in range(copies):
+            bufs = [ds.stage_images.clone(), ds.stage_counts.clone(), ds.stage_offsets.clone(),
+                    ds.stage_ranges.clone()]
+            keep += bufs
+            d = _lib.StreamDesc.from_buffer_copy(ds.desc)
+            d.stage_images, d.stage_counts, d.stage_offsets, d.stage_ranges = [b.data_ptr() for b in bufs]
+            descs.append(d)
+        ws = torch.empty(max(int(lib.mtc_decode_workspace_bytes(ctypes.byref(ds.desc), 1)), 256), dtype=torch.uint8,
+                         device=dev)
+
+        def decode(i):
+            _lib.check(lib.mtc_decode(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0), pr_ptr, pc_ptr,
+                                      y1.data_ptr(), y1.stride(0), ws.data_ptr(), ws.numel(),
+                                      ds.decode_counters.data_ptr(), ds.status.data_ptr(), None, stream.cuda_stream),
+                       "decode")
 
     for i in range(max(args.warmup, copies)):
         decode(i)
@@ -351,8 +374,9 @@ def main():
     dec_local_gbs = local_bytes / (dec_us * 1e-6) / 1e9
     if args.only == "decode":
         if rank == 0:
-            print(json.dumps({"only": "decode", "us_per_call": dec_us, "GB/s": dec_gbs,
-                              "config": workload_config(args)}), flush=True)
+            print(json.dumps({"only": "decode", "kernel": args.decode_kernel, "us_per_call": dec_us,
+                              "GB/s": dec_gbs, "stream_bytes": stream_bytes, "config": workload_config(args)}),
+                  flush=True)
         if world > 1:
             barrier()
             dist.destroy_process_group()

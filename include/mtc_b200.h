@@ -254,6 +254,67 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
                        size_t ws_bytes, uint32_t* counters, uint32_t* status, const mtc_epilogue* ep,
                        void* stream);
 
+/* Strip stream: the decode-sized layout of a packed matrix.  A strip is 8
+ * output features (stored order) over all of K; its 8x8 groups and 4x4
+ * micro-blocks are sorted by precision into steps that one warp consumes
+ * with straight-line code, and consecutive steps of a strip form batch
+ * records that one bulk copy moves.  See tensorpack_b200/csrc/mtc_strip.cuh
+ * for the byte layout.  All pointers are device pointers for
+ * mtc_strip_decode. */
+typedef struct mtc_strip_desc {
+  const uint8_t* stream;        /* batch records, 16-byte aligned */
+  const uint32_t* batch_off;    /* [n_batches + 1] byte offset of each batch record (last = total) */
+  const uint32_t* strip_batch;  /* [n_strips + 1] first batch of each strip (last = n_batches) */
+  int32_t K, N;                 /* logical shape of W */
+  int32_t tk, tn;               /* 32x32 tiles along K and N (padded up) */
+  int32_t n_strips, n_batches;  /* n_strips = 4 tn */
+  int32_t exp2;                 /* the stream's scales are scale * 2^exp2 */
+  uint32_t max_batch_bytes;     /* largest batch record */
+  uint64_t stream_bytes;
+} mtc_strip_desc;
+
+/* Build the strip stream on the HOST from the leaf list the repack reads
+ * (mtc_leaf_in, tile CSR and the reference-layout arena of
+ * MTCMatrix.from_allocation, mtc/kernels/gemm.py:449-478).  All pointers are
+ * host pointers; no CUDA call is made.  `exp2` pre-scales every scale by
+ * 2^exp2 (choose it so the largest |scale| * 2^exp2 is at most 1); leaves of
+ * P16 or whose pre-scaled scale is not exact in fp16 take the fp32 path.
+ * Batch records hold at most `batch_bytes` bytes (2048..65536, multiple of
+ * 16) and `batch_steps` steps.
+ * plan: out4 = {stream bytes, n_batches, n_strips, largest batch record}.
+ * fill: writes `stream` (stream bytes), `batch_off` (n_batches + 1) and
+ *       `strip_batch` (n_strips + 1). */
+MTC_API int mtc_strip_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn,
+                           int32_t exp2, uint32_t batch_bytes, uint32_t batch_steps, uint64_t* out4);
+MTC_API int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc_leaf_in* leaves,
+                           const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn, int32_t exp2,
+                           uint32_t batch_bytes, uint32_t batch_steps, uint8_t* stream, uint32_t* batch_off,
+                           uint32_t* strip_batch);
+
+/* Validate a host strip stream (record offsets and sizes, strip ranges,
+ * every step descriptor and entry row) before it is uploaded; the decode
+ * kernel relies on it.  Host pointers; returns MTC_ERR_INVALID with a
+ * message naming the first bad record. */
+MTC_API int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, const uint32_t* batch_off,
+                            const uint32_t* strip_batch, int32_t n_batches, int32_t n_strips, int32_t tk,
+                            uint32_t max_batch_bytes);
+
+/* Decode GEMM over the strip stream for M <= 4: Y[:, col_perm] =
+ * X[:, row_perm] @ Wp (replaces mtc_gemm, gemm.py:541-574, and the
+ * gather/GEMM/scatter of permutation.py:15-21).  X is M x K fp32, Y is
+ * M x N fp32.  Products are q * fp16(fp16(x) * fp16(scale * 2^exp2)) on
+ * the tensor cores (mma.sync, fp32 accumulation); the fp32 path computes
+ * q * (fp16(x) * scale * 2^exp2) in fp32.  `ws` (size from
+ * mtc_strip_workspace_bytes) holds per-batch partial sums; `counters` points
+ * at n_strips + 2 u32 that are zero before the first call and are left zero
+ * by every successful call; after a call that set a status bit the caller
+ * zeroes them again.  `status` (nullable) receives MTC_STATUS_* bits. */
+MTC_API size_t mtc_strip_workspace_bytes(const mtc_strip_desc* s, int32_t M);
+MTC_API int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t M, int64_t ldx,
+                             const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy, void* ws,
+                             size_t ws_bytes, uint32_t* counters, uint32_t* status, const mtc_epilogue* ep,
+                             void* stream);
+
 /* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
  * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,
  * gemm.py:541-574, and permutation.py:15-21).  Takes the INVERSE column

@@ -22,6 +22,10 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libmtc_b200.so")
+# CPU model of the strip-stream decode kernel used by the format tests (host
+# code only; never loaded by the package).
+MODEL_SRC = os.path.join(ROOT, "tests", "native", "strip_model.cu")
+MODEL_LIB = os.path.join(ROOT, "tests", "native", "libstrip_model.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -83,12 +87,30 @@ def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB
     return out
 
 
+def build_strip_model(force: bool = False) -> str:
+    """Compile the tests' CPU model of the strip kernel (host code, nvcc as
+    the C++ front end so that it shares mtc_strip.cuh with the kernel)."""
+    deps = [MODEL_SRC, os.path.join(CSRC, "mtc_strip.cuh")]
+    if (not force and os.path.exists(MODEL_LIB)
+            and all(os.path.getmtime(d) <= os.path.getmtime(MODEL_LIB) for d in deps)):
+        return MODEL_LIB
+    tmp = MODEL_LIB + ".tmp"
+    cmd = [nvcc(), "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-shared",
+           MODEL_SRC, "-o", tmp]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {MODEL_SRC}:\n{r.stderr}")
+    os.replace(tmp, MODEL_LIB)
+    return MODEL_LIB
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_strip_model(force=a.force))
 
 
 if __name__ == "__main__":

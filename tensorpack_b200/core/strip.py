@@ -1,0 +1,105 @@
+"""Host side of the strip stream, the decode-sized (M <= 4) device layout.
+
+The stream is built on the host by the native library (``mtc_strip_plan`` /
+``mtc_strip_fill``, pure host code in csrc/mtc_strip_build.cu) from the same
+leaf list and reference-layout arena the GPU repack reads
+(mtc/kernels/gemm.py:449-478), then uploaded by ``DeviceStream``.  A strip is
+8 output features over all of K; its 8x8 groups and 4x4 micro-blocks are
+sorted by precision into steps of straight-line decode, and the steps of a
+strip are grouped into batch records of at most ``batch_bytes`` bytes that
+the kernel moves with one bulk copy each.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from math import ceil, log2
+
+import numpy as np
+
+from .. import _lib
+from . import layout
+
+BATCH_BYTES = 4096   # largest batch record (one shared-memory slot of the kernel)
+BATCH_STEPS = 64     # most steps per batch record
+MAX_M = 4            # tokens per strip-kernel call
+
+
+def strip_exp2(ls: layout.LeafSet) -> int:
+    """Power-of-two pre-scale of the stream's scales: the largest |scale| of
+    a live leaf maps to at most 1, so |x * scale| stays within the checked
+    fp16 range of x."""
+    live = (ls.mode != 0) & (ls.scale != 0)
+    if not live.any():
+        return 0
+    smax = float(np.max(np.abs(ls.scale[live].astype(np.float64))))
+    if not np.isfinite(smax) or smax <= 0.0:
+        return 0
+    return int(max(-100, min(100, -ceil(log2(smax)))))
+
+
+@dataclass
+class HostStripStream:
+    """A strip stream in host memory (numpy arrays) with its geometry."""
+
+    K: int
+    N: int
+    tk: int
+    tn: int
+    exp2: int
+    stream: np.ndarray       # uint8, batch records
+    batch_off: np.ndarray    # uint32 [n_batches + 1]
+    strip_batch: np.ndarray  # uint32 [n_strips + 1]
+    max_batch_bytes: int
+
+    @property
+    def n_strips(self) -> int:
+        return int(self.strip_batch.shape[0] - 1)
+
+    @property
+    def n_batches(self) -> int:
+        return int(self.batch_off.shape[0] - 1)
+
+    def desc(self, stream_ptr=None, batch_off_ptr=None, strip_batch_ptr=None) -> _lib.StripDesc:
+        """The C descriptor; pointers default to the host arrays."""
+        return _lib.StripDesc(
+            stream=stream_ptr if stream_ptr is not None else self.stream.ctypes.data,
+            batch_off=batch_off_ptr if batch_off_ptr is not None else self.batch_off.ctypes.data,
+            strip_batch=strip_batch_ptr if strip_batch_ptr is not None else self.strip_batch.ctypes.data,
+            K=self.K, N=self.N, tk=self.tk, tn=self.tn, n_strips=self.n_strips, n_batches=self.n_batches,
+            exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, stream_bytes=int(self.stream.nbytes))
+
+
+def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS) -> HostStripStream:
+    """Build the strip stream of an MTCMatrix on the host (no GPU needed)."""
+    lib = _lib.load()
+    K, N = (int(v) for v in mat.shape)
+    ls = mat.leaf_set
+    leaves, begin, tk, tn = layout.device_leaf_list(ls, K, N)
+    exp2 = strip_exp2(ls)
+    arena = np.ascontiguousarray(mat.arena.raw_buffer[:max(mat.total_bytes_allocated, 1)])
+    leaves = np.ascontiguousarray(leaves)
+    begin = np.ascontiguousarray(begin, dtype=np.uint32)
+    out = (ctypes.c_uint64 * 4)()
+    _lib.check(lib.mtc_strip_plan(leaves.ctypes.data, begin.ctypes.data, tk, tn, exp2, batch_bytes, batch_steps,
+                                  out), "strip plan")
+    total, n_batches, n_strips, max_batch = (int(v) for v in out)
+    # 16 spare bytes so that every record can be read with 16-byte loads
+    stream = np.zeros(total + 16, dtype=np.uint8)
+    batch_off = np.zeros(n_batches + 1, dtype=np.uint32)
+    strip_batch = np.zeros(n_strips + 1, dtype=np.uint32)
+    _lib.check(lib.mtc_strip_fill(arena.ctypes.data, arena.nbytes, leaves.ctypes.data, begin.ctypes.data, tk, tn,
+                                  exp2, batch_bytes, batch_steps, stream.ctypes.data, batch_off.ctypes.data,
+                                  strip_batch.ctypes.data), "strip fill")
+    hs = HostStripStream(K, N, tk, tn, exp2, stream, batch_off, strip_batch, max_batch)
+    check(hs)
+    return hs
+
+
+def check(hs: HostStripStream) -> None:
+    """Validate every record of a host strip stream (raises ValueError)."""
+    lib = _lib.load()
+    _lib.check(lib.mtc_strip_check(hs.stream.ctypes.data, hs.stream.nbytes, hs.batch_off.ctypes.data,
+                                   hs.strip_batch.ctypes.data, hs.n_batches, hs.n_strips, hs.tk,
+                                   hs.max_batch_bytes), "strip stream")

@@ -20,6 +20,7 @@ from ..core import layout
 
 BAND_TILES = 8  # tiles per column band = 256 output features (one per consumer warp)
 DECODE_MAX_M = 16  # largest M served by the split-K decode kernel
+STRIP_MAX_M = 4    # largest M served by the strip-stream decode kernel
 # Version of the device tile stream layout (tile descriptors, records, row
 # offsets, sub-stage images).  A stream saved by another version is rebuilt
 # from the host layout instead of uploaded.
@@ -183,6 +184,11 @@ class DeviceStream:
         self._ws = {}
         self.n_leaves = n_leaves
         self.source = getattr(self, "source", "repack")  # "repack" or "file" (uploaded by from_buffers)
+        self._mat = mat          # host layout, for the strip stream built on first use
+        self._strip = None
+        # decode kernel for M <= 4: "tensor" (tcgen05 over the sub-stage images)
+        # or "strip" (mma.sync over the strip stream)
+        self.decode_kernel = "tensor"
 
     def with_perms(self, row_perm, col_perm) -> "DeviceStream":
         """The same packed stream (buffers shared, nothing repacked) with other
@@ -207,6 +213,7 @@ class DeviceStream:
             new.decode_counters = torch.zeros_like(self.decode_counters)
             new.status = torch.zeros_like(self.status)
         new._ws = {}
+        new._strip = None if self._strip is None else self._strip.with_own_counters()
         return new
 
     # ------------------------------------------------------------------ saving / loading
@@ -307,6 +314,32 @@ class DeviceStream:
                                   _stream(self.device)), "decode")
         return Y
 
+    def strip(self) -> "DeviceStrip":
+        """The strip stream of this matrix on this device (the decode layout
+        for M <= 4), built on the host and uploaded at first use."""
+        if self._strip is None:
+            from ..core import strip as _strip
+
+            self._strip = DeviceStrip(_strip.build_host(self._mat), self.device)
+        return self._strip
+
+    def decode_strip(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
+        """Y[:M] = X @ W for M <= 4 (mma.sync kernel over the strip stream);
+        ``ep`` from ``epilogue()`` fuses a bias and activation."""
+        lib = _lib.load()
+        st = self.strip()
+        M = X.shape[0]
+        need = int(lib.mtc_strip_workspace_bytes(ctypes.byref(st.desc), M))
+        ws = self._ws.get("strip")
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+            self._ws["strip"] = ws
+        _lib.check(lib.mtc_strip_decode(ctypes.byref(st.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
+                                        _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), ws.data_ptr(), ws.numel(),
+                                        st.counters.data_ptr(), self.status.data_ptr(), _ep(ep),
+                                        _stream(self.device)), "strip decode")
+        return Y
+
     def prefill_workspace(self, M: int) -> torch.Tensor:
         lib = _lib.load()
         permuted = 1 if self.col_perm_inv is not None else 0
@@ -356,7 +389,10 @@ class DeviceStream:
     def matmul(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
         """Y = X @ W (+ the fused epilogue ``ep``), picking the decode kernel
         for M <= 16 and the tensor-core prefill kernel above."""
-        if X.shape[0] <= DECODE_MAX_M:
+        M = X.shape[0]
+        if M <= STRIP_MAX_M and self.decode_kernel == "strip":
+            return self.decode_strip(X, Y, ep)
+        if M <= DECODE_MAX_M:
             return self.decode(X, Y, ep)
         return self.prefill(X, Y, ep)
 
@@ -371,6 +407,9 @@ class DeviceStream:
             self.status.zero_()
             self.counters.zero_()
             self.decode_counters.zero_()
+            strip = getattr(self, "_strip", None)
+            if strip is not None:
+                strip.counters.zero_()
             bits = []
             if v & _lib.STATUS_TIMEOUT:
                 bits.append("pipeline wait timed out")
@@ -379,3 +418,32 @@ class DeviceStream:
             if v & _lib.STATUS_BAD_STREAM:
                 bits.append("tile stream failed a bounds check")
             raise RuntimeError("MTC kernel status: " + "; ".join(bits))
+
+
+class DeviceStrip:
+    """The strip stream of one matrix on one device: batch records, batch
+    offsets, per-strip batch ranges (uploaded from a HostStripStream), the
+    C descriptor and the kernel's ticket / schedule words."""
+
+    def __init__(self, hs, device):
+        dev = torch.device(device)
+        with torch.cuda.device(dev):
+            self.stream = torch.from_numpy(hs.stream).to(dev)
+            self.batch_off = torch.from_numpy(hs.batch_off.view(np.int32)).to(dev)
+            self.strip_batch = torch.from_numpy(hs.strip_batch.view(np.int32)).to(dev)
+            self.counters = torch.zeros(hs.n_strips + 2, dtype=torch.int32, device=dev)
+        self.host = hs
+        self.device = dev
+        self.desc = hs.desc(self.stream.data_ptr(), self.batch_off.data_ptr(), self.strip_batch.data_ptr())
+
+    @property
+    def stream_bytes(self) -> int:
+        return int(self.host.batch_off[-1])
+
+    def with_own_counters(self) -> "DeviceStrip":
+        import copy
+
+        new = copy.copy(self)
+        new.counters = torch.zeros_like(self.counters)
+        new.desc = _lib.StripDesc.from_buffer_copy(self.desc)
+        return new

@@ -1,0 +1,187 @@
+"""The strip stream (decode-sized device layout) on the CPU.
+
+The stream is built by the native host builder (mtc_strip_plan / _fill) and
+consumed by a CPU model of the strip kernel (tests/native/strip_model.cu),
+which runs the kernel's own per-lane decode from mtc_strip.cuh for all 32
+lanes of every step and evaluates its mma.sync.m16n8k16 fragments with the
+PTX layout of that shape.  Checked here:
+  * every precision's code placement packs and decodes 16 codes losslessly
+    and uses exactly 16 m bits;
+  * structural invariants of the batch records;
+  * the model's product equals the fp64 product with the reference dequant
+    (mtc/core/quadtree.py:157-171, permutation.py:76-79, gemm.py:510-538)
+    within the north-star 2e-3, and the exact product of the operands the
+    kernel forms -- q * fp16(fp16(x) * fp16(scale * 2^e)) on the fast path,
+    q * fp32(fp16(x) * scale * 2^e) on the fp32 path -- within 1e-6 (fp64
+    summation order only).
+"""
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import inputs
+from oracle import mtc_oracle as O
+from strip_emul import emulated_product
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+MODES = (2, 3, 4, 5, 6, 8)
+
+
+@pytest.fixture(scope="module")
+def model():
+    from tensorpack_b200 import build
+
+    build.build()
+    path = build.build_strip_model()
+    lib = ctypes.CDLL(path)
+    lib.strip_model_gemm.restype = ctypes.c_int
+    lib.strip_model_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5 + [ctypes.c_void_p, ctypes.c_int] + \
+        [ctypes.c_void_p] * 3
+    lib.strip_model_lane_roundtrip.restype = ctypes.c_int
+    lib.strip_model_lane_roundtrip.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    return lib
+
+
+def _roundtrip(model, cls, q):
+    q = np.ascontiguousarray(q, dtype=np.int32)
+    out = np.zeros(16, np.int32)
+    words = np.zeros(5, np.uint32)
+    rc = model.strip_model_lane_roundtrip(cls, q.ctypes.data, out.ctypes.data, words.ctypes.data)
+    return rc, out, words
+
+
+@pytest.mark.parametrize("cls", range(6))
+def test_lane_codes_roundtrip(model, cls):
+    m = MODES[cls]
+    lo, hi = -(1 << (m - 1)), (1 << (m - 1)) - 1
+    rng = np.random.default_rng(cls)
+    cases = [np.full(16, lo), np.full(16, hi), np.arange(16) % (hi - lo + 1) + lo]
+    cases += [rng.integers(lo, hi + 1, 16) for _ in range(200)]
+    for q in cases:
+        rc, out, _ = _roundtrip(model, cls, q)
+        assert rc == 0, f"P{m}: placement collision"
+        assert np.array_equal(out, q), (m, q, out)
+    # every code bit has its own position: all-ones codes set exactly 16 m bits
+    _, _, words = _roundtrip(model, cls, np.full(16, hi))  # u = 2^m - 1
+    bits = sum(bin(int(w)).count("1") for w in words)
+    assert bits == 16 * m
+
+
+def _check(model, mat, deq_orig, X, tol_emul=1e-6):
+    from tensorpack_b200.core import strip
+
+    hs = strip.build_host(mat)
+    # structure of the batch records
+    offs = hs.batch_off.astype(np.int64)
+    assert (offs % 16 == 0).all() and (np.diff(offs) >= 16).all()
+    assert np.diff(offs).max() == hs.max_batch_bytes <= strip.BATCH_BYTES
+    assert offs[-1] <= hs.stream.size
+    sb = hs.strip_batch.astype(np.int64)
+    assert sb[0] == 0 and sb[-1] == hs.n_batches and (np.diff(sb) >= 1).all()
+    assert hs.n_strips == 4 * hs.tn
+    K, N = mat.shape
+    M = X.shape[0]
+    pr = None if mat.row_perm is None else np.ascontiguousarray(mat.row_perm, dtype=np.int32)
+    pc = None if mat.col_perm is None else np.ascontiguousarray(mat.col_perm, dtype=np.int32)
+    Y = np.zeros((M, N), np.float32)
+    Xc = np.ascontiguousarray(X, dtype=np.float32)
+    rc = model.strip_model_gemm(hs.stream.ctypes.data, hs.batch_off.ctypes.data, hs.strip_batch.ctypes.data,
+                                hs.n_strips, hs.tk, K, N, hs.exp2, Xc.ctypes.data, M,
+                                None if pr is None else pr.ctypes.data, None if pc is None else pc.ctypes.data,
+                                Y.ctypes.data)
+    assert rc == 0
+    ref = X.astype(np.float64) @ deq_orig.astype(np.float64)
+    assert O.relative_frobenius_error(ref, Y) < 2e-3
+    emul, fast = emulated_product(mat, deq_orig, X, hs.exp2)
+    assert O.relative_frobenius_error(emul, Y) < tol_emul
+    return hs, fast
+
+
+def _qt(golden, name, prefix):
+    g = np.load(os.path.join(golden, name))
+    sizes = tuple(int(s) for s in g[prefix + "sizes"])
+    return g, O.QuadtreeAllocation(sizes, {s: g[f"{prefix}leaf_{s}"] for s in sizes},
+                                   {s: g[f"{prefix}modes_{s}"] for s in sizes},
+                                   {s: g[f"{prefix}scales_{s}"] for s in sizes}, None,
+                                   int(g[prefix + "total_bits"]))
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_forced_modes_all_edges(model, M):
+    """All eight precisions at all four leaf edges, signed bf16 scales."""
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    W, sizes, leaf, modes, scales = inputs.forced_mode_allocation(256, 384, seed=0, p_split=0.5)
+    alloc = O.QuadtreeAllocation(sizes, leaf, modes, scales, None, 0)
+    deq = O.quadtree_dequant(W, sizes, leaf, modes, scales)
+    m = MTCMatrix.from_qt_allocation(W, alloc)
+    X = np.random.default_rng(M).standard_normal((M, 256)).astype(np.float32)
+    hs, fast = _check(model, m, deq, X)
+    assert (~fast).any() and fast.any()  # both the fast and the fp32 path ran
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_llm_like_permuted(model, golden_dir, M):
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, inner = _qt(golden_dir, "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    stored = O.quadtree_dequant(W[pr][:, pc], inner.sizes, inner.leaf, inner.modes, inner.scales)
+    X = inputs.llm_activations(M, 256, seed=M, outlier_seed=1)
+    _check(model, m, O.unpermute(stored, pr, pc), X)
+
+
+def test_multiscale(model, golden_dir):
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, a = _qt(golden_dir, "multiscale_256.npz", "")
+    W = inputs.multiscale(256, seed=2)
+    m = MTCMatrix.from_qt_allocation(W, a)
+    deq = O.quadtree_dequant(W, a.sizes, a.leaf, a.modes, a.scales)
+    X = np.random.default_rng(0).standard_normal((2, 256)).astype(np.float32)
+    _check(model, m, deq, X)
+
+
+def test_ragged_fixed_blocks_fp32_scales(model):
+    """48 x 80 (padded to 64 x 96), 16x16 blocks of every mode, fp32 scales:
+    inexact scales and P16 take the fp32 path, padding strips are empty."""
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    rng = np.random.default_rng(3)
+    W = rng.standard_normal((48, 80)).astype(np.float32)
+    modes = rng.choice([0, 2, 3, 4, 5, 6, 8, 16], size=(3, 5)).astype(np.uint8)
+    qmax = np.array([1.0 if x in (0, 2) else 2.0 ** (int(x) - 1) - 1 for x in modes.ravel()]).reshape(3, 5)
+    scales = (np.abs(W.reshape(3, 16, 5, 16)).max(axis=(1, 3)) / qmax).astype(np.float32)
+    m = MTCMatrix.from_allocation(W, modes, scales, 16)
+    deq = O.fixed_dequant(W, modes, np.where(modes == 0, 0, scales).astype(np.float32), 16)
+    X = rng.standard_normal((3, 48)).astype(np.float32)
+    _check(model, m, deq, X)
+
+
+def test_all_p0_matrix_gives_zeros(model):
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    W = np.zeros((64, 64), np.float32)
+    m = MTCMatrix.from_allocation(W, np.zeros((4, 4), np.uint8), np.zeros((4, 4), np.float32), 16)
+    X = np.ones((1, 64), np.float32)
+    hs, _ = _check(model, m, np.zeros((64, 64), np.float32), X)
+    assert hs.n_batches == hs.n_strips  # one empty record per strip
+
+
+def test_stream_bytes_near_accounted(golden_dir):
+    """Decode reads the stream once: its size stays close to the accounted bits."""
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, inner = _qt(golden_dir, "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    hs = strip.build_host(m)
+    ratio = int(hs.batch_off[-1]) / (m.accounted_bits / 8)
+    assert ratio < 1.25, ratio
