@@ -332,14 +332,11 @@ def main():
             d = _lib.StripDesc.from_buffer_copy(sp.desc)
             d.stream, d.batch_off, d.strip_batch = [b.data_ptr() for b in bufs]
             descs.append(d)
-        ws = torch.empty(max(int(lib.mtc_strip_workspace_bytes(ctypes.byref(sp.desc), 1)), 256), dtype=torch.uint8,
-                         device=dev)
 
         def decode(i):
             _lib.check(lib.mtc_strip_decode(ctypes.byref(descs[i % copies]), x1.data_ptr(), 1, x1.stride(0), pr_ptr,
-                                            pc_ptr, y1.data_ptr(), y1.stride(0), ws.data_ptr(), ws.numel(),
-                                            sp.counters.data_ptr(), ds.status.data_ptr(), None, stream.cuda_stream),
-                       "strip decode")
+                                            pc_ptr, y1.data_ptr(), y1.stride(0), ds.status.data_ptr(), None,
+                                            stream.cuda_stream), "strip decode")
     else:
         stream_bytes = ds.stage_images.numel()
         copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)

@@ -259,17 +259,23 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
  * micro-blocks are sorted by precision into steps that one warp consumes
  * with straight-line code, and consecutive steps of a strip form batch
  * records that one bulk copy moves.  See tensorpack_b200/csrc/mtc_strip.cuh
- * for the byte layout.  All pointers are device pointers for
+ * for the byte layout.  All pointers but cta_part are device pointers for
  * mtc_strip_decode. */
+#define MTC_STRIP_MAX_CTA 480     /* most CTA ranges of one strip-kernel launch */
+
 typedef struct mtc_strip_desc {
   const uint8_t* stream;        /* batch records, 16-byte aligned */
   const uint32_t* batch_off;    /* [n_batches + 1] byte offset of each batch record (last = total) */
   const uint32_t* strip_batch;  /* [n_strips + 1] first batch of each strip (last = n_batches) */
+  const uint32_t* cta_part;     /* HOST, [2 (n_cta + 1)]: first strip and first batch of each CTA's range
+                                   (mtc_strip_partition); the end pair is (n_strips, n_batches) */
   int32_t K, N;                 /* logical shape of W */
   int32_t tk, tn;               /* 32x32 tiles along K and N (padded up) */
   int32_t n_strips, n_batches;  /* n_strips = 4 tn */
   int32_t exp2;                 /* the stream's scales are scale * 2^exp2 */
   uint32_t max_batch_bytes;     /* largest batch record */
+  int32_t n_cta;                /* CTA ranges, 1..MTC_STRIP_MAX_CTA */
+  uint32_t max_cta_batches;     /* most batch records in one CTA range */
   uint64_t stream_bytes;
 } mtc_strip_desc;
 
@@ -299,21 +305,28 @@ MTC_API int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, const 
                             const uint32_t* strip_batch, int32_t n_batches, int32_t n_strips, int32_t tk,
                             uint32_t max_batch_bytes);
 
+/* Split a strip stream into CTA ranges for mtc_strip_decode (host pointers,
+ * no CUDA call): contiguous ranges of whole strips balanced by record bytes
+ * over `target_ctas` (normally the SM count), each holding at most
+ * `max_batches` batch records unless a single strip has more.  Writes
+ * cta_part (2 (n_cta + 1) words, room for max_ctas + 1 pairs), n_cta and the
+ * largest range's batch count. */
+MTC_API int mtc_strip_partition(const uint32_t* batch_off, const uint32_t* strip_batch, int32_t n_strips,
+                                int32_t target_ctas, int32_t max_batches, int32_t max_ctas, uint32_t* cta_part,
+                                int32_t* n_cta, uint32_t* max_cta_batches);
+
 /* Decode GEMM over the strip stream for M <= 4: Y[:, col_perm] =
  * X[:, row_perm] @ Wp (replaces mtc_gemm, gemm.py:541-574, and the
  * gather/GEMM/scatter of permutation.py:15-21).  X is M x K fp32, Y is
  * M x N fp32.  Products are q * fp16(fp16(x) * fp16(scale * 2^exp2)) on
  * the tensor cores (mma.sync, fp32 accumulation); the fp32 path computes
- * q * (fp16(x) * scale * 2^exp2) in fp32.  `ws` (size from
- * mtc_strip_workspace_bytes) holds per-batch partial sums; `counters` points
- * at n_strips + 2 u32 that are zero before the first call and are left zero
- * by every successful call; after a call that set a status bit the caller
- * zeroes them again.  `status` (nullable) receives MTC_STATUS_* bits. */
-MTC_API size_t mtc_strip_workspace_bytes(const mtc_strip_desc* s, int32_t M);
+ * q * (fp16(x) * scale * 2^exp2) in fp32.  One CTA per range of
+ * `s->cta_part`; partial sums and tickets live in shared memory, so the
+ * call takes no workspace and leaves no state behind.  `status` (nullable)
+ * receives MTC_STATUS_* bits. */
 MTC_API int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t M, int64_t ldx,
-                             const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy, void* ws,
-                             size_t ws_bytes, uint32_t* counters, uint32_t* status, const mtc_epilogue* ep,
-                             void* stream);
+                             const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
+                             uint32_t* status, const mtc_epilogue* ep, void* stream);
 
 /* Fused dequant + tcgen05 GEMM for prefill-sized M (any M >= 1; used for
  * M > 16): Y[:, col_perm] = X[:, row_perm] @ Wp (replaces mtc_gemm,

@@ -49,17 +49,18 @@ assert ctypes.sizeof(StreamDesc) == 104
 
 
 class StripDesc(ctypes.Structure):
-    """struct mtc_strip_desc."""
+    """struct mtc_strip_desc (cta_part is a host pointer)."""
 
     _fields_ = [
-        ("stream", c_p), ("batch_off", c_p), ("strip_batch", c_p),
+        ("stream", c_p), ("batch_off", c_p), ("strip_batch", c_p), ("cta_part", c_p),
         ("K", c_i32), ("N", c_i32), ("tk", c_i32), ("tn", c_i32),
         ("n_strips", c_i32), ("n_batches", c_i32), ("exp2", c_i32), ("max_batch_bytes", c_u32),
-        ("stream_bytes", c_u64),
+        ("n_cta", c_i32), ("max_cta_batches", c_u32), ("stream_bytes", c_u64),
     ]
 
 
-assert ctypes.sizeof(StripDesc) == 64
+assert ctypes.sizeof(StripDesc) == 80
+STRIP_MAX_CTA = 480
 
 
 class Epilogue(ctypes.Structure):
@@ -96,9 +97,9 @@ SIGNATURES = {
     "mtc_strip_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, ctypes.POINTER(c_u64)]),
     "mtc_strip_fill": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_p, c_p, c_p]),
     "mtc_strip_check": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32]),
-    "mtc_strip_workspace_bytes": (c_size, [ctypes.POINTER(StripDesc), c_i32]),
-    "mtc_strip_decode": (c_i32, [ctypes.POINTER(StripDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_size,
-                                 c_p, c_p, _EP, c_p]),
+    "mtc_strip_partition": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, ctypes.POINTER(c_i32),
+                                    ctypes.POINTER(c_u32)]),
+    "mtc_strip_decode": (c_i32, [ctypes.POINTER(StripDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, _EP, c_p]),
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemm_prefill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64,
                                  c_p, c_size, c_p, _EP, c_p]),

@@ -24,6 +24,7 @@ from . import layout
 BATCH_BYTES = 4096   # largest batch record (one shared-memory slot of the kernel)
 BATCH_STEPS = 64     # most steps per batch record
 MAX_M = 4            # tokens per strip-kernel call
+CTA_BATCHES = 128    # most batch records per CTA range (shared-memory partial sums)
 
 
 def strip_exp2(ls: layout.LeafSet) -> int:
@@ -61,14 +62,27 @@ class HostStripStream:
     def n_batches(self) -> int:
         return int(self.batch_off.shape[0] - 1)
 
-    def desc(self, stream_ptr=None, batch_off_ptr=None, strip_batch_ptr=None) -> _lib.StripDesc:
-        """The C descriptor; pointers default to the host arrays."""
+    def partition(self, target_ctas: int, max_batches: int = CTA_BATCHES):
+        """CTA ranges for the decode kernel: (cta_part uint32 [2 (n + 1)], n,
+        largest range's batch count)."""
+        lib = _lib.load()
+        part = np.zeros(2 * (_lib.STRIP_MAX_CTA + 1), dtype=np.uint32)
+        n = ctypes.c_int32()
+        most = ctypes.c_uint32()
+        _lib.check(lib.mtc_strip_partition(self.batch_off.ctypes.data, self.strip_batch.ctypes.data, self.n_strips,
+                                           int(target_ctas), int(max_batches), _lib.STRIP_MAX_CTA,
+                                           part.ctypes.data, ctypes.byref(n), ctypes.byref(most)), "strip partition")
+        return part[:2 * (n.value + 1)].copy(), n.value, most.value
+
+    def desc(self, stream_ptr, batch_off_ptr, strip_batch_ptr, cta_part: np.ndarray, n_cta: int,
+             max_cta_batches: int) -> _lib.StripDesc:
+        """The C descriptor with the device pointers of an uploaded copy and
+        a CTA partition (``cta_part`` must stay alive while it is used)."""
         return _lib.StripDesc(
-            stream=stream_ptr if stream_ptr is not None else self.stream.ctypes.data,
-            batch_off=batch_off_ptr if batch_off_ptr is not None else self.batch_off.ctypes.data,
-            strip_batch=strip_batch_ptr if strip_batch_ptr is not None else self.strip_batch.ctypes.data,
+            stream=stream_ptr, batch_off=batch_off_ptr, strip_batch=strip_batch_ptr, cta_part=cta_part.ctypes.data,
             K=self.K, N=self.N, tk=self.tk, tn=self.tn, n_strips=self.n_strips, n_batches=self.n_batches,
-            exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, stream_bytes=int(self.stream.nbytes))
+            exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, n_cta=n_cta, max_cta_batches=max_cta_batches,
+            stream_bytes=int(self.stream.nbytes))
 
 
 def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS) -> HostStripStream:

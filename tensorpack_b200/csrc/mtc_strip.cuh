@@ -38,8 +38,9 @@
 //            [n0 + n1 x 32 B: the 16 codes as LSB-first m-bit two's complement]
 // Batch record (one bulk copy, never crossing a strip):
 //   [u32 strip][u32 n_steps][n_steps u32 step descriptors][pad16][steps]
-// Step descriptor: bits 0-3 kind, 4-8 n0 (groups for a group step), 9-13 n1,
-// 14-31 step bytes / 16.
+// Step descriptor: bits 0-3 kind, 4 full step, 5-9 n0 (groups for a group
+// step), 10-14 n1, 15-21 step bytes / 16, 22-31 length of the run of
+// identical full steps that starts here (1 for other steps).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -75,14 +76,25 @@ __host__ __device__ constexpr int prim_bytes(int c) {
 __host__ __device__ constexpr int sec_bytes(int c) { return c == 1 || c == 3 ? 2 : c == 4 ? 4 : 0; }
 __host__ __device__ constexpr int bias_of_class(int c) { return 1 << (mode_of_class(c) - 1); }
 
-// Step descriptor fields.
-__host__ __device__ constexpr uint32_t make_desc(int kind, int n0, int n1, int bytes) {
-  return (uint32_t)kind | ((uint32_t)n0 << 4) | ((uint32_t)n1 << 9) | ((uint32_t)(bytes >> 4) << 14);
+// Step descriptor fields.  A step is "full" when every lane has an item
+// (8 groups, or 16 micro-blocks of each quartet); its lane offsets are then
+// compile-time constants.  The first step of a run of identical full steps
+// (same kind) carries the run's length, so the kernel loops over the run
+// without reading the following descriptors.
+__host__ __device__ constexpr bool full_counts(int kind, int n0, int n1) {
+  return kind < kU2 ? n0 == 8 : (n0 == 16 && n1 == 16);
+}
+constexpr int kMaxRun = 1023;  // 10-bit run length
+__host__ __device__ constexpr uint32_t make_desc(int kind, int n0, int n1, int bytes, int run = 1) {
+  return (uint32_t)kind | ((uint32_t)(full_counts(kind, n0, n1) ? 1 : 0) << 4) | ((uint32_t)n0 << 5) |
+         ((uint32_t)n1 << 10) | ((uint32_t)(bytes >> 4) << 15) | ((uint32_t)run << 22);
 }
 __host__ __device__ inline int desc_kind(uint32_t d) { return (int)(d & 15u); }
-__host__ __device__ inline int desc_n0(uint32_t d) { return (int)((d >> 4) & 31u); }
-__host__ __device__ inline int desc_n1(uint32_t d) { return (int)((d >> 9) & 31u); }
-__host__ __device__ inline int desc_bytes(uint32_t d) { return (int)((d >> 14) << 4); }
+__host__ __device__ inline bool desc_full(uint32_t d) { return (d >> 4) & 1u; }
+__host__ __device__ inline int desc_n0(uint32_t d) { return (int)((d >> 5) & 31u); }
+__host__ __device__ inline int desc_n1(uint32_t d) { return (int)((d >> 10) & 31u); }
+__host__ __device__ inline int desc_bytes(uint32_t d) { return (int)(((d >> 15) & 127u) << 4); }
+__host__ __device__ inline int desc_run(uint32_t d) { return (int)(d >> 22); }
 
 // Bytes of a step record.
 __host__ __device__ inline int step_bytes(int kind, int n0, int n1) {
@@ -199,6 +211,29 @@ __host__ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
 #endif
 }
 
+// (a & b) | c and a | (b & c) as single LOP3s; c / the mask come in
+// registers so both constants of a pair are available to one instruction.
+template <uint32_t B>
+__host__ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t c) {
+#ifdef __CUDA_ARCH__
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "n"(B), "r"(c));
+  return r;
+#else
+  return (a & B) | c;
+#endif
+}
+template <uint32_t C>
+__host__ __device__ __forceinline__ uint32_t lop3_or_and(uint32_t a, uint32_t b) {
+#ifdef __CUDA_ARCH__
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xF8;" : "=r"(r) : "r"(a), "r"(b), "n"(C));
+  return r;
+#else
+  return a | (b & C);
+#endif
+}
+
 __host__ __device__ __forceinline__ uint32_t ldu32(const uint8_t* p) {
 #ifdef __CUDA_ARCH__
   return *reinterpret_cast<const uint32_t*>(p);
@@ -244,10 +279,10 @@ __host__ __device__ __forceinline__ uint32_t decode_pair(const uint32_t* A, uint
   if constexpr (r.pbits == 8) {
     v = prmt(A[r.pw], 0x64646464u, (K & 1) ? 0x4341u : 0x4240u);  // bytes j and j + 2 over 0x64
   } else {
-    v = ((A[r.pw] >> r.prs) & (field2(r.pbits) << r.p)) | kMagic;
+    v = lop3_and_or<(field2(r.pbits) << r.p)>(A[r.pw] >> r.prs, kMagic);
     if constexpr (r.sbits > 0) {
       const uint32_t s = r.ss >= 0 ? (B >> (r.ss >= 0 ? r.ss : 0)) : (B << (r.ss < 0 ? -r.ss : 0));
-      v |= s & (field2(r.sbits) << (r.p + r.pbits));
+      v = lop3_or_and<(field2(r.sbits) << (r.p + r.pbits))>(v, s);
     }
   }
   constexpr double scale = 1.0 / (double)(1 << r.p);
@@ -337,20 +372,32 @@ __host__ __device__ __forceinline__ LaneSlot lane_slot(bool group, int n0, int n
 // A fragments (a[0..3]: columns 0, 1; a[4..7]: columns 2, 3) and B fragments
 // (x * scale at the lane's k rows, per token) of a fast-class lane.  Invalid
 // lanes decode whatever sits at plane index 0 and get a zero scale, so their
-// products are zero.
-template <int C, bool GROUP, int MT>
+// products are zero.  FULL steps take every lane, so all offsets are
+// constants.
+template <int C, bool GROUP, bool FULL, int MT>
 __host__ __device__ __forceinline__ void lane_fast(const uint8_t* step, int n0, int n1, int lane,
                                                    const uint16_t* x16, int kpad, uint32_t a[8],
                                                    uint32_t b[MT][2]) {
   constexpr int PB = prim_bytes(C), SB = sec_bytes(C);
-  const LaneSlot s = lane_slot(GROUP, n0, n1, lane);
-  const uint32_t e = s.valid ? ldu32(step + 4 * s.eidx) : 0u;
-  const uint8_t* planes = step + pad16(4 * s.nent);
+  uint32_t e;
+  const uint8_t *pa, *pb;
+  if constexpr (FULL) {
+    constexpr int NENT = GROUP ? 8 : 32, E = pad16(4 * NENT);
+    e = ldu32(step + 4 * (GROUP ? ((lane & 15) >> 1) : lane));
+    pa = step + E + lane * PB;
+    pb = step + E + 32 * PB + lane * SB;
+  } else {
+    const LaneSlot s = lane_slot(GROUP, n0, n1, lane);
+    e = s.valid ? ldu32(step + 4 * s.eidx) : 0u;
+    const uint8_t* planes = step + pad16(4 * s.nent);
+    pa = planes + s.idx * PB;
+    pb = planes + s.lanes * PB + s.idx * SB;
+  }
   uint32_t A[PB / 4];
-  ldwords(planes + s.idx * PB, A, PB / 4);
+  ldwords(pa, A, PB / 4);
   uint32_t B = 0;
-  if constexpr (SB == 2) B = spread16(ldu16(planes + s.lanes * PB + s.idx * 2));
-  if constexpr (SB == 4) B = ldu32(planes + s.lanes * PB + s.idx * 4);
+  if constexpr (SB == 2) B = spread16(ldu16(pb));
+  if constexpr (SB == 4) B = ldu32(pb);
   decode_lane<C>(A, B, a);
   const int xo = GROUP ? (int)(e >> 16) * 8 + (lane & 1) * 4 : (int)(e >> 16) * 4;
   const uint32_t s2 = prmt(e, e, 0x1010u);
@@ -365,6 +412,8 @@ __host__ __device__ __forceinline__ void lane_fast(const uint8_t* step, int n0, 
 }
 
 // Generic lane: fp32 products into g[m][c] (c = column of the lane's quartet).
+// Code i of the micro-block (row-major) is the m-bit field at bit i m of the
+// lane's 32-byte slot, read through a two-byte window.
 template <int MT>
 __host__ __device__ __forceinline__ void lane_generic(const uint8_t* step, int n0, int n1, int lane,
                                                       const uint16_t* x16, int kpad, float g[MT][4]) {
@@ -374,25 +423,22 @@ __host__ __device__ __forceinline__ void lane_generic(const uint8_t* step, int n
   float sc;
   memcpy(&sc, &e0, 4);
   const int row4 = (int)(e1 & 0xFFFFu), mode = (int)((e1 >> 16) & 31u);
-  uint32_t w[8];
-  ldwords(step + pad16(8 * s.nent) + kGenericSlot * s.idx, w, 4);
-  ldwords(step + pad16(8 * s.nent) + kGenericSlot * s.idx + 16, w + 4, 4);
+  const uint8_t* codes = step + pad16(8 * s.nent) + kGenericSlot * s.idx;
+  float xr[MT][4];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    float xr[4];
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) xr[r] = h2f(x16[(size_t)m * kpad + row4 * 4 + r]) * sc;
+    for (int r = 0; r < 4; ++r) xr[m][r] = h2f(x16[(size_t)m * kpad + row4 * 4 + r]) * sc;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+  for (int i = 0; i < 16; ++i) {
+    const int bit = i * mode;
+    const uint32_t win = (uint32_t)codes[bit >> 3] | ((uint32_t)codes[(bit >> 3) + 1] << 8) |
+                         ((uint32_t)codes[(bit >> 3) + 2 < kGenericSlot ? (bit >> 3) + 2 : kGenericSlot - 1] << 16);
+    const uint32_t u = (win >> (bit & 7)) & ((1u << mode) - 1u);
+    const float q = (float)((int)(u << (32 - mode)) >> (32 - mode));
+    const int r = i >> 2, c = i & 3;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int bit = (4 * r + c) * mode;
-        const uint64_t win = ((uint64_t)w[(bit >> 5) + 1 < 8 ? (bit >> 5) + 1 : 7] << 32) | w[bit >> 5];
-        const uint32_t u = (uint32_t)(win >> (bit & 31)) & ((1u << mode) - 1u);
-        const int q = (int)(u << (32 - mode)) >> (32 - mode);
-        g[m][c] += (float)q * xr[r];
-      }
-    }
+    for (int m = 0; m < MT; ++m) g[m][c] += q * xr[m][r];
   }
 }
 

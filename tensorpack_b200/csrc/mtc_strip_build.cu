@@ -197,7 +197,17 @@ __host__ bool fill_strip(const Ctx& c, int strip, const StripPlan& P, uint8_t* o
     for (int si = s0; si < s1; ++si) {
       const Step& S = P.steps[si];
       const int sb = step_bytes(S.kind, S.n0, S.n1);
-      const uint32_t d = make_desc(S.kind, S.n0, S.n1, sb);
+      // run of identical full steps starting here (only its first descriptor is read)
+      int run = 1;
+      if (full_counts(S.kind, S.n0, S.n1)) {
+        const bool head = si == s0 || P.steps[si - 1].kind != S.kind ||
+                          !full_counts(P.steps[si - 1].kind, P.steps[si - 1].n0, P.steps[si - 1].n1);
+        if (head)
+          while (si + run < s1 && run < kMaxRun && P.steps[si + run].kind == S.kind &&
+                 full_counts(S.kind, P.steps[si + run].n0, P.steps[si + run].n1))
+            ++run;
+      }
+      const uint32_t d = make_desc(S.kind, S.n0, S.n1, sb, run);
       memcpy(rec + 8 + 4 * (si - s0), &d, 4);
       int q[4][4];
       if (S.kind < kU2) {
@@ -412,6 +422,13 @@ extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, con
           MTC_REQUIRE(n0 <= 16 && n1 <= 16 && n0 + n1 >= 1, "mtc_strip_check: batch %u step %u counts", b, i);
         MTC_REQUIRE(sb == step_bytes(kind, n0, n1) && pos + (uint32_t)sb <= size,
                     "mtc_strip_check: batch %u step %u size", b, i);
+        MTC_REQUIRE(desc_full(d) == full_counts(kind, n0, n1), "mtc_strip_check: batch %u step %u full flag", b, i);
+        const int run = desc_run(d);
+        MTC_REQUIRE(run >= 1 && (run == 1 || desc_full(d)) && i + (uint32_t)run <= nst,
+                    "mtc_strip_check: batch %u step %u run length %d", b, i, run);
+        for (int r = 1; r < run; ++r)
+          MTC_REQUIRE(((ldu32(rec + 8 + 4 * (i + r)) ^ d) & 0x3FFFFFu) == 0,
+                      "mtc_strip_check: batch %u step %u run of unlike steps", b, i);
         const uint8_t* st = rec + pos;
         const int nent = kind < kU2 ? n0 : n0 + n1;
         for (int j = 0; j < nent; ++j) {
@@ -431,5 +448,48 @@ extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, con
       MTC_REQUIRE(pos == size, "mtc_strip_check: batch %u steps do not fill the record", b);
     }
   }
+  return MTC_OK;
+}
+
+// CTA partition of a strip stream for the decode kernel: contiguous ranges of
+// whole strips, balanced by record bytes over `target_ctas` CTAs, each range
+// holding at most `max_batches` batch records (or one strip, if a single
+// strip has more).  Writes (first strip, first batch) of every range and the
+// end pair into cta_part (2 (n_cta + 1) words, host), n_cta and the largest
+// range's batch count.
+extern "C" int mtc_strip_partition(const uint32_t* batch_off, const uint32_t* strip_batch, int32_t n_strips,
+                                   int32_t target_ctas, int32_t max_batches, int32_t max_ctas, uint32_t* cta_part,
+                                   int32_t* n_cta_out, uint32_t* max_cta_batches_out) {
+  clear_error();
+  MTC_REQUIRE(batch_off && strip_batch && cta_part && n_cta_out && max_cta_batches_out,
+              "mtc_strip_partition: null pointer argument");
+  MTC_REQUIRE(n_strips >= 1 && target_ctas >= 1 && max_batches >= 1 && max_ctas >= 1,
+              "mtc_strip_partition: bad sizes");
+  auto sbytes = [&](int s) { return (uint64_t)batch_off[strip_batch[s + 1]] - batch_off[strip_batch[s]]; };
+  auto sbat = [&](int s) { return strip_batch[s + 1] - strip_batch[s]; };
+  const uint64_t total = (uint64_t)batch_off[strip_batch[n_strips]];
+  uint64_t done = 0;
+  uint32_t most = 0;
+  int c = 0, s = 0;
+  cta_part[0] = 0;
+  cta_part[1] = 0;
+  while (s < n_strips) {
+    MTC_REQUIRE(c < max_ctas, "mtc_strip_partition: more than %d CTA ranges needed", max_ctas);
+    const uint64_t target = (total - done) / (uint64_t)std::max(1, target_ctas - c);
+    uint64_t bytes = 0;
+    uint32_t nb = 0;
+    do {
+      bytes += sbytes(s);
+      nb += sbat(s);
+      ++s;
+    } while (s < n_strips && nb + sbat(s) <= (uint32_t)max_batches && bytes + sbytes(s) / 2 <= target);
+    done += bytes;
+    most = std::max(most, nb);
+    ++c;
+    cta_part[2 * c] = (uint32_t)s;
+    cta_part[2 * c + 1] = strip_batch[s];
+  }
+  *n_cta_out = c;
+  *max_cta_batches_out = most;
   return MTC_OK;
 }

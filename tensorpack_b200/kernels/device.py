@@ -213,7 +213,7 @@ class DeviceStream:
             new.decode_counters = torch.zeros_like(self.decode_counters)
             new.status = torch.zeros_like(self.status)
         new._ws = {}
-        new._strip = None if self._strip is None else self._strip.with_own_counters()
+        new._strip = self._strip  # read-only on the device: shared
         return new
 
     # ------------------------------------------------------------------ saving / loading
@@ -328,16 +328,9 @@ class DeviceStream:
         ``ep`` from ``epilogue()`` fuses a bias and activation."""
         lib = _lib.load()
         st = self.strip()
-        M = X.shape[0]
-        need = int(lib.mtc_strip_workspace_bytes(ctypes.byref(st.desc), M))
-        ws = self._ws.get("strip")
-        if ws is None or ws.numel() < need:
-            ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
-            self._ws["strip"] = ws
-        _lib.check(lib.mtc_strip_decode(ctypes.byref(st.desc), X.data_ptr(), M, X.stride(0), _ptr(self.row_perm),
-                                        _ptr(self.col_perm), Y.data_ptr(), Y.stride(0), ws.data_ptr(), ws.numel(),
-                                        st.counters.data_ptr(), self.status.data_ptr(), _ep(ep),
-                                        _stream(self.device)), "strip decode")
+        _lib.check(lib.mtc_strip_decode(ctypes.byref(st.desc), X.data_ptr(), X.shape[0], X.stride(0),
+                                        _ptr(self.row_perm), _ptr(self.col_perm), Y.data_ptr(), Y.stride(0),
+                                        self.status.data_ptr(), _ep(ep), _stream(self.device)), "strip decode")
         return Y
 
     def prefill_workspace(self, M: int) -> torch.Tensor:
@@ -407,9 +400,6 @@ class DeviceStream:
             self.status.zero_()
             self.counters.zero_()
             self.decode_counters.zero_()
-            strip = getattr(self, "_strip", None)
-            if strip is not None:
-                strip.counters.zero_()
             bits = []
             if v & _lib.STATUS_TIMEOUT:
                 bits.append("pipeline wait timed out")
@@ -422,28 +412,24 @@ class DeviceStream:
 
 class DeviceStrip:
     """The strip stream of one matrix on one device: batch records, batch
-    offsets, per-strip batch ranges (uploaded from a HostStripStream), the
-    C descriptor and the kernel's ticket / schedule words."""
+    offsets and per-strip batch ranges (uploaded from a HostStripStream),
+    the CTA partition for this device's SM count, and the C descriptor."""
 
     def __init__(self, hs, device):
         dev = torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
         with torch.cuda.device(dev):
             self.stream = torch.from_numpy(hs.stream).to(dev)
             self.batch_off = torch.from_numpy(hs.batch_off.view(np.int32)).to(dev)
             self.strip_batch = torch.from_numpy(hs.strip_batch.view(np.int32)).to(dev)
-            self.counters = torch.zeros(hs.n_strips + 2, dtype=torch.int32, device=dev)
+        sms = int(_lib.load().mtc_device_sm_count(dev.index))
+        self.cta_part, self.n_cta, self.max_cta_batches = hs.partition(max(sms, 1))
         self.host = hs
         self.device = dev
-        self.desc = hs.desc(self.stream.data_ptr(), self.batch_off.data_ptr(), self.strip_batch.data_ptr())
+        self.desc = hs.desc(self.stream.data_ptr(), self.batch_off.data_ptr(), self.strip_batch.data_ptr(),
+                            self.cta_part, self.n_cta, self.max_cta_batches)
 
     @property
     def stream_bytes(self) -> int:
         return int(self.host.batch_off[-1])
-
-    def with_own_counters(self) -> "DeviceStrip":
-        import copy
-
-        new = copy.copy(self)
-        new.counters = torch.zeros_like(self.counters)
-        new.desc = _lib.StripDesc.from_buffer_copy(self.desc)
-        return new

@@ -28,9 +28,14 @@ namespace {
 constexpr int MT = kMaxM;
 
 template <int C, bool G>
-void fast_lanes(const uint8_t* st, int n0, int n1, const uint16_t* x16, int kpad, uint32_t a[32][8],
+void fast_lanes(const uint8_t* st, int n0, int n1, bool full, const uint16_t* x16, int kpad, uint32_t a[32][8],
                 uint32_t b[32][MT][2]) {
-  for (int L = 0; L < 32; ++L) lane_fast<C, G, MT>(st, n0, n1, L, x16, kpad, a[L], b[L]);
+  for (int L = 0; L < 32; ++L) {
+    if (full)
+      lane_fast<C, G, true, MT>(st, n0, n1, L, x16, kpad, a[L], b[L]);
+    else
+      lane_fast<C, G, false, MT>(st, n0, n1, L, x16, kpad, a[L], b[L]);
+  }
 }
 
 // D = A (16x16) x B (16x8) of one mma from the lanes' fragments.
@@ -74,9 +79,21 @@ extern "C" int strip_model_gemm(const uint8_t* stream, const uint32_t* batch_off
     const uint32_t nst = ldu32(base + 4);
     const uint8_t* st = base + pad16(8 + 4 * (int)nst);
     double* out = part.data() + (size_t)bi * MT * 8;
+    uint32_t run_d = 0;
+    int run_left = 0;
     for (uint32_t s = 0; s < nst; ++s) {
-      const uint32_t d = ldu32(base + 8 + 4 * s);
+      // inside a run the kernel reuses the run's first descriptor
+      uint32_t d = ldu32(base + 8 + 4 * s);
+      if (run_left > 0) {
+        d = run_d;
+        --run_left;
+      } else if (desc_run(d) > 1) {
+        run_d = d;
+        run_left = desc_run(d) - 1;
+      }
       const int kind = desc_kind(d), n0 = desc_n0(d), n1 = desc_n1(d);
+      const bool full = desc_full(d);
+      if (full != full_counts(kind, n0, n1)) return -3;
       if (kind == kGeneric) {
         for (int L = 0; L < 32; ++L) {
           float g[MT][4] = {};
@@ -86,18 +103,18 @@ extern "C" int strip_model_gemm(const uint8_t* stream, const uint32_t* batch_off
         }
       } else {
         switch (kind) {
-          case kG2: fast_lanes<0, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kG3: fast_lanes<1, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kG4: fast_lanes<2, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kG5: fast_lanes<3, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kG6: fast_lanes<4, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kG8: fast_lanes<5, true>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU2: fast_lanes<0, false>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU3: fast_lanes<1, false>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU4: fast_lanes<2, false>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU5: fast_lanes<3, false>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU6: fast_lanes<4, false>(st, n0, n1, x16.data(), kpad, a, b); break;
-          case kU8: fast_lanes<5, false>(st, n0, n1, x16.data(), kpad, a, b); break;
+          case kG2: fast_lanes<0, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kG3: fast_lanes<1, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kG4: fast_lanes<2, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kG5: fast_lanes<3, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kG6: fast_lanes<4, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kG8: fast_lanes<5, true>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU2: fast_lanes<0, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU3: fast_lanes<1, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU4: fast_lanes<2, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU5: fast_lanes<3, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU6: fast_lanes<4, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
+          case kU8: fast_lanes<5, false>(st, n0, n1, full, x16.data(), kpad, a, b); break;
           default: return -2;
         }
         for (int m = 0; m < MT; ++m)

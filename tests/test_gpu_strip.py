@@ -5,8 +5,8 @@ Through the C ABI (DeviceStream.decode_strip) against:
     permutation.py:76-79): relative Frobenius error < 2e-3 (north-star bar);
   * the exact emulation of the products the kernel forms (tests/strip_emul.py):
     < 1e-5, i.e. fp32 accumulation order only;
-and checks the fused epilogue, determinism, the zeroed tickets after each
-call, and the Llama-3-8B gate shape against the tensor-core decode.
+and checks the fused epilogue, determinism and the Llama-3-8B gate shape
+against the tensor-core decode.
 """
 
 import os
@@ -18,8 +18,7 @@ import inputs
 from oracle import mtc_oracle as O
 from strip_emul import emulated_product
 
-# Not yet in the `-m gpu` set: selected explicitly until its first GPU run.
-pytestmark = pytest.mark.skipif(not __import__("torch").cuda.is_available(), reason="needs a CUDA device")
+pytestmark = pytest.mark.gpu
 
 TOL_REF = 2e-3
 TOL_EMUL = 1e-5
@@ -54,7 +53,6 @@ def run_strip(m, X, dev, ep=None):
     ds.decode_strip(Xd, Y, ep)
     torch.cuda.synchronize()
     ds.check_status()
-    assert int(ds.strip().counters.abs().sum().item()) == 0, "tickets / schedule not left zero"
     return Y.cpu().numpy()
 
 

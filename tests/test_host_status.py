@@ -4,7 +4,7 @@ A kernel that gives up part-way (a bounded wait that ran out, a tile record
 that failed a bounds check, activations beyond the fp16 range) sets
 MTC_STATUS_* bits; ``DeviceStream.check_status`` turns them into a
 RuntimeError and restores the zero state of the split-K ticket arrays that
-the next call relies on (strip-kernel tickets and schedule words included).
+the next call relies on.
 """
 
 import pytest
@@ -19,8 +19,6 @@ def stream_with(status):
     ds.status = torch.tensor([status], dtype=torch.int32)
     ds.counters = torch.tensor([3, 0, 1], dtype=torch.int32)
     ds.decode_counters = torch.tensor([2, 5, 0, 0, 1, 0], dtype=torch.int32)
-    ds._strip = type("StripState", (), {})()
-    ds._strip.counters = torch.tensor([0, 4, 1, 7], dtype=torch.int32)
     return ds
 
 
@@ -43,5 +41,4 @@ def test_failed_call_raises_and_clears_tickets(bits, text):
         ds.check_status()
     assert int(ds.status.item()) == 0
     assert not ds.counters.any() and not ds.decode_counters.any()
-    assert not ds._strip.counters.any()
     ds.check_status()  # reported once

@@ -185,3 +185,33 @@ def test_stream_bytes_near_accounted(golden_dir):
     hs = strip.build_host(m)
     ratio = int(hs.batch_off[-1]) / (m.accounted_bits / 8)
     assert ratio < 1.25, ratio
+
+
+@pytest.mark.parametrize("target", [1, 5, 13, 64, 148, 400])
+def test_cta_partition_covers_and_balances(golden_dir, target):
+    """Ranges of whole strips cover the stream in order, respect the batch
+    cap, and no range exceeds the mean by more than one strip."""
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, inner = _qt(golden_dir, "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    hs = strip.build_host(m, batch_bytes=2048)
+    for cap in (strip.CTA_BATCHES, 3):
+        part, n, most = hs.partition(target, max_batches=cap)
+        s_, b_ = part[0::2].astype(np.int64), part[1::2].astype(np.int64)
+        assert len(s_) == n + 1 and s_[0] == 0 and b_[0] == 0
+        assert s_[-1] == hs.n_strips and b_[-1] == hs.n_batches
+        assert (np.diff(s_) >= 1).all() and np.array_equal(b_, hs.strip_batch[s_].astype(np.int64))
+        nb = np.diff(b_)
+        assert most == nb.max()
+        single = np.diff(s_) == 1
+        assert ((nb <= cap) | single).all()
+        if cap == strip.CTA_BATCHES:
+            assert n <= target
+            off = hs.batch_off.astype(np.int64)
+            cta_bytes = off[b_[1:]] - off[b_[:-1]]
+            strip_bytes = np.diff(off[hs.strip_batch.astype(np.int64)])
+            assert cta_bytes.max() <= off[-1] / n + strip_bytes.max()
