@@ -12,9 +12,11 @@ tensorpack_b200.quant.
   value     prefill: Y = X @ W at M = 4096 through the fused dequant +
             tcgen05 path (gather, GEMM, column scatter), TFLOP/s = 2 M K N / t,
             L2 flushed before every step (256 MB write)
-  decode    M = 1 through the tensor-core decode kernel, GB/s of accounted packed
-            bytes (payload + scales + modes + split flags + permutation
-            indices), rotating over copies of the stream totalling > 4x L2
+  decode    M = 1 through the strip-stream decode kernel (mma.sync over
+            precision-sorted steps; --decode-kernel tensor for the tcgen05
+            decode), GB/s of accounted packed bytes (payload + scales + modes
+            + split flags + permutation indices), rotating over copies of the
+            stream totalling > 4x L2
   e2e       the prefill metric through the public API with pinned host X and
             Y: host->device copy, GEMM, device->host copy per step (one GPU:
             tensorpack_b200.kernels.gemm.HostGemm, which overlaps the copies
@@ -194,9 +196,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--decode-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decode-kernel", default="tensor", choices=["tensor", "strip"],
-                    help="decode M = 1 through the tcgen05 kernel over the sub-stage images (tensor) or the "
-                         "mma.sync kernel over the strip stream (strip)")
+    ap.add_argument("--decode-kernel", default="strip", choices=["tensor", "strip"],
+                    help="decode M = 1 through the mma.sync kernel over the strip stream (strip, default) or the "
+                         "tcgen05 kernel over the sub-stage images (tensor)")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
                     help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
@@ -434,9 +436,13 @@ def main():
                          "kernel": "prefill_kernel (fused dequant + tcgen05)", "peak_source": peak_src,
                          "kernel_ms": kern_ms},
             "decode": {"value": dec_gbs, "unit": "GB/s", "us_per_call": dec_us, "M": 1,
-                       "accounted_bytes": accounted_bytes, "device_bytes": ds.device_bytes,
+                       "kernel": "strip_kernel (mma.sync over the strip stream)" if args.decode_kernel == "strip"
+                       else "decode_kernel (tcgen05 over the sub-stage images)",
+                       "accounted_bytes": accounted_bytes, "device_bytes": stream_bytes,
                        "roofline": {"bound": "hbm", "achieved": dec_local_gbs, "peak": hbm_peak, "unit": "GB/s",
-                                    "frac": dec_local_gbs / hbm_peak, "traffic": committed_traffic("decode_kernel"),
+                                    "frac": dec_local_gbs / hbm_peak,
+                                    "traffic": committed_traffic("strip_kernel" if args.decode_kernel == "strip"
+                                                                 else "decode_kernel"),
                                     "peak_source": peak_src},
                        "copies_rotated": copies},
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
