@@ -186,9 +186,9 @@ class DeviceStream:
         self.source = getattr(self, "source", "repack")  # "repack" or "file" (uploaded by from_buffers)
         self._mat = mat          # host layout, for the strip stream built on first use
         self._strip = None
-        # decode kernel for M <= 4: "tensor" (tcgen05 over the sub-stage images)
-        # or "strip" (mma.sync over the strip stream)
-        self.decode_kernel = "tensor"
+        # decode kernel for M <= 4: "strip" (mma.sync over the strip stream,
+        # built on first use) or "tensor" (tcgen05 over the sub-stage images)
+        self.decode_kernel = "strip"
 
     def with_perms(self, row_perm, col_perm) -> "DeviceStream":
         """The same packed stream (buffers shared, nothing repacked) with other
@@ -380,8 +380,9 @@ class DeviceStream:
                    "prefill scatter")
 
     def matmul(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
-        """Y = X @ W (+ the fused epilogue ``ep``), picking the decode kernel
-        for M <= 16 and the tensor-core prefill kernel above."""
+        """Y = X @ W (+ the fused epilogue ``ep``): the strip-stream decode for
+        M <= 4 (``decode_kernel = "tensor"`` selects the tcgen05 decode), the
+        tcgen05 decode for M <= 16, the tensor-core prefill kernel above."""
         M = X.shape[0]
         if M <= STRIP_MAX_M and self.decode_kernel == "strip":
             return self.decode_strip(X, Y, ep)

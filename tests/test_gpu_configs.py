@@ -7,11 +7,13 @@ checks:
     allocation bit for bit (mtc/core/quadtree.py:157-171,
     mtc/core/permutation.py:76-79), and the packed bits equal the allocation's
     accounted bits (tests/test_allocation.py:85-86);
-  * Y = mtc_gemm(X, W) (the decode kernel for M <= 16, the prefill kernel
-    above) is within the north-star relative Frobenius error 2e-3
-    (mtc/eval/reference.py:31-38) of the fp64 product with that dequant, and
-    within 1e-5 of the fp64 product of the exact fp16 operands the tensor
-    cores consume (accumulation order only).  The second bound grows in
+  * Y = mtc_gemm(X, W) (the strip-stream decode for M <= 4, the tcgen05
+    decode for M <= 16, the prefill kernel above) is within the north-star
+    relative Frobenius error 2e-3 (mtc/eval/reference.py:31-38) of the fp64
+    product with that dequant, and within 1e-5 of the fp64 product of the
+    exact operands the kernel forms (accumulation order only; for the strip
+    decode q * fp16(fp16(x) fp16(s 2^e)), tests/strip_emul.py).  The second
+    bound grows in
     proportion to K beyond K = 4096: the prefill accumulates the whole
     reduction in one fp32 TMEM accumulator, one rounding per 16-deep MMA
     step, and at K = 14336 (896 steps) its error against the exact product
@@ -83,6 +85,9 @@ def check_layer(m, stored, pr, pc, Xs, dev):
 
     deq = stored if pr is None else O.unpermute(stored, pr, pc)
     assert np.array_equal(m.to_array(), deq)
+    from strip_emul import emulated_product_torch
+    from test_gpu_parity import uses_strip
+
     ds = m.device_stream(dev)
     W64 = torch.from_numpy(deq).to(dev).double()
     w16 = torch.from_numpy(O.fp16_weight_oracle(stored, ds.exp2)).to(dev).double() * 2.0 ** (-ds.exp2)
@@ -97,13 +102,17 @@ def check_layer(m, stored, pr, pc, Xs, dev):
         assert Y.shape == (Xt.shape[0], m.shape[1]) and Y.dtype == torch.float32
         X64 = Xt.double()
         e_ref = rel_frob(X64 @ W64, Y)
-        x16 = (Xt if pr_t is None else Xt[:, pr_t]).half().double()
-        Yp = x16 @ w16
-        if pc_t is None:
-            ref16 = Yp
+        if uses_strip(ds, Xt.shape[0]):  # exact operands of the strip-stream decode
+            x16 = Yp = None
+            ref16 = emulated_product_torch(m, stored, Xt.float(), ds.strip().host.exp2)
         else:
-            ref16 = torch.empty_like(Yp)
-            ref16[:, pc_t] = Yp
+            x16 = (Xt if pr_t is None else Xt[:, pr_t]).half().double()
+            Yp = x16 @ w16
+            if pc_t is None:
+                ref16 = Yp
+            else:
+                ref16 = torch.empty_like(Yp)
+                ref16[:, pc_t] = Yp
         e16 = rel_frob(ref16, Y)
         print(f"K={m.shape[0]} N={m.shape[1]} M={Xt.shape[0]}: vs reference dequant {e_ref:.3e}, "
               f"vs fp16 operands {e16:.3e}")

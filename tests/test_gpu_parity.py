@@ -7,8 +7,10 @@ CPU oracle and the golden fixtures produced by the reference:
     gemm.py:510-538);
   * GEMM outputs must be within relative Frobenius error 2e-3 of the fp64
     product with the reference dequant, and within
-    1e-5 of the same product computed from the fp16 operands the tensor cores
-    consume (which isolates accumulation-order differences).
+    1e-5 of the same product computed from the exact operands the kernel
+    forms (which isolates accumulation-order differences): fp16(q s 2^e) and
+    fp16(x) for the tcgen05 kernels, q and fp16(fp16(x) fp16(s 2^e)) for the
+    strip-stream decode that serves M <= 4.
 """
 
 import os
@@ -18,6 +20,7 @@ import pytest
 
 import inputs
 from oracle import mtc_oracle as O
+from strip_emul import emulated_product
 
 pytestmark = pytest.mark.gpu
 
@@ -71,12 +74,21 @@ def run_gemm(m, X, dev):
     return Y.cpu().numpy()
 
 
+def uses_strip(ds, M):
+    from tensorpack_b200.kernels.device import STRIP_MAX_M
+
+    return M <= STRIP_MAX_M and ds.decode_kernel == "strip"
+
+
 def check_gemm(m, W_deq_orig, W_stored, X, dev):
     ds = m.device_stream(dev)
     Y = run_gemm(m, X, dev)
     ref = X.astype(np.float64) @ W_deq_orig.astype(np.float64)
     e_ref = O.relative_frobenius_error(ref, Y)
-    e16 = O.relative_frobenius_error(fp16_product(X, W_stored, ds.exp2, m.row_perm, m.col_perm), Y)
+    if uses_strip(ds, X.shape[0]):
+        e16 = O.relative_frobenius_error(emulated_product(m, W_deq_orig, X, ds.strip().host.exp2)[0], Y)
+    else:
+        e16 = O.relative_frobenius_error(fp16_product(X, W_stored, ds.exp2, m.row_perm, m.col_perm), Y)
     assert e_ref < TOL_REF, e_ref
     assert e16 < TOL_F16, e16
     return Y
@@ -205,8 +217,8 @@ def test_gemv_forced_modes(dev, M):
 
 @pytest.mark.parametrize("M", [1, 5, 16])
 def test_cuda_core_gemv_matches_reference(golden_dir, dev, M):
-    """mtc_gemv (split-K mma.sync kernel, also behind mtc_gemv_static) against the reference; mtc_gemm itself
-    routes M <= 16 to the tensor-core mtc_decode."""
+    """mtc_gemv (split-K mma.sync kernel, also behind mtc_gemv_static) against the reference and against the
+    tensor-core mtc_decode (mtc_gemm routes M <= 4 to the strip decode and 5..16 to mtc_decode)."""
     import torch
 
     from tensorpack_b200.kernels.gemm import MTCMatrix
