@@ -223,9 +223,9 @@ MTC_API int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int64_
 
 /* Decode GEMM (M <= 16) that allocates nothing and takes no workspace.  No
  * counterpart in the reference: it exists for callers that cannot allocate
- * device memory when they run a step (inside a graph capture or an allocator
- * hook, or a plugin whose host framework only hands over inputs and
- * outputs).  Same arguments and result as mtc_gemv minus the scratch; the
+ * device memory when they run a step (an allocator hook, a real-time loop
+ * that must not take the allocator's lock, or a plugin whose host framework
+ * owns the device heap and only hands over inputs and outputs).  Same arguments and result as mtc_gemv minus the scratch; the
  * split-K partial sums and band tickets live in an 8 MiB array built into
  * the library (held on every GPU that loads it until process exit), which
  * limits the matrix to 4096 column bands (N <= 1,048,576) and to partial

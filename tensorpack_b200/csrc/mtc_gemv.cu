@@ -347,7 +347,7 @@ extern "C" int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int
 // Decode GEMM without caller-provided scratch.
 //
 // Some callers cannot allocate device memory at the point where they run a
-// decode step: code inside a CUDA-graph capture or an allocator hook, a
+// decode step: code inside an allocator hook, a
 // plugin whose host framework owns the device heap and hands it only input
 // and output buffers, or a real-time loop that must not take the allocator's
 // lock.  mtc_gemv_static serves them: it runs the same split-K kernel as

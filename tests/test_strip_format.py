@@ -215,3 +215,82 @@ def test_cta_partition_covers_and_balances(golden_dir, target):
             cta_bytes = off[b_[1:]] - off[b_[:-1]]
             strip_bytes = np.diff(off[hs.strip_batch.astype(np.int64)])
             assert cta_bytes.max() <= off[-1] / n + strip_bytes.max()
+
+
+def _llm_host(batch_bytes=2048):
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, inner = _qt(os.path.join(ROOT, "tests", "golden"), "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    return strip.build_host(m, batch_bytes=batch_bytes)
+
+
+@pytest.mark.parametrize("damage", ["strip", "nsteps", "kind", "count", "size", "run", "row", "offset", "cover"])
+def test_validator_rejects_damaged_streams(damage):
+    """mtc_strip_check, which gates every upload, names the first bad record."""
+    import copy
+
+    from tensorpack_b200.core import strip
+
+    hs = _llm_host()
+    bad = copy.deepcopy(hs)
+    o = int(bad.batch_off[3])
+    words = bad.stream[o:o + 64].view(np.uint32)  # header + descriptors of batch 3
+    if damage == "strip":
+        words[0] += 1
+    elif damage == "nsteps":
+        words[1] = 10 ** 6
+    elif damage == "kind":
+        words[2] = (words[2] & ~np.uint32(15)) | np.uint32(13)
+    elif damage == "count":
+        words[2] = (words[2] & ~np.uint32(31 << 5)) | np.uint32(9 << 5)
+    elif damage == "size":
+        words[2] = words[2] + np.uint32(1 << 15)
+    elif damage == "run":
+        words[2] = (words[2] & np.uint32(0x3FFFFF)) | np.uint32(1000 << 22)
+    elif damage == "row":
+        nst = int(words[1])
+        st = o + ((8 + 4 * nst + 15) // 16) * 16
+        bad.stream[st + 2:st + 4] = 0xFF  # first entry's k row
+    elif damage == "offset":
+        bad.batch_off[5] += 16
+    elif damage == "cover":
+        bad.strip_batch[-1] -= 1
+    with pytest.raises(ValueError, match="strip stream"):
+        strip.check(bad)
+    strip.check(hs)  # the undamaged stream passes
+
+
+def test_decode_rejects_bad_arguments_without_a_gpu():
+    """Argument and partition checks come before any CUDA call."""
+    import ctypes
+
+    from tensorpack_b200 import _lib
+
+    lib = _lib.load()
+    hs = _llm_host()
+    part, n, most = hs.partition(4)
+    d = hs.desc(16, 16, 16, part, n, most)  # fake device pointers: nothing is launched
+    X = Y = 16
+
+    def call(desc, M=1, ldx=256, ldy=512):
+        return lib.mtc_strip_decode(ctypes.byref(desc), X, M, ldx, None, None, Y, ldy, None, None, None)
+
+    for M in (0, 5):
+        assert call(d, M=M) == _lib.MTC_ERR_INVALID and b"M=" in lib.mtc_last_error()
+    assert call(d, ldx=255) == _lib.MTC_ERR_INVALID
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.n_cta = 0
+    assert call(bad) == _lib.MTC_ERR_INVALID
+    short = part.copy()
+    short[-2] -= 1  # ranges no longer reach the last strip
+    bad = hs.desc(16, 16, 16, short, n, most)
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"partition" in lib.mtc_last_error()
+    bad = hs.desc(16, 16, 16, part, n, 1)  # a range with more batches than max_cta_batches
+    assert call(bad) == _lib.MTC_ERR_INVALID
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.stream = 8  # not 16-byte aligned
+    assert call(bad) == _lib.MTC_ERR_INVALID

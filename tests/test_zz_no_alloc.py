@@ -1,8 +1,8 @@
 """The decode GEMM entry point that allocates nothing (mtc_gemv_static).
 
 It is for callers that cannot allocate device memory when they run a decode
-step (graph capture, allocator hooks, plugins that only receive inputs and
-outputs): its split-K scratch is an array built into the library.  Called
+step (allocator hooks, real-time loops that must not take the allocator's
+lock, plugins that only receive inputs and outputs): its split-K scratch is an array built into the library.  Called
 through the C ABI, twice in a row, it must agree with the workspace-taking
 entry point mtc_gemv within the fp16-operand tolerance of the other GPU tests
 (the two may split K differently, so summation order can differ).  The file
