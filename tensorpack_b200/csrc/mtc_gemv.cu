@@ -347,10 +347,9 @@ extern "C" int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int
 // Decode GEMM without caller-provided scratch.
 //
 // Some callers cannot allocate device memory at the point where they run a
-// decode step: code inside an allocator hook, a
-// plugin whose host framework owns the device heap and hands it only input
-// and output buffers, or a real-time loop that must not take the allocator's
-// lock.  mtc_gemv_static serves them: it runs the same split-K kernel as
+// decode step: code inside an allocator hook, a plugin whose host framework
+// owns the device heap and hands it only input and output buffers, or a
+// real-time loop that must not take the allocator's lock.  mtc_gemv_static serves them: it runs the same split-K kernel as
 // mtc_gemv, with its scratch (the partial sums of the split-K units and the
 // per-band tickets) taken from the fixed array below instead of from a
 // workspace argument.  It calls no cudaMalloc / cudaFree.
