@@ -262,6 +262,8 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
  * for the byte layout.  All pointers but cta_part are device pointers for
  * mtc_strip_decode. */
 #define MTC_STRIP_MAX_CTA 480     /* most CTA ranges of one strip-kernel launch */
+#define MTC_STRIP_WIDE 1u         /* stream flag: group steps of 16 groups, each lane both column quartets
+                                     of one group's k half (four MMAs per B fragment) */
 
 typedef struct mtc_strip_desc {
   const uint8_t* stream;        /* batch records, 16-byte aligned */
@@ -276,6 +278,8 @@ typedef struct mtc_strip_desc {
   uint32_t max_batch_bytes;     /* largest batch record */
   int32_t n_cta;                /* CTA ranges, 1..MTC_STRIP_MAX_CTA */
   uint32_t max_cta_batches;     /* most batch records in one CTA range */
+  uint32_t flags;               /* MTC_STRIP_* flags the stream was built with */
+  int32_t pad_;
   uint64_t stream_bytes;
 } mtc_strip_desc;
 
@@ -286,16 +290,17 @@ typedef struct mtc_strip_desc {
  * 2^exp2 (choose it so the largest |scale| * 2^exp2 is at most 1); leaves of
  * P16 or whose pre-scaled scale is not exact in fp16 take the fp32 path.
  * Batch records hold at most `batch_bytes` bytes (2048..65536, multiple of
- * 16) and `batch_steps` steps.
+ * 16) and `batch_steps` steps.  `flags`: 0 or MTC_STRIP_WIDE.
  * plan: out4 = {stream bytes, n_batches, n_strips, largest batch record}.
  * fill: writes `stream` (stream bytes), `batch_off` (n_batches + 1) and
  *       `strip_batch` (n_strips + 1). */
 MTC_API int mtc_strip_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn,
-                           int32_t exp2, uint32_t batch_bytes, uint32_t batch_steps, uint64_t* out4);
+                           int32_t exp2, uint32_t batch_bytes, uint32_t batch_steps, uint32_t flags,
+                           uint64_t* out4);
 MTC_API int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc_leaf_in* leaves,
                            const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn, int32_t exp2,
-                           uint32_t batch_bytes, uint32_t batch_steps, uint8_t* stream, uint32_t* batch_off,
-                           uint32_t* strip_batch);
+                           uint32_t batch_bytes, uint32_t batch_steps, uint32_t flags, uint8_t* stream,
+                           uint32_t* batch_off, uint32_t* strip_batch);
 
 /* Validate a host strip stream (record offsets and sizes, strip ranges,
  * every step descriptor and entry row) before it is uploaded; the decode
@@ -303,7 +308,7 @@ MTC_API int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc
  * message naming the first bad record. */
 MTC_API int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, const uint32_t* batch_off,
                             const uint32_t* strip_batch, int32_t n_batches, int32_t n_strips, int32_t tk,
-                            uint32_t max_batch_bytes);
+                            uint32_t max_batch_bytes, uint32_t flags);
 
 /* Split a strip stream into CTA ranges for mtc_strip_decode (host pointers,
  * no CUDA call): contiguous ranges of whole strips balanced by record bytes

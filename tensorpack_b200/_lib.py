@@ -55,11 +55,12 @@ class StripDesc(ctypes.Structure):
         ("stream", c_p), ("batch_off", c_p), ("strip_batch", c_p), ("cta_part", c_p),
         ("K", c_i32), ("N", c_i32), ("tk", c_i32), ("tn", c_i32),
         ("n_strips", c_i32), ("n_batches", c_i32), ("exp2", c_i32), ("max_batch_bytes", c_u32),
-        ("n_cta", c_i32), ("max_cta_batches", c_u32), ("stream_bytes", c_u64),
+        ("n_cta", c_i32), ("max_cta_batches", c_u32), ("flags", c_u32), ("pad_", c_i32), ("stream_bytes", c_u64),
     ]
 
 
-assert ctypes.sizeof(StripDesc) == 80
+assert ctypes.sizeof(StripDesc) == 88
+STRIP_WIDE = 1
 STRIP_MAX_CTA = 480
 
 
@@ -94,9 +95,9 @@ SIGNATURES = {
     "mtc_decode_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32]),
     "mtc_decode": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, c_size, c_p,
                            c_p, _EP, c_p]),
-    "mtc_strip_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, ctypes.POINTER(c_u64)]),
-    "mtc_strip_fill": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_p, c_p, c_p]),
-    "mtc_strip_check": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32]),
+    "mtc_strip_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_u32, ctypes.POINTER(c_u64)]),
+    "mtc_strip_fill": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_u32, c_p, c_p, c_p]),
+    "mtc_strip_check": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32]),
     "mtc_strip_partition": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, ctypes.POINTER(c_i32),
                                     ctypes.POINTER(c_u32)]),
     "mtc_strip_decode": (c_i32, [ctypes.POINTER(StripDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, _EP, c_p]),

@@ -53,6 +53,7 @@ class HostStripStream:
     batch_off: np.ndarray    # uint32 [n_batches + 1]
     strip_batch: np.ndarray  # uint32 [n_strips + 1]
     max_batch_bytes: int
+    flags: int = 0           # 0 or _lib.STRIP_WIDE
 
     @property
     def n_strips(self) -> int:
@@ -82,11 +83,15 @@ class HostStripStream:
             stream=stream_ptr, batch_off=batch_off_ptr, strip_batch=strip_batch_ptr, cta_part=cta_part.ctypes.data,
             K=self.K, N=self.N, tk=self.tk, tn=self.tn, n_strips=self.n_strips, n_batches=self.n_batches,
             exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, n_cta=n_cta, max_cta_batches=max_cta_batches,
-            stream_bytes=int(self.stream.nbytes))
+            flags=self.flags, stream_bytes=int(self.stream.nbytes))
 
 
-def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS) -> HostStripStream:
-    """Build the strip stream of an MTCMatrix on the host (no GPU needed)."""
+def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS,
+               wide: bool = False) -> HostStripStream:
+    """Build the strip stream of an MTCMatrix on the host (no GPU needed).
+    ``wide`` packs group steps of 16 groups with two micro-blocks per lane
+    (MTC_STRIP_WIDE; checked on the CPU model of the kernel only so far)."""
+    flags = _lib.STRIP_WIDE if wide else 0
     lib = _lib.load()
     K, N = (int(v) for v in mat.shape)
     ls = mat.leaf_set
@@ -97,16 +102,16 @@ def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STE
     begin = np.ascontiguousarray(begin, dtype=np.uint32)
     out = (ctypes.c_uint64 * 4)()
     _lib.check(lib.mtc_strip_plan(leaves.ctypes.data, begin.ctypes.data, tk, tn, exp2, batch_bytes, batch_steps,
-                                  out), "strip plan")
+                                  flags, out), "strip plan")
     total, n_batches, n_strips, max_batch = (int(v) for v in out)
     # 16 spare bytes so that every record can be read with 16-byte loads
     stream = np.zeros(total + 16, dtype=np.uint8)
     batch_off = np.zeros(n_batches + 1, dtype=np.uint32)
     strip_batch = np.zeros(n_strips + 1, dtype=np.uint32)
     _lib.check(lib.mtc_strip_fill(arena.ctypes.data, arena.nbytes, leaves.ctypes.data, begin.ctypes.data, tk, tn,
-                                  exp2, batch_bytes, batch_steps, stream.ctypes.data, batch_off.ctypes.data,
+                                  exp2, batch_bytes, batch_steps, flags, stream.ctypes.data, batch_off.ctypes.data,
                                   strip_batch.ctypes.data), "strip fill")
-    hs = HostStripStream(K, N, tk, tn, exp2, stream, batch_off, strip_batch, max_batch)
+    hs = HostStripStream(K, N, tk, tn, exp2, stream, batch_off, strip_batch, max_batch, flags)
     check(hs)
     return hs
 
@@ -116,4 +121,4 @@ def check(hs: HostStripStream) -> None:
     lib = _lib.load()
     _lib.check(lib.mtc_strip_check(hs.stream.ctypes.data, hs.stream.nbytes, hs.batch_off.ctypes.data,
                                    hs.strip_batch.ctypes.data, hs.n_batches, hs.n_strips, hs.tk,
-                                   hs.max_batch_bytes), "strip stream")
+                                   hs.max_batch_bytes, hs.flags), "strip stream")

@@ -97,9 +97,36 @@ __device__ __forceinline__ void partial_step(const uint8_t* st, int n0, int n1, 
   }
 }
 
+// Wide group steps (streams built with kWide): lane = (group, k half), both
+// quartets; four MMAs share the B fragment.  acc[j] holds columns 2j, 2j + 1
+// of the strip on every quad's diagonal.
+template <int C, bool FULL, int MT>
+__device__ __forceinline__ void wide_step(const uint8_t* st, int n, int lane, const uint16_t* x16, int kpad,
+                                          float accw[4][MT][4]) {
+  uint32_t a0[8], a1[8], b[MT][2];
+  lane_wide<C, FULL, MT>(st, n, lane, x16, kpad, a0, a1, b);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    mma_f16(accw[0][m], a0[0], a0[1], a0[2], a0[3], b[m][0], b[m][1]);
+    mma_f16(accw[1][m], a0[4], a0[5], a0[6], a0[7], b[m][0], b[m][1]);
+    mma_f16(accw[2][m], a1[0], a1[1], a1[2], a1[3], b[m][0], b[m][1]);
+    mma_f16(accw[3][m], a1[4], a1[5], a1[6], a1[7], b[m][0], b[m][1]);
+  }
+}
+template <int C, int MT>
+__device__ __forceinline__ void wide_run(int run, const uint8_t*& st, int lane, const uint16_t* x16, int kpad,
+                                         float accw[4][MT][4]) {
+  constexpr int BYTES = strip::pad16(64 + 64 * (prim_bytes(C) + sec_bytes(C)));
+#pragma unroll 2
+  for (int r = 0; r < run; ++r) {
+    wide_step<C, true, MT>(st, 16, lane, x16, kpad, accw);
+    st += BYTES;
+  }
+}
+
 // One batch record in shared memory -> its partial sums (lanes 0 .. 8 MT - 1
 // return the sum of column lane & 7 of token lane >> 3; other lanes 0).
-template <int MT>
+template <int MT, bool WIDE>
 __device__ __forceinline__ float process_batch(const uint8_t* base, int lane, const uint16_t* x16, int kpad,
                                                float* scr) {
   const uint32_t nst = ldu32(base + 4);
@@ -110,11 +137,41 @@ __device__ __forceinline__ float process_batch(const uint8_t* base, int lane, co
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc1[m][r] = acc2[m][r] = gacc[m][r] = 0.0f;
+  float accw[WIDE ? 4 : 1][MT][4];
+  if constexpr (WIDE) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) accw[j][m][r] = 0.0f;
+  }
   bool gen = false;
   uint32_t i = 0;
   while (i < nst) {
     const uint32_t d = ldu32(dsc + 4 * i);
     const int n0 = desc_n0(d), n1 = desc_n1(d), run = desc_run(d);
+    if constexpr (WIDE) {
+      if (desc_kind(d) < kU2) {
+        switch (d & 31u) {
+          case 16 + kG2: wide_run<0, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case 16 + kG3: wide_run<1, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case 16 + kG4: wide_run<2, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case 16 + kG5: wide_run<3, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case 16 + kG6: wide_run<4, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case 16 + kG8: wide_run<5, MT>(run, st, lane, x16, kpad, accw); i += run; continue;
+          case kG2: wide_step<0, false, MT>(st, n0, lane, x16, kpad, accw); break;
+          case kG3: wide_step<1, false, MT>(st, n0, lane, x16, kpad, accw); break;
+          case kG4: wide_step<2, false, MT>(st, n0, lane, x16, kpad, accw); break;
+          case kG5: wide_step<3, false, MT>(st, n0, lane, x16, kpad, accw); break;
+          case kG6: wide_step<4, false, MT>(st, n0, lane, x16, kpad, accw); break;
+          default: wide_step<5, false, MT>(st, n0, lane, x16, kpad, accw); break;
+        }
+        st += desc_bytes(d);
+        ++i;
+        continue;
+      }
+    }
     switch (d & 31u) {  // kind, plus 16 for a full step
       case 16 + kG2: full_run<0, true, MT>(run, st, lane, x16, kpad, acc1, acc2); i += run; continue;
       case 16 + kG3: full_run<1, true, MT>(run, st, lane, x16, kpad, acc1, acc2); i += run; continue;
@@ -164,6 +221,19 @@ __device__ __forceinline__ float process_batch(const uint8_t* base, int lane, co
       o[3] = odd ? acc2[m][3] : acc2[m][2];
     }
   }
+  if constexpr (WIDE) {  // wide accumulators: every quad holds all 8 columns
+    if (t == (g >> 1)) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float* o = scr + MT * 40 + (m * 8 + g) * 8;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o[2 * j] = odd ? accw[j][m][1] : accw[j][m][0];
+          o[2 * j + 1] = odd ? accw[j][m][3] : accw[j][m][2];
+        }
+      }
+    }
+  }
   if (gen) {  // generic lanes: column c of quartet lane >> 4 -> sum over each half warp
 #pragma unroll
     for (int m = 0; m < MT; ++m)
@@ -184,13 +254,18 @@ __device__ __forceinline__ float process_batch(const uint8_t* base, int lane, co
     const float* s = scr + m * 32 + 16 * h + c;
     v = s[0] + s[4] + s[8] + s[12];
     if (gen) v += scr[MT * 32 + (m * 2 + h) * 4 + c];
+    if constexpr (WIDE) {
+      const float* w = scr + MT * 40 + m * 64 + f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v += w[8 * q];
+    }
   }
   __syncwarp();
   return v;
 }
 
-template <int MT>
-__global__ void __launch_bounds__(MT == 4 ? 512 : 768, 1) strip_kernel(const StripParams p) {
+template <int MT, bool WIDE>
+__global__ void __launch_bounds__((MT == 4 || (WIDE && MT == 2)) ? 512 : 768, 1) strip_kernel(const StripParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nw = p.nw, ns = p.ns;
@@ -199,7 +274,7 @@ __global__ void __launch_bounds__(MT == 4 ? 512 : 768, 1) strip_kernel(const Str
   const int b0 = (int)p.part[2 * c + 1], b1 = (int)p.part[2 * c + 3];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [nw][ns]
   uint16_t* x16 = reinterpret_cast<uint16_t*>(smem + p.off_x);
-  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * (MT * 40);
+  float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * (MT * (WIDE ? 104 : 40));
   float* part = reinterpret_cast<float*>(smem + p.off_part);         // [cap][MT][8]
   uint32_t* meta = reinterpret_cast<uint32_t*>(smem + p.off_meta);   // tickets [cap], first batch [cap + 1], queue
   uint32_t* tick = meta;
@@ -324,7 +399,7 @@ __global__ void __launch_bounds__(MT == 4 ? 512 : 768, 1) strip_kernel(const Str
       abort = true;
       break;
     }
-    const float v = process_batch<MT>(base, lane, x16, p.kpad, scr);
+    const float v = process_batch<MT, WIDE>(base, lane, x16, p.kpad, scr);
     // refill the slot (its bytes are consumed)
     if (lane == 0 && nb < b1) {
       fence_proxy_async();
@@ -373,8 +448,10 @@ struct Plan {
   size_t smem;
 };
 
-bool make_plan(const mtc_strip_desc* s, int M, Plan* pl) {
-  if (M < 1 || M > kMaxM) return false;
+// Tokens per launch: 1, 2 or 4 (wide streams at most 2: four accumulators
+// per token).
+bool make_plan(const mtc_strip_desc* s, int M, bool wide, Plan* pl) {
+  if (M < 1 || M > (wide ? 2 : kMaxM)) return false;
   pl->mt = M == 1 ? 1 : M == 2 ? 2 : 4;
   pl->slot_bytes = (s->max_batch_bytes + 127u) & ~127u;
   pl->cap = (int)s->max_cta_batches;
@@ -384,12 +461,12 @@ bool make_plan(const mtc_strip_desc* s, int M, Plan* pl) {
   const size_t partb = up((size_t)pl->cap * pl->mt * 8 * 4);
   const size_t metab = up(((size_t)2 * pl->cap + 2) * 4);
   const size_t budget = 227 * 1024;
-  const int max_nw = pl->mt == 4 ? 16 : 24;
+  const int max_nw = (pl->mt == 4 || (wide && pl->mt == 2)) ? 16 : 24;
   // three slots per warp while at least 16 warps fit, else two
   for (int ns = kMaxSlots; ns >= 2; --ns)
     for (int nw = max_nw; nw >= 4; --nw) {
       const size_t bars = up((size_t)nw * ns * 8);
-      const size_t scr = up((size_t)nw * pl->mt * 40 * 4);
+      const size_t scr = up((size_t)nw * pl->mt * (wide ? 104 : 40) * 4);
       const size_t need = bars + xb + scr + partb + metab + (size_t)nw * ns * pl->slot_bytes;
       if (need <= budget && (ns == 2 || nw >= 16)) {
         pl->nw = nw;
@@ -435,56 +512,64 @@ extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t
   EpiArg e;
   int rc = read_epilogue(ep, &e, "mtc_strip_decode");
   if (rc) return rc;
-  Plan pl;
-  MTC_REQUIRE(make_plan(s, M, &pl), "mtc_strip_decode: K=%d / %u batches per CTA do not fit shared memory at M=%d",
-              s->K, s->max_cta_batches, M);
-  StripParams p;
-  p.stream = s->stream;
-  p.batch_off = s->batch_off;
-  p.strip_batch = s->strip_batch;
-  p.n_batches = s->n_batches;
-  p.n_strips = s->n_strips;
-  p.K = s->K;
-  p.N = s->N;
-  p.kpad = s->tk * 32;
-  p.inv_pow2e = ldexpf(1.0f, -s->exp2);
-  p.X = X;
-  p.ldx = ldx;
-  p.M = M;
-  p.pr = row_perm;
-  p.pc = col_perm;
-  p.Y = Y;
-  p.ldy = ldy;
-  p.status = status;
-  p.ep = Epi{e.bias, e.act};
-  p.timeout_ns = 2000000000ull;
-  p.nw = pl.nw;
-  p.ns = pl.ns;
-  p.cap = pl.cap;
-  p.slot_bytes = pl.slot_bytes;
-  p.off_x = pl.off_x;
-  p.off_scr = pl.off_scr;
-  p.off_part = pl.off_part;
-  p.off_meta = pl.off_meta;
-  p.off_slots = pl.off_slots;
-  for (int i = 0; i < 2 * (s->n_cta + 1); ++i) p.part[i] = s->cta_part[i];
+  const bool wide = (s->flags & MTC_STRIP_WIDE) != 0;
+  const int per = wide ? 2 : strip::kMaxM;  // tokens per launch
   cudaStream_t st = as_stream(stream);
-  static bool opted[3] = {false, false, false};
-  const int which = pl.mt == 1 ? 0 : pl.mt == 2 ? 1 : 2;
-  const void* fn = which == 0 ? (const void*)strip_kernel<1> : which == 1 ? (const void*)strip_kernel<2>
-                                                                          : (const void*)strip_kernel<4>;
-  if (!opted[which]) {
-    MTC_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                   "mtc_strip_decode: smem attribute");
-    opted[which] = true;
+  static bool opted[6] = {false, false, false, false, false, false};
+  for (int m0 = 0; m0 < M; m0 += per) {
+    const int Mi = M - m0 < per ? M - m0 : per;
+    Plan pl;
+    MTC_REQUIRE(make_plan(s, Mi, wide, &pl),
+                "mtc_strip_decode: K=%d / %u batches per CTA do not fit shared memory at M=%d", s->K,
+                s->max_cta_batches, Mi);
+    StripParams p;
+    p.stream = s->stream;
+    p.batch_off = s->batch_off;
+    p.strip_batch = s->strip_batch;
+    p.n_batches = s->n_batches;
+    p.n_strips = s->n_strips;
+    p.K = s->K;
+    p.N = s->N;
+    p.kpad = s->tk * 32;
+    p.inv_pow2e = ldexpf(1.0f, -s->exp2);
+    p.X = X + (long long)m0 * ldx;
+    p.ldx = ldx;
+    p.M = Mi;
+    p.pr = row_perm;
+    p.pc = col_perm;
+    p.Y = Y + (long long)m0 * ldy;
+    p.ldy = ldy;
+    p.status = status;
+    p.ep = Epi{e.bias, e.act};
+    p.timeout_ns = 2000000000ull;
+    p.nw = pl.nw;
+    p.ns = pl.ns;
+    p.cap = pl.cap;
+    p.slot_bytes = pl.slot_bytes;
+    p.off_x = pl.off_x;
+    p.off_scr = pl.off_scr;
+    p.off_part = pl.off_part;
+    p.off_meta = pl.off_meta;
+    p.off_slots = pl.off_slots;
+    for (int i = 0; i < 2 * (s->n_cta + 1); ++i) p.part[i] = s->cta_part[i];
+    const int which = (pl.mt == 1 ? 0 : pl.mt == 2 ? 1 : 2) + (wide ? 3 : 0);
+    const void* fns[6] = {(const void*)strip_kernel<1, false>, (const void*)strip_kernel<2, false>,
+                          (const void*)strip_kernel<4, false>, (const void*)strip_kernel<1, true>,
+                          (const void*)strip_kernel<2, true>,  (const void*)strip_kernel<2, true>};
+    if (!opted[which]) {
+      MTC_CHECK_CUDA(cudaFuncSetAttribute(fns[which], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                     "mtc_strip_decode: smem attribute");
+      opted[which] = true;
+    }
+    const dim3 grid(s->n_cta), block(pl.nw * 32);
+    switch (which) {
+      case 0: strip_kernel<1, false><<<grid, block, pl.smem, st>>>(p); break;
+      case 1: strip_kernel<2, false><<<grid, block, pl.smem, st>>>(p); break;
+      case 2: strip_kernel<4, false><<<grid, block, pl.smem, st>>>(p); break;
+      case 3: strip_kernel<1, true><<<grid, block, pl.smem, st>>>(p); break;
+      default: strip_kernel<2, true><<<grid, block, pl.smem, st>>>(p); break;
+    }
+    MTC_CHECK_LAUNCH("mtc_strip_decode");
   }
-  const dim3 grid(s->n_cta), block(pl.nw * 32);
-  if (which == 0)
-    strip_kernel<1><<<grid, block, pl.smem, st>>>(p);
-  else if (which == 1)
-    strip_kernel<2><<<grid, block, pl.smem, st>>>(p);
-  else
-    strip_kernel<4><<<grid, block, pl.smem, st>>>(p);
-  MTC_CHECK_LAUNCH("mtc_strip_decode");
   return MTC_OK;
 }

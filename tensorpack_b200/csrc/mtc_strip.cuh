@@ -81,12 +81,20 @@ __host__ __device__ constexpr int bias_of_class(int c) { return 1 << (mode_of_cl
 // compile-time constants.  The first step of a run of identical full steps
 // (same kind) carries the run's length, so the kernel loops over the run
 // without reading the following descriptors.
-__host__ __device__ constexpr bool full_counts(int kind, int n0, int n1) {
-  return kind < kU2 ? n0 == 8 : (n0 == 16 && n1 == 16);
+//
+// Wide streams (flag kWide): a group step holds up to 16 groups and lane L
+// takes both column quartets of group L >> 1, k half L & 1 (32 weights, four
+// MMAs sharing one B fragment).  Micro and generic steps are the same in both
+// forms.
+constexpr uint32_t kWide = 1u;  // stream flag (MTC_STRIP_WIDE)
+__host__ __device__ constexpr int group_step_max(bool wide) { return wide ? 16 : 8; }
+__host__ __device__ constexpr bool full_counts(int kind, int n0, int n1, bool wide = false) {
+  return kind < kU2 ? n0 == group_step_max(wide) : (n0 == 16 && n1 == 16);
 }
 constexpr int kMaxRun = 1023;  // 10-bit run length
-__host__ __device__ constexpr uint32_t make_desc(int kind, int n0, int n1, int bytes, int run = 1) {
-  return (uint32_t)kind | ((uint32_t)(full_counts(kind, n0, n1) ? 1 : 0) << 4) | ((uint32_t)n0 << 5) |
+__host__ __device__ constexpr uint32_t make_desc(int kind, int n0, int n1, int bytes, int run = 1,
+                                                 bool wide = false) {
+  return (uint32_t)kind | ((uint32_t)(full_counts(kind, n0, n1, wide) ? 1 : 0) << 4) | ((uint32_t)n0 << 5) |
          ((uint32_t)n1 << 10) | ((uint32_t)(bytes >> 4) << 15) | ((uint32_t)run << 22);
 }
 __host__ __device__ inline int desc_kind(uint32_t d) { return (int)(d & 15u); }
@@ -96,7 +104,8 @@ __host__ __device__ inline int desc_n1(uint32_t d) { return (int)((d >> 10) & 31
 __host__ __device__ inline int desc_bytes(uint32_t d) { return (int)(((d >> 15) & 127u) << 4); }
 __host__ __device__ inline int desc_run(uint32_t d) { return (int)(d >> 22); }
 
-// Bytes of a step record.
+// Bytes of a step record (the same in wide streams: a wide group step of n
+// groups has 2 n lanes of two micro-blocks each).
 __host__ __device__ inline int step_bytes(int kind, int n0, int n1) {
   if (kind < kU2) {
     const int c = kind, lanes = 4 * n0;
@@ -400,6 +409,54 @@ __host__ __device__ __forceinline__ void lane_fast(const uint8_t* step, int n0, 
   if constexpr (SB == 4) B = ldu32(pb);
   decode_lane<C>(A, B, a);
   const int xo = GROUP ? (int)(e >> 16) * 8 + (lane & 1) * 4 : (int)(e >> 16) * 4;
+  const uint32_t s2 = prmt(e, e, 0x1010u);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const uint8_t* xp = reinterpret_cast<const uint8_t*>(x16 + (size_t)m * kpad + xo);
+    uint32_t xw[2];
+    ldwords(xp, xw, 2);
+    b[m][0] = hmul2(xw[0], s2);
+    b[m][1] = hmul2(xw[1], s2);
+  }
+}
+
+// Wide group step lane: group L >> 1, k half L & 1, both quartets.  a0 / a1
+// are the A fragments of quartet 0 / 1 (columns 0-3 / 4-7 of the strip); b is
+// shared by the four MMAs.  Plane A holds the lane's two micro-blocks side by
+// side (2 prim_bytes), plane B likewise (2 sec_bytes).
+template <int C, bool FULL, int MT>
+__host__ __device__ __forceinline__ void lane_wide(const uint8_t* step, int n, int lane, const uint16_t* x16,
+                                                   int kpad, uint32_t a0[8], uint32_t a1[8], uint32_t b[MT][2]) {
+  constexpr int PB = prim_bytes(C), SB = sec_bytes(C);
+  const bool valid = FULL || lane < 2 * n;
+  const int idx = valid ? lane : 0;
+  const int lanes = FULL ? 32 : 2 * n;
+  const int E = FULL ? 64 : pad16(4 * n);
+  const uint32_t e = valid ? ldu32(step + 4 * (lane >> 1)) : 0u;
+  const uint8_t* pa = step + E + idx * 2 * PB;
+  const uint8_t* pb = step + E + lanes * 2 * PB + idx * 2 * SB;
+  uint32_t A[2 * PB / 4];
+  if constexpr (PB == 16) {
+    ldwords(pa, A, 4);
+    ldwords(pa + 16, A + 4, 4);
+  } else {
+    ldwords(pa, A, 2 * PB / 4);
+  }
+  uint32_t B0 = 0, B1 = 0;
+  if constexpr (SB == 2) {
+    const uint32_t w = ldu32(pb);
+    B0 = spread16(w & 0xFFFFu);
+    B1 = spread16(w >> 16);
+  }
+  if constexpr (SB == 4) {
+    uint32_t w[2];
+    ldwords(pb, w, 2);
+    B0 = w[0];
+    B1 = w[1];
+  }
+  decode_lane<C>(A, B0, a0);
+  decode_lane<C>(A + PB / 4, B1, a1);
+  const int xo = (int)(e >> 16) * 8 + (lane & 1) * 4;
   const uint32_t s2 = prmt(e, e, 0x1010u);
 #pragma unroll
   for (int m = 0; m < MT; ++m) {

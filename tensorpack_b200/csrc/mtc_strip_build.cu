@@ -36,6 +36,7 @@ struct Ctx {
   const uint8_t* arena;
   uint64_t arena_bytes;
   uint32_t batch_bytes, batch_steps;
+  bool wide;  // group steps of 16 groups, two micro-blocks per lane
 };
 
 // One item of a strip: a group (8 k x 8 features) or a micro-block (4 x 4).
@@ -119,9 +120,10 @@ __host__ bool plan_strip(const Ctx& c, int strip, StripPlan* P) {
     }
   }
   // steps in kind order
+  const int gmax = group_step_max(c.wide);
   for (int cls = 0; cls < 6; ++cls) {
     const int n = (int)P->grp[cls].size();
-    for (int i = 0; i < n; i += 8) P->steps.push_back(Step{kG2 + cls, std::min(8, n - i), 0, i, 0});
+    for (int i = 0; i < n; i += gmax) P->steps.push_back(Step{kG2 + cls, std::min(gmax, n - i), 0, i, 0});
   }
   auto split_steps = [&](int kind, const std::vector<Item>& L0, const std::vector<Item>& L1) {
     const int a = (int)L0.size(), b = (int)L1.size();
@@ -199,18 +201,45 @@ __host__ bool fill_strip(const Ctx& c, int strip, const StripPlan& P, uint8_t* o
       const int sb = step_bytes(S.kind, S.n0, S.n1);
       // run of identical full steps starting here (only its first descriptor is read)
       int run = 1;
-      if (full_counts(S.kind, S.n0, S.n1)) {
+      if (full_counts(S.kind, S.n0, S.n1, c.wide)) {
         const bool head = si == s0 || P.steps[si - 1].kind != S.kind ||
-                          !full_counts(P.steps[si - 1].kind, P.steps[si - 1].n0, P.steps[si - 1].n1);
+                          !full_counts(P.steps[si - 1].kind, P.steps[si - 1].n0, P.steps[si - 1].n1, c.wide);
         if (head)
           while (si + run < s1 && run < kMaxRun && P.steps[si + run].kind == S.kind &&
-                 full_counts(S.kind, P.steps[si + run].n0, P.steps[si + run].n1))
+                 full_counts(S.kind, P.steps[si + run].n0, P.steps[si + run].n1, c.wide))
             ++run;
       }
-      const uint32_t d = make_desc(S.kind, S.n0, S.n1, sb, run);
+      const uint32_t d = make_desc(S.kind, S.n0, S.n1, sb, run, c.wide);
       memcpy(rec + 8 + 4 * (si - s0), &d, 4);
       int q[4][4];
-      if (S.kind < kU2) {
+      if (S.kind < kU2 && c.wide) {
+        // wide group step: lane 2 gs + kr holds quartets 0 and 1 of group gs, k half kr
+        const int cls = S.kind, n = S.n0, PB = prim_bytes(cls), SB = sec_bytes(cls), lanes = 2 * n;
+        uint8_t* planes = st + pad16(4 * n);
+        for (int gs = 0; gs < n; ++gs) {
+          const Item& it = P.grp[cls][S.first0 + gs];
+          const mtc_leaf_in& L = c.leaves[it.leaf];
+          float sc;
+          memcpy(&sc, &L.scale_bits, 4);
+          const uint32_t e = (uint32_t)exact_f16(sc, c.exp2) | ((uint32_t)it.row << 16);
+          memcpy(st + 4 * gs, &e, 4);
+          for (int kr = 0; kr < 2; ++kr) {
+            const int lane = 2 * gs + kr;
+            for (int h = 0; h < 2; ++h) {
+              micro_codes(c, L, it.kt, 2 * it.row + kr, 2 * strip + h, q);
+              uint32_t A[4], B;
+              if (!pack_lane(cls, q, A, &B)) return false;
+              memcpy(planes + lane * 2 * PB + h * PB, A, PB);
+              if (SB == 2) {
+                const uint16_t b16 = (uint16_t)((B & 0xFFu) | ((B >> 8) & 0xFF00u));
+                memcpy(planes + lanes * 2 * PB + lane * 4 + h * 2, &b16, 2);
+              } else if (SB == 4) {
+                memcpy(planes + lanes * 2 * PB + lane * 8 + h * 4, &B, 4);
+              }
+            }
+          }
+        }
+      } else if (S.kind < kU2) {
         const int cls = S.kind, n = S.n0, PB = prim_bytes(cls), SB = sec_bytes(cls);
         uint8_t* planes = st + pad16(4 * n);
         for (int gs = 0; gs < n; ++gs) {
@@ -298,7 +327,8 @@ void parallel_for(int n, F f) {
 }
 
 int check_args(const mtc_leaf_in* leaves, const uint32_t* begin, int32_t tk, int32_t tn, uint32_t batch_bytes,
-               uint32_t batch_steps, const char* who) {
+               uint32_t batch_steps, uint32_t flags, const char* who) {
+  MTC_REQUIRE((flags & ~kWide) == 0, "%s: unknown stream flags 0x%x", who, flags);
   MTC_REQUIRE(leaves && begin, "%s: null pointer argument", who);
   MTC_REQUIRE(tk >= 1 && tn >= 1, "%s: bad tile grid %d x %d", who, tk, tn);
   MTC_REQUIRE(tk * 8 <= 65535, "%s: K of %d tiles exceeds the 16-bit micro-block row", who, tk);
@@ -314,12 +344,13 @@ int check_args(const mtc_leaf_in* leaves, const uint32_t* begin, int32_t tk, int
 using namespace mtc;
 
 extern "C" int mtc_strip_plan(const mtc_leaf_in* leaves, const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn,
-                              int32_t exp2, uint32_t batch_bytes, uint32_t batch_steps, uint64_t* out4) {
+                              int32_t exp2, uint32_t batch_bytes, uint32_t batch_steps, uint32_t flags,
+                              uint64_t* out4) {
   clear_error();
-  int rc = check_args(leaves, tile_leaf_begin, tk, tn, batch_bytes, batch_steps, "mtc_strip_plan");
+  int rc = check_args(leaves, tile_leaf_begin, tk, tn, batch_bytes, batch_steps, flags, "mtc_strip_plan");
   if (rc) return rc;
   MTC_REQUIRE(out4, "mtc_strip_plan: null out4");
-  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, nullptr, 0, batch_bytes, batch_steps};
+  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, nullptr, 0, batch_bytes, batch_steps, (flags & kWide) != 0};
   const int n_strips = tn * 4;
   std::vector<uint64_t> bytes(n_strips), nb(n_strips), mx(n_strips);
   std::atomic<int> bad(0);
@@ -346,10 +377,10 @@ extern "C" int mtc_strip_plan(const mtc_leaf_in* leaves, const uint32_t* tile_le
 
 extern "C" int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const mtc_leaf_in* leaves,
                               const uint32_t* tile_leaf_begin, int32_t tk, int32_t tn, int32_t exp2,
-                              uint32_t batch_bytes, uint32_t batch_steps, uint8_t* stream, uint32_t* batch_off,
-                              uint32_t* strip_batch) {
+                              uint32_t batch_bytes, uint32_t batch_steps, uint32_t flags, uint8_t* stream,
+                              uint32_t* batch_off, uint32_t* strip_batch) {
   clear_error();
-  int rc = check_args(leaves, tile_leaf_begin, tk, tn, batch_bytes, batch_steps, "mtc_strip_fill");
+  int rc = check_args(leaves, tile_leaf_begin, tk, tn, batch_bytes, batch_steps, flags, "mtc_strip_fill");
   if (rc) return rc;
   MTC_REQUIRE(arena && stream && batch_off && strip_batch, "mtc_strip_fill: null pointer argument");
   const int n_strips = tn * 4;
@@ -363,7 +394,8 @@ extern "C" int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const 
                     L.mode == 8 || L.mode == 16,
                 "mtc_strip_fill: leaf %u has mode %d", l, (int)L.mode);
   }
-  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, arena, arena_bytes, batch_bytes, batch_steps};
+  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, arena, arena_bytes, batch_bytes, batch_steps,
+              (flags & kWide) != 0};
   std::vector<StripPlan> plans(n_strips);
   std::atomic<int> bad(0);
   parallel_for(n_strips, [&](int s) {
@@ -392,8 +424,10 @@ extern "C" int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const 
 // and every entry's k row against the matrix.  The kernel trusts what passes.
 extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, const uint32_t* batch_off,
                                const uint32_t* strip_batch, int32_t n_batches, int32_t n_strips, int32_t tk,
-                               uint32_t max_batch_bytes) {
+                               uint32_t max_batch_bytes, uint32_t flags) {
   clear_error();
+  MTC_REQUIRE((flags & ~kWide) == 0, "mtc_strip_check: unknown stream flags 0x%x", flags);
+  const bool wide = (flags & kWide) != 0;
   MTC_REQUIRE(stream && batch_off && strip_batch, "mtc_strip_check: null pointer argument");
   MTC_REQUIRE(n_strips >= 1 && n_batches >= n_strips && tk >= 1, "mtc_strip_check: bad sizes");
   MTC_REQUIRE(strip_batch[0] == 0 && (int64_t)strip_batch[n_strips] == n_batches,
@@ -417,12 +451,14 @@ extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, con
         const int kind = desc_kind(d), n0 = desc_n0(d), n1 = desc_n1(d), sb = desc_bytes(d);
         MTC_REQUIRE(kind < kKinds, "mtc_strip_check: batch %u step %u kind %d", b, i, kind);
         if (kind < kU2)
-          MTC_REQUIRE(n0 >= 1 && n0 <= 8 && n1 == 0, "mtc_strip_check: batch %u step %u group count", b, i);
+          MTC_REQUIRE(n0 >= 1 && n0 <= group_step_max(wide) && n1 == 0, "mtc_strip_check: batch %u step %u group count",
+                      b, i);
         else
           MTC_REQUIRE(n0 <= 16 && n1 <= 16 && n0 + n1 >= 1, "mtc_strip_check: batch %u step %u counts", b, i);
         MTC_REQUIRE(sb == step_bytes(kind, n0, n1) && pos + (uint32_t)sb <= size,
                     "mtc_strip_check: batch %u step %u size", b, i);
-        MTC_REQUIRE(desc_full(d) == full_counts(kind, n0, n1), "mtc_strip_check: batch %u step %u full flag", b, i);
+        MTC_REQUIRE(desc_full(d) == full_counts(kind, n0, n1, wide), "mtc_strip_check: batch %u step %u full flag", b,
+                    i);
         const int run = desc_run(d);
         MTC_REQUIRE(run >= 1 && (run == 1 || desc_full(d)) && i + (uint32_t)run <= nst,
                     "mtc_strip_check: batch %u step %u run length %d", b, i, run);

@@ -11,6 +11,9 @@
 // (lane 4g + g/2, elements g & 1 and 2 + (g & 1)).  Accumulation is in fp64
 // here, so results differ from the GPU's fp32 sums by rounding only.
 //
+// Wide streams (MTC_STRIP_WIDE) are followed the same way: a wide group
+// step's four MMAs are evaluated from the lanes' two A-fragment sets.
+//
 // Never part of the GEMM path: the library in tensorpack_b200/ has no CPU
 // product; this file is built into tests/native/libstrip_model.so.
 #include <math.h>
@@ -63,9 +66,21 @@ void mma_model(const uint32_t a[32][8], int half, const uint32_t b[32][MT][2], i
 
 }  // namespace
 
+template <int C>
+void wide_lanes(const uint8_t* st, int n, bool full, const uint16_t* x16, int kpad, uint32_t a[32][8],
+                uint32_t a2[32][8], uint32_t b[32][MT][2]) {
+  for (int L = 0; L < 32; ++L) {
+    if (full)
+      lane_wide<C, true, MT>(st, n, L, x16, kpad, a[L], a2[L], b[L]);
+    else
+      lane_wide<C, false, MT>(st, n, L, x16, kpad, a[L], a2[L], b[L]);
+  }
+}
+
 extern "C" int strip_model_gemm(const uint8_t* stream, const uint32_t* batch_off, const uint32_t* strip_batch,
                                 int n_strips, int tk, int K, int N, int exp2, const float* X, int M,
-                                const int32_t* pr, const int32_t* pc, float* Y) {
+                                const int32_t* pr, const int32_t* pc, float* Y, uint32_t flags) {
+  const bool wide = (flags & kWide) != 0;
   if (M < 1 || M > MT) return -1;
   const int kpad = tk * 32;
   std::vector<uint16_t> x16((size_t)MT * kpad, 0);
@@ -73,7 +88,7 @@ extern "C" int strip_model_gemm(const uint8_t* stream, const uint32_t* batch_off
     for (int k = 0; k < K; ++k) x16[(size_t)m * kpad + k] = f2h(X[(size_t)m * K + (pr ? pr[k] : k)]);
   const int n_batches = (int)strip_batch[n_strips];
   std::vector<double> part((size_t)n_batches * MT * 8, 0.0);
-  static uint32_t a[32][8], b[32][MT][2];
+  static uint32_t a[32][8], a2[32][8], b[32][MT][2];
   for (int bi = 0; bi < n_batches; ++bi) {
     const uint8_t* base = stream + batch_off[bi];
     const uint32_t nst = ldu32(base + 4);
@@ -93,8 +108,30 @@ extern "C" int strip_model_gemm(const uint8_t* stream, const uint32_t* batch_off
       }
       const int kind = desc_kind(d), n0 = desc_n0(d), n1 = desc_n1(d);
       const bool full = desc_full(d);
-      if (full != full_counts(kind, n0, n1)) return -3;
-      if (kind == kGeneric) {
+      if (full != full_counts(kind, n0, n1, wide)) return -3;
+      if (wide && kind < kU2) {
+        // four MMAs (columns 0-1, 2-3 of quartet 0 from a, 4-5, 6-7 of quartet 1
+        // from a2) sharing one B fragment; every quad's diagonal covers all 8 columns
+        switch (kind) {
+          case kG2: wide_lanes<0>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+          case kG3: wide_lanes<1>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+          case kG4: wide_lanes<2>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+          case kG5: wide_lanes<3>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+          case kG6: wide_lanes<4>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+          default: wide_lanes<5>(st, n0, full, x16.data(), kpad, a, a2, b); break;
+        }
+        for (int m = 0; m < MT; ++m)
+          for (int j = 0; j < 4; ++j) {
+            double D[16][8];
+            mma_model(j < 2 ? a : a2, j & 1, b, m, D);
+            for (int g = 0; g < 8; ++g) {
+              const int t = g >> 1, sel = g & 1;
+              const double c[4] = {D[g][2 * t], D[g][2 * t + 1], D[g + 8][2 * t], D[g + 8][2 * t + 1]};
+              out[m * 8 + 2 * j] += c[sel];
+              out[m * 8 + 2 * j + 1] += c[2 + sel];
+            }
+          }
+      } else if (kind == kGeneric) {
         for (int L = 0; L < 32; ++L) {
           float g[MT][4] = {};
           lane_generic<MT>(st, n0, n1, L, x16.data(), kpad, g);

@@ -39,7 +39,7 @@ def model():
     lib = ctypes.CDLL(path)
     lib.strip_model_gemm.restype = ctypes.c_int
     lib.strip_model_gemm.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5 + [ctypes.c_void_p, ctypes.c_int] + \
-        [ctypes.c_void_p] * 3
+        [ctypes.c_void_p] * 3 + [ctypes.c_uint32]
     lib.strip_model_lane_roundtrip.restype = ctypes.c_int
     lib.strip_model_lane_roundtrip.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     return lib
@@ -70,10 +70,10 @@ def test_lane_codes_roundtrip(model, cls):
     assert bits == 16 * m
 
 
-def _check(model, mat, deq_orig, X, tol_emul=1e-6):
+def _check(model, mat, deq_orig, X, tol_emul=1e-6, wide=False):
     from tensorpack_b200.core import strip
 
-    hs = strip.build_host(mat)
+    hs = strip.build_host(mat, wide=wide)
     # structure of the batch records
     offs = hs.batch_off.astype(np.int64)
     assert (offs % 16 == 0).all() and (np.diff(offs) >= 16).all()
@@ -91,7 +91,7 @@ def _check(model, mat, deq_orig, X, tol_emul=1e-6):
     rc = model.strip_model_gemm(hs.stream.ctypes.data, hs.batch_off.ctypes.data, hs.strip_batch.ctypes.data,
                                 hs.n_strips, hs.tk, K, N, hs.exp2, Xc.ctypes.data, M,
                                 None if pr is None else pr.ctypes.data, None if pc is None else pc.ctypes.data,
-                                Y.ctypes.data)
+                                Y.ctypes.data, hs.flags)
     assert rc == 0
     ref = X.astype(np.float64) @ deq_orig.astype(np.float64)
     assert O.relative_frobenius_error(ref, Y) < 2e-3
@@ -109,8 +109,9 @@ def _qt(golden, name, prefix):
                                    int(g[prefix + "total_bits"]))
 
 
+@pytest.mark.parametrize("wide", [False, True])
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
-def test_forced_modes_all_edges(model, M):
+def test_forced_modes_all_edges(model, M, wide):
     """All eight precisions at all four leaf edges, signed bf16 scales."""
     from tensorpack_b200.kernels.gemm import MTCMatrix
 
@@ -119,12 +120,13 @@ def test_forced_modes_all_edges(model, M):
     deq = O.quadtree_dequant(W, sizes, leaf, modes, scales)
     m = MTCMatrix.from_qt_allocation(W, alloc)
     X = np.random.default_rng(M).standard_normal((M, 256)).astype(np.float32)
-    hs, fast = _check(model, m, deq, X)
+    hs, fast = _check(model, m, deq, X, wide=wide)
     assert (~fast).any() and fast.any()  # both the fast and the fp32 path ran
 
 
+@pytest.mark.parametrize("wide", [False, True])
 @pytest.mark.parametrize("M", [1, 4])
-def test_llm_like_permuted(model, golden_dir, M):
+def test_llm_like_permuted(model, golden_dir, M, wide):
     from tensorpack_b200.kernels.gemm import MTCMatrix
 
     g, inner = _qt(golden_dir, "llm_like_256x512.npz", "b4.25_inner_")
@@ -133,10 +135,11 @@ def test_llm_like_permuted(model, golden_dir, M):
     m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
     stored = O.quadtree_dequant(W[pr][:, pc], inner.sizes, inner.leaf, inner.modes, inner.scales)
     X = inputs.llm_activations(M, 256, seed=M, outlier_seed=1)
-    _check(model, m, O.unpermute(stored, pr, pc), X)
+    _check(model, m, O.unpermute(stored, pr, pc), X, wide=wide)
 
 
-def test_multiscale(model, golden_dir):
+@pytest.mark.parametrize("wide", [False, True])
+def test_multiscale(model, golden_dir, wide):
     from tensorpack_b200.kernels.gemm import MTCMatrix
 
     g, a = _qt(golden_dir, "multiscale_256.npz", "")
@@ -144,10 +147,11 @@ def test_multiscale(model, golden_dir):
     m = MTCMatrix.from_qt_allocation(W, a)
     deq = O.quadtree_dequant(W, a.sizes, a.leaf, a.modes, a.scales)
     X = np.random.default_rng(0).standard_normal((2, 256)).astype(np.float32)
-    _check(model, m, deq, X)
+    _check(model, m, deq, X, wide=wide)
 
 
-def test_ragged_fixed_blocks_fp32_scales(model):
+@pytest.mark.parametrize("wide", [False, True])
+def test_ragged_fixed_blocks_fp32_scales(model, wide):
     """48 x 80 (padded to 64 x 96), 16x16 blocks of every mode, fp32 scales:
     inexact scales and P16 take the fp32 path, padding strips are empty."""
     from tensorpack_b200.kernels.gemm import MTCMatrix
@@ -160,7 +164,7 @@ def test_ragged_fixed_blocks_fp32_scales(model):
     m = MTCMatrix.from_allocation(W, modes, scales, 16)
     deq = O.fixed_dequant(W, modes, np.where(modes == 0, 0, scales).astype(np.float32), 16)
     X = rng.standard_normal((3, 48)).astype(np.float32)
-    _check(model, m, deq, X)
+    _check(model, m, deq, X, wide=wide)
 
 
 def test_all_p0_matrix_gives_zeros(model):
@@ -294,3 +298,34 @@ def test_decode_rejects_bad_arguments_without_a_gpu():
     bad = _lib.StripDesc.from_buffer_copy(d)
     bad.stream = 8  # not 16-byte aligned
     assert call(bad) == _lib.MTC_ERR_INVALID
+
+
+def test_wide_stream_packs_sixteen_groups_per_step(golden_dir):
+    """Wide streams fill group steps with up to 16 groups, are as compact as
+    the narrow form, and pass the validator only with their own flag."""
+    from tensorpack_b200 import _lib
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    g, inner = _qt(golden_dir, "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    narrow, wide = strip.build_host(m), strip.build_host(m, wide=True)
+    assert wide.flags == _lib.STRIP_WIDE and narrow.flags == 0
+    assert abs(int(wide.batch_off[-1]) - int(narrow.batch_off[-1])) < 0.02 * int(narrow.batch_off[-1])
+    n_max = 0
+    for b in range(wide.n_batches):
+        o = int(wide.batch_off[b])
+        nst = int(wide.stream[o + 4:o + 8].view(np.uint32)[0])
+        d = wide.stream[o + 8:o + 8 + 4 * nst].view(np.uint32)
+        grp = (d & 15) < 6
+        if grp.any():
+            n_max = max(n_max, int(((d[grp] >> 5) & 31).max()))
+    assert n_max == 16
+    import copy
+
+    relabeled = copy.deepcopy(wide)
+    relabeled.flags = 0
+    with pytest.raises(ValueError):
+        strip.check(relabeled)
