@@ -506,6 +506,7 @@ extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t
     MTC_REQUIRE(s->cta_part[2 * c + 2] > s->cta_part[2 * c] && s->cta_part[2 * c + 3] > s->cta_part[2 * c + 1] &&
                     s->cta_part[2 * c + 3] - s->cta_part[2 * c + 1] <= s->max_cta_batches,
                 "mtc_strip_decode: CTA range %d is empty or exceeds max_cta_batches", c);
+  MTC_REQUIRE((s->flags & ~MTC_STRIP_WIDE) == 0, "mtc_strip_decode: unknown stream flags 0x%x", s->flags);
   MTC_REQUIRE((reinterpret_cast<uintptr_t>(s->stream) & 15) == 0, "mtc_strip_decode: stream not 16-byte aligned");
   MTC_REQUIRE(s->max_batch_bytes >= 16 && s->max_batch_bytes <= 65536 && (s->max_batch_bytes & 15) == 0,
               "mtc_strip_decode: bad max_batch_bytes %u", s->max_batch_bytes);

@@ -298,6 +298,9 @@ def test_decode_rejects_bad_arguments_without_a_gpu():
     bad = _lib.StripDesc.from_buffer_copy(d)
     bad.stream = 8  # not 16-byte aligned
     assert call(bad) == _lib.MTC_ERR_INVALID
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.flags = 6  # unknown stream flags
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"flags" in lib.mtc_last_error()
 
 
 def test_wide_stream_packs_sixteen_groups_per_step(golden_dir):
