@@ -325,16 +325,11 @@ extern "C" int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
   p.timeout_ns = 2000000000ull;
   cudaStream_t st = as_stream(stream);
-  // Opt in to the largest dynamic shared memory once per kernel instance
-  // (per-launch sizes stay below it).
-  static bool opted[2] = {false, false};
-  const int which = pl.tg - 1;
-  if (!opted[which]) {
-    MTC_CHECK_CUDA(cudaFuncSetAttribute(which ? (const void*)gemv_kernel<2> : (const void*)gemv_kernel<1>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                   "mtc_gemv: smem attribute");
-    opted[which] = true;
-  }
+  // The opt-in to large dynamic shared memory is a per-device attribute:
+  // set it on every call, so every device a process uses gets it.
+  MTC_CHECK_CUDA(cudaFuncSetAttribute(pl.tg == 2 ? (const void*)gemv_kernel<2> : (const void*)gemv_kernel<1>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                 "mtc_gemv: smem attribute");
   if (pl.tg == 1)
     gemv_kernel<1><<<pl.units, kThreads, pl.smem, st>>>(p);
   else

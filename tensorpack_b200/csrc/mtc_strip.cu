@@ -516,7 +516,6 @@ extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t
   const bool wide = (s->flags & MTC_STRIP_WIDE) != 0;
   const int per = wide ? 2 : strip::kMaxM;  // tokens per launch
   cudaStream_t st = as_stream(stream);
-  static bool opted[6] = {false, false, false, false, false, false};
   for (int m0 = 0; m0 < M; m0 += per) {
     const int Mi = M - m0 < per ? M - m0 : per;
     Plan pl;
@@ -557,11 +556,9 @@ extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t
     const void* fns[6] = {(const void*)strip_kernel<1, false>, (const void*)strip_kernel<2, false>,
                           (const void*)strip_kernel<4, false>, (const void*)strip_kernel<1, true>,
                           (const void*)strip_kernel<2, true>,  (const void*)strip_kernel<2, true>};
-    if (!opted[which]) {
-      MTC_CHECK_CUDA(cudaFuncSetAttribute(fns[which], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                     "mtc_strip_decode: smem attribute");
-      opted[which] = true;
-    }
+    // per-device attribute: set on every call (a process may use several GPUs)
+    MTC_CHECK_CUDA(cudaFuncSetAttribute(fns[which], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                   "mtc_strip_decode: smem attribute");
     const dim3 grid(s->n_cta), block(pl.nw * 32);
     switch (which) {
       case 0: strip_kernel<1, false><<<grid, block, pl.smem, st>>>(p); break;
