@@ -196,9 +196,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--decode-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decode-kernel", default="strip", choices=["tensor", "strip"],
-                    help="decode M = 1 through the mma.sync kernel over the strip stream (strip, default) or the "
-                         "tcgen05 kernel over the sub-stage images (tensor)")
+    ap.add_argument("--decode-kernel", default="strip", choices=["tensor", "strip", "strip-wide"],
+                    help="decode M = 1 through the mma.sync kernel over the strip stream (strip, default), over "
+                         "its wide form (strip-wide: 16-group steps, four MMAs per B fragment) or the tcgen05 "
+                         "kernel over the sub-stage images (tensor)")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
                     help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
@@ -324,8 +325,8 @@ def main():
     descs, keep = [], []
     pr_ptr = None if ds.row_perm is None else ds.row_perm.data_ptr()
     pc_ptr = None if ds.col_perm is None else ds.col_perm.data_ptr()
-    if args.decode_kernel == "strip":
-        sp = ds.strip()
+    if args.decode_kernel.startswith("strip"):
+        sp = ds.strip(wide=args.decode_kernel == "strip-wide")
         stream_bytes = sp.stream.numel()
         copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
         for _ in range(copies):
@@ -436,13 +437,15 @@ def main():
                          "kernel": "prefill_kernel (fused dequant + tcgen05)", "peak_source": peak_src,
                          "kernel_ms": kern_ms},
             "decode": {"value": dec_gbs, "unit": "GB/s", "us_per_call": dec_us, "M": 1,
-                       "kernel": "strip_kernel (mma.sync over the strip stream)" if args.decode_kernel == "strip"
-                       else "decode_kernel (tcgen05 over the sub-stage images)",
+                       "kernel": {"strip": "strip_kernel (mma.sync over the strip stream)",
+                                  "strip-wide": "strip_kernel (mma.sync over the wide strip stream)",
+                                  "tensor": "decode_kernel (tcgen05 over the sub-stage images)"}[args.decode_kernel],
                        "accounted_bytes": accounted_bytes, "device_bytes": stream_bytes,
                        "roofline": {"bound": "hbm", "achieved": dec_local_gbs, "peak": hbm_peak, "unit": "GB/s",
                                     "frac": dec_local_gbs / hbm_peak,
                                     "traffic": committed_traffic("strip_kernel" if args.decode_kernel == "strip"
-                                                                 else "decode_kernel"),
+                                                                 else "decode_kernel" if args.decode_kernel == "tensor"
+                                                                 else None),
                                     "peak_source": peak_src},
                        "copies_rotated": copies},
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",

@@ -314,12 +314,17 @@ class DeviceStream:
                                   _stream(self.device)), "decode")
         return Y
 
-    def strip(self) -> "DeviceStrip":
+    def strip(self, wide: bool = False) -> "DeviceStrip":
         """The strip stream of this matrix on this device (the decode layout
-        for M <= 4), built on the host and uploaded at first use."""
-        if self._strip is None:
-            from ..core import strip as _strip
+        for M <= 4), built on the host and uploaded at first use.  ``wide``
+        gives the MTC_STRIP_WIDE form (opt-in; the decode uses the default)."""
+        from ..core import strip as _strip
 
+        if wide:
+            if getattr(self, "_strip_wide", None) is None:
+                self._strip_wide = DeviceStrip(_strip.build_host(self._mat, wide=True), self.device)
+            return self._strip_wide
+        if self._strip is None:
             self._strip = DeviceStrip(_strip.build_host(self._mat), self.device)
         return self._strip
 
