@@ -200,6 +200,9 @@ def main():
                     help="decode M = 1 through the mma.sync kernel over the strip stream (strip, default), over "
                          "its wide form (strip-wide: 16-group steps, four MMAs per B fragment) or the tcgen05 "
                          "kernel over the sub-stage images (tensor)")
+    ap.add_argument("--strip-batch-bytes", type=int, default=None,
+                    help="batch record limit of the strip stream (default 4096; 2048..65536)")
+    ap.add_argument("--strip-batch-steps", type=int, default=None, help="steps per strip batch record (default 64)")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
                     help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
@@ -326,7 +329,8 @@ def main():
     pr_ptr = None if ds.row_perm is None else ds.row_perm.data_ptr()
     pc_ptr = None if ds.col_perm is None else ds.col_perm.data_ptr()
     if args.decode_kernel.startswith("strip"):
-        sp = ds.strip(wide=args.decode_kernel == "strip-wide")
+        sp = ds.strip(wide=args.decode_kernel == "strip-wide", batch_bytes=args.strip_batch_bytes,
+                      batch_steps=args.strip_batch_steps)
         stream_bytes = sp.stream.numel()
         copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
         for _ in range(copies):
