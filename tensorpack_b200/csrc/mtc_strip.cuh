@@ -36,6 +36,9 @@
 //            [plane A][plane B][pad16]      (lanes of quartet 0, then quartet 1)
 //   generic: [n0 + n1 x (fp32 scale * 2^exp2, micro row | mode << 16), pad16]
 //            [n0 + n1 x 32 B: the 16 codes as LSB-first m-bit two's complement]
+//   group in a wide stream (MTC_STRIP_WIDE): up to 16 groups; lane L takes
+//            group L >> 1, k half L & 1 and both quartets, whose two
+//            micro-blocks sit side by side in each plane (2n lanes).
 // Batch record (one bulk copy, never crossing a strip):
 //   [u32 strip][u32 n_steps][n_steps u32 step descriptors][pad16][steps]
 // Step descriptor: bits 0-3 kind, 4 full step, 5-9 n0 (groups for a group
