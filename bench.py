@@ -203,6 +203,8 @@ def main():
     ap.add_argument("--strip-batch-bytes", type=int, default=None,
                     help="batch record limit of the strip stream (default 4096; 2048..65536)")
     ap.add_argument("--strip-batch-steps", type=int, default=None, help="steps per strip batch record (default 64)")
+    ap.add_argument("--strip-merge-modes", action="store_true",
+                    help="strip stream with P2 items packed as P3 and P6 items as P8 (fewer step kinds)")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "decode"],
                     help="run one part only (small profiler captures); the JSON line then carries that part")
     args = ap.parse_args()
@@ -330,7 +332,7 @@ def main():
     pc_ptr = None if ds.col_perm is None else ds.col_perm.data_ptr()
     if args.decode_kernel.startswith("strip"):
         sp = ds.strip(wide=args.decode_kernel == "strip-wide", batch_bytes=args.strip_batch_bytes,
-                      batch_steps=args.strip_batch_steps)
+                      batch_steps=args.strip_batch_steps, merge_modes=args.strip_merge_modes)
         stream_bytes = sp.stream.numel()
         copies = max(2, int(4 * L2_BYTES // max(stream_bytes, 1)) + 1)
         for _ in range(copies):

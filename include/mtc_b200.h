@@ -264,6 +264,8 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
 #define MTC_STRIP_MAX_CTA 480     /* most CTA ranges of one strip-kernel launch */
 #define MTC_STRIP_WIDE 1u         /* stream flag: group steps of 16 groups, each lane both column quartets
                                      of one group's k half (four MMAs per B fragment) */
+#define MTC_STRIP_MERGE_MODES 2u  /* build flag (mtc_strip_plan / _fill only): P2 items packed with the P3
+                                     decoder and P6 items with the P8 one, exactly, for fewer step kinds */
 
 typedef struct mtc_strip_desc {
   const uint8_t* stream;        /* batch records, 16-byte aligned */
@@ -290,7 +292,9 @@ typedef struct mtc_strip_desc {
  * 2^exp2 (choose it so the largest |scale| * 2^exp2 is at most 1); leaves of
  * P16 or whose pre-scaled scale is not exact in fp16 take the fp32 path.
  * Batch records hold at most `batch_bytes` bytes (2048..65536, multiple of
- * 16) and `batch_steps` steps.  `flags`: 0 or MTC_STRIP_WIDE.
+ * 16) and `batch_steps` steps.  `flags`: MTC_STRIP_WIDE and / or
+ * MTC_STRIP_MERGE_MODES (the latter is not a stream flag: the descriptor and
+ * the validator take only MTC_STRIP_WIDE).
  * plan: out4 = {stream bytes, n_batches, n_strips, largest batch record}.
  * fill: writes `stream` (stream bytes), `batch_off` (n_batches + 1) and
  *       `strip_batch` (n_strips + 1). */

@@ -61,6 +61,7 @@ class StripDesc(ctypes.Structure):
 
 assert ctypes.sizeof(StripDesc) == 88
 STRIP_WIDE = 1
+STRIP_MERGE_MODES = 2
 STRIP_MAX_CTA = 480
 
 

@@ -87,11 +87,13 @@ class HostStripStream:
 
 
 def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS,
-               wide: bool = False) -> HostStripStream:
+               wide: bool = False, merge_modes: bool = False) -> HostStripStream:
     """Build the strip stream of an MTCMatrix on the host (no GPU needed).
     ``wide`` packs group steps of 16 groups with two micro-blocks per lane
-    (MTC_STRIP_WIDE; checked on the CPU model of the kernel only so far)."""
-    flags = _lib.STRIP_WIDE if wide else 0
+    (MTC_STRIP_WIDE); ``merge_modes`` packs P2 items with the P3 decoder and
+    P6 items with the P8 one (exact, fewer step kinds).  Both are checked on
+    the CPU model of the kernel only so far and are off by default."""
+    flags = (_lib.STRIP_WIDE if wide else 0) | (_lib.STRIP_MERGE_MODES if merge_modes else 0)
     lib = _lib.load()
     K, N = (int(v) for v in mat.shape)
     ls = mat.leaf_set
@@ -111,7 +113,7 @@ def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STE
     _lib.check(lib.mtc_strip_fill(arena.ctypes.data, arena.nbytes, leaves.ctypes.data, begin.ctypes.data, tk, tn,
                                   exp2, batch_bytes, batch_steps, flags, stream.ctypes.data, batch_off.ctypes.data,
                                   strip_batch.ctypes.data), "strip fill")
-    hs = HostStripStream(K, N, tk, tn, exp2, stream, batch_off, strip_batch, max_batch, flags)
+    hs = HostStripStream(K, N, tk, tn, exp2, stream, batch_off, strip_batch, max_batch, flags & _lib.STRIP_WIDE)
     check(hs)
     return hs
 

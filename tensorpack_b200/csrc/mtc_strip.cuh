@@ -89,7 +89,8 @@ __host__ __device__ constexpr int bias_of_class(int c) { return 1 << (mode_of_cl
 // takes both column quartets of group L >> 1, k half L & 1 (32 weights, four
 // MMAs sharing one B fragment).  Micro and generic steps are the same in both
 // forms.
-constexpr uint32_t kWide = 1u;  // stream flag (MTC_STRIP_WIDE)
+constexpr uint32_t kWide = 1u;        // stream flag (MTC_STRIP_WIDE)
+constexpr uint32_t kMergeModes = 2u;  // build flag (MTC_STRIP_MERGE_MODES): P2 packed as P3, P6 as P8
 __host__ __device__ constexpr int group_step_max(bool wide) { return wide ? 16 : 8; }
 __host__ __device__ constexpr bool full_counts(int kind, int n0, int n1, bool wide = false) {
   return kind < kU2 ? n0 == group_step_max(wide) : (n0 == 16 && n1 == 16);

@@ -36,8 +36,17 @@ struct Ctx {
   const uint8_t* arena;
   uint64_t arena_bytes;
   uint32_t batch_bytes, batch_steps;
-  bool wide;  // group steps of 16 groups, two micro-blocks per lane
+  bool wide;   // group steps of 16 groups, two micro-blocks per lane
+  bool merge;  // P2 items packed as P3 and P6 items as P8 (fewer step kinds)
 };
+
+// Decoder class of a leaf mode, after the optional merge of P2 into P3 and
+// P6 into P8 (their codes lie inside the wider ranges, so they are exact).
+__host__ inline int packed_class(const Ctx& c, int mode) {
+  const int cls = class_of_mode(mode);
+  if (!c.merge) return cls;
+  return cls == 0 ? 1 : cls == 4 ? 5 : cls;
+}
 
 // One item of a strip: a group (8 k x 8 features) or a micro-block (4 x 4).
 struct Item {
@@ -95,7 +104,7 @@ __host__ bool plan_strip(const Ctx& c, int strip, StripPlan* P) {
         if (L.mode == 0) continue;
         float sc;
         memcpy(&sc, &L.scale_bits, 4);
-        const int cls = class_of_mode(L.mode);
+        const int cls = packed_class(c, L.mode);
         if (cls >= 0 && exact_f16(sc, c.exp2) >= 0) {
           P->grp[cls].push_back(Item{(uint32_t)mb[0][0], grow, kt});
         } else {
@@ -110,7 +119,7 @@ __host__ bool plan_strip(const Ctx& c, int strip, StripPlan* P) {
           if (L.mode == 0) continue;
           float sc;
           memcpy(&sc, &L.scale_bits, 4);
-          const int cls = class_of_mode(L.mode);
+          const int cls = packed_class(c, L.mode);
           const Item it{(uint32_t)mb[a][h], 2 * grow + a, kt};
           if (cls >= 0 && exact_f16(sc, c.exp2) >= 0)
             P->mic[cls][h].push_back(it);
@@ -328,7 +337,7 @@ void parallel_for(int n, F f) {
 
 int check_args(const mtc_leaf_in* leaves, const uint32_t* begin, int32_t tk, int32_t tn, uint32_t batch_bytes,
                uint32_t batch_steps, uint32_t flags, const char* who) {
-  MTC_REQUIRE((flags & ~kWide) == 0, "%s: unknown stream flags 0x%x", who, flags);
+  MTC_REQUIRE((flags & ~(kWide | kMergeModes)) == 0, "%s: unknown stream flags 0x%x", who, flags);
   MTC_REQUIRE(leaves && begin, "%s: null pointer argument", who);
   MTC_REQUIRE(tk >= 1 && tn >= 1, "%s: bad tile grid %d x %d", who, tk, tn);
   MTC_REQUIRE(tk * 8 <= 65535, "%s: K of %d tiles exceeds the 16-bit micro-block row", who, tk);
@@ -350,7 +359,8 @@ extern "C" int mtc_strip_plan(const mtc_leaf_in* leaves, const uint32_t* tile_le
   int rc = check_args(leaves, tile_leaf_begin, tk, tn, batch_bytes, batch_steps, flags, "mtc_strip_plan");
   if (rc) return rc;
   MTC_REQUIRE(out4, "mtc_strip_plan: null out4");
-  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, nullptr, 0, batch_bytes, batch_steps, (flags & kWide) != 0};
+  const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, nullptr, 0, batch_bytes, batch_steps, (flags & kWide) != 0,
+              (flags & kMergeModes) != 0};
   const int n_strips = tn * 4;
   std::vector<uint64_t> bytes(n_strips), nb(n_strips), mx(n_strips);
   std::atomic<int> bad(0);
@@ -395,7 +405,7 @@ extern "C" int mtc_strip_fill(const uint8_t* arena, uint64_t arena_bytes, const 
                 "mtc_strip_fill: leaf %u has mode %d", l, (int)L.mode);
   }
   const Ctx c{leaves, tile_leaf_begin, tk, tn, exp2, arena, arena_bytes, batch_bytes, batch_steps,
-              (flags & kWide) != 0};
+              (flags & kWide) != 0, (flags & kMergeModes) != 0};
   std::vector<StripPlan> plans(n_strips);
   std::atomic<int> bad(0);
   parallel_for(n_strips, [&](int s) {

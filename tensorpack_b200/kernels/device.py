@@ -315,19 +315,21 @@ class DeviceStream:
         return Y
 
     def strip(self, wide: bool = False, batch_bytes: Optional[int] = None,
-              batch_steps: Optional[int] = None) -> "DeviceStrip":
+              batch_steps: Optional[int] = None, merge_modes: bool = False) -> "DeviceStrip":
         """The strip stream of this matrix on this device (the decode layout
         for M <= 4), built on the host and uploaded at first use.  ``wide``
-        gives the MTC_STRIP_WIDE form; ``batch_bytes`` / ``batch_steps``
+        gives the MTC_STRIP_WIDE form, ``merge_modes`` packs P2 / P6 items
+        with the P3 / P8 decoders; ``batch_bytes`` / ``batch_steps``
         override the batch record limits.  The decode uses the default
         stream; the other forms are built on request (for measurements)."""
         from ..core import strip as _strip
 
-        if wide or batch_bytes is not None or batch_steps is not None:
-            key = (wide, batch_bytes or _strip.BATCH_BYTES, batch_steps or _strip.BATCH_STEPS)
+        if wide or merge_modes or batch_bytes is not None or batch_steps is not None:
+            key = (wide, merge_modes, batch_bytes or _strip.BATCH_BYTES, batch_steps or _strip.BATCH_STEPS)
             other = self.__dict__.setdefault("_strip_other", {})
             if key not in other:
-                other[key] = DeviceStrip(_strip.build_host(self._mat, key[1], key[2], wide=wide), self.device)
+                other[key] = DeviceStrip(_strip.build_host(self._mat, key[2], key[3], wide=wide,
+                                                           merge_modes=merge_modes), self.device)
             return other[key]
         if self._strip is None:
             self._strip = DeviceStrip(_strip.build_host(self._mat), self.device)

@@ -70,10 +70,10 @@ def test_lane_codes_roundtrip(model, cls):
     assert bits == 16 * m
 
 
-def _check(model, mat, deq_orig, X, tol_emul=1e-6, wide=False):
+def _check(model, mat, deq_orig, X, tol_emul=1e-6, wide=False, merge=False):
     from tensorpack_b200.core import strip
 
-    hs = strip.build_host(mat, wide=wide)
+    hs = strip.build_host(mat, wide=wide, merge_modes=merge)
     # structure of the batch records
     offs = hs.batch_off.astype(np.int64)
     assert (offs % 16 == 0).all() and (np.diff(offs) >= 16).all()
@@ -332,3 +332,24 @@ def test_wide_stream_packs_sixteen_groups_per_step(golden_dir):
     relabeled.flags = 0
     with pytest.raises(ValueError):
         strip.check(relabeled)
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_merged_modes_are_exact_and_drop_p2_p6_kinds(model, wide):
+    """P2 items packed with the P3 decoder and P6 items with the P8 one give
+    the same product, and the stream then has no P2 / P6 steps."""
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    W, sizes, leaf, modes, scales = inputs.forced_mode_allocation(256, 384, seed=0, p_split=0.5)
+    alloc = O.QuadtreeAllocation(sizes, leaf, modes, scales, None, 0)
+    deq = O.quadtree_dequant(W, sizes, leaf, modes, scales)
+    m = MTCMatrix.from_qt_allocation(W, alloc)
+    X = np.random.default_rng(5).standard_normal((2, 256)).astype(np.float32)
+    hs, _ = _check(model, m, deq, X, wide=wide, merge=True)
+    kinds = set()
+    for b in range(hs.n_batches):
+        o = int(hs.batch_off[b])
+        nst = int(hs.stream[o + 4:o + 8].view(np.uint32)[0])
+        kinds |= set((hs.stream[o + 8:o + 8 + 4 * nst].view(np.uint32) & 15).tolist())
+    assert not kinds & {0, 4, 6, 10} and kinds & {1, 5, 7, 11}  # no G2, G6, U2, U6; merged kinds present
