@@ -353,3 +353,22 @@ def test_merged_modes_are_exact_and_drop_p2_p6_kinds(model, wide):
         nst = int(hs.stream[o + 4:o + 8].view(np.uint32)[0])
         kinds |= set((hs.stream[o + 8:o + 8 + 4 * nst].view(np.uint32) & 15).tolist())
     assert not kinds & {0, 4, 6, 10} and kinds & {1, 5, 7, 11}  # no G2, G6, U2, U6; merged kinds present
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_shape_not_multiple_of_eight(model, wide):
+    """44 x 84 in 4x4 blocks of every mode: the last strip straddles N (its
+    columns beyond 84 are padding) and K is padded to 64."""
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    rng = np.random.default_rng(11)
+    W = rng.standard_normal((44, 84)).astype(np.float32)
+    modes = rng.choice([0, 2, 3, 4, 5, 6, 8, 16], size=(11, 21)).astype(np.uint8)
+    qmax = np.array([1.0 if x in (0, 2) else 2.0 ** (int(x) - 1) - 1 for x in modes.ravel()]).reshape(11, 21)
+    amax = np.abs(W.reshape(11, 4, 21, 4)).max(axis=(1, 3))
+    scales = (amax / qmax).astype(np.float32)
+    scales = (scales.view(np.uint32) & 0xFFFF0000).view(np.float32)  # bf16 scales: the fast path
+    m = MTCMatrix.from_allocation(W, modes, scales, 4)
+    deq = O.fixed_dequant(W, modes, np.where(modes == 0, 0, scales).astype(np.float32), 4)
+    X = rng.standard_normal((2, 44)).astype(np.float32)
+    _check(model, m, deq, X, wide=wide)
