@@ -16,7 +16,11 @@ the allocator:
   and the sub-stage images of the tensor-core kernels), so that loading onto
   a GPU uploads bytes instead of repacking.  The stream is tagged with the
   device format version; a file whose stream version differs from the
-  library's is still loadable, and its stream is rebuilt from the host layout.
+  library's is still loadable, and its stream is rebuilt from the host layout;
+* optionally the strip stream of the decode kernel (batch records and their
+  tables, built on the host, so saving it needs no GPU), tagged and handled
+  the same way: a stream of the library's strip version is validated record
+  by record and used instead of being built again.
 
 File layout (little endian):
 
@@ -89,7 +93,7 @@ def _host_arrays(mat) -> Dict[str, np.ndarray]:
     return arrs
 
 
-def _entry_meta(mat, stream_meta: Optional[dict]) -> dict:
+def _entry_meta(mat, stream_meta: Optional[dict], strip_meta: Optional[dict] = None) -> dict:
     meta = {
         "kind": "quadtree" if mat.is_quadtree else "fixed",
         "shape": [int(x) for x in mat.shape],
@@ -101,14 +105,19 @@ def _entry_meta(mat, stream_meta: Optional[dict]) -> dict:
     }
     if stream_meta is not None:
         meta["stream"] = stream_meta
+    if strip_meta is not None:
+        meta["strip"] = strip_meta
     return meta
 
 
-def save_mtc(path: PathLike, matrices, *, include_stream: bool = False, device=None) -> None:
+def save_mtc(path: PathLike, matrices, *, include_stream: bool = False, device=None,
+             include_strip: bool = False) -> None:
     """Write one MTCMatrix, or a mapping name -> MTCMatrix, to ``path``.
 
     ``include_stream`` also stores each matrix's device tile stream (built on
-    ``device``, default the current CUDA device, if it does not exist yet)."""
+    ``device``, default the current CUDA device, if it does not exist yet);
+    ``include_strip`` stores the strip stream of the decode kernel (built on
+    the host)."""
     single = not isinstance(matrices, Mapping)
     items = {_SINGLE: matrices} if single else dict(matrices)
     if not items:
@@ -119,11 +128,16 @@ def save_mtc(path: PathLike, matrices, *, include_stream: bool = False, device=N
         if "/" in name or not name:
             raise ValueError(f"bad matrix name {name!r}")
         arrs = _host_arrays(mat)
-        stream_meta = None
+        stream_meta = strip_meta = None
         if include_stream:
             ds = mat.device_stream(device)
             stream_meta, sarrs = ds.export_buffers()
             arrs.update({"stream." + k: v for k, v in sarrs.items()})
+        if include_strip:
+            from . import strip as _strip
+
+            strip_meta, parrs = _strip.export_host(mat.host_strip())
+            arrs.update({"strip." + k: v for k, v in parrs.items()})
         recs = {}
         for key, a in arrs.items():
             a = np.ascontiguousarray(a)
@@ -131,7 +145,7 @@ def save_mtc(path: PathLike, matrices, *, include_stream: bool = False, device=N
                    "crc32": zlib.crc32(a.view(np.uint8).reshape(-1)) & 0xFFFFFFFF}
             recs[key] = rec
             payload.append((a, rec))
-        meta = _entry_meta(mat, stream_meta)
+        meta = _entry_meta(mat, stream_meta, strip_meta)
         meta["arrays"] = recs
         header["entries"][name] = meta
     # offsets depend on the header length, which depends on the offsets:
@@ -304,8 +318,16 @@ def load_mtc(path: PathLike, *, device=None, use_stream: bool = True, mmap: bool
     out = {}
     for name, meta in header["entries"].items():
         a = _read_arrays(path, meta["arrays"], mmap, size)
-        host = {k: v for k, v in a.items() if not k.startswith("stream.")}
+        host = {k: v for k, v in a.items() if not k.startswith(("stream.", "strip."))}
         mat = _build_matrix(name, meta, host)
+        pm = meta.get("strip")
+        if use_stream and pm is not None:
+            from . import strip as _strip
+
+            parrs = {k[len("strip."):]: v for k, v in a.items() if k.startswith("strip.")}
+            hs = _strip.import_host(mat, pm, parrs)
+            if hs is not None:
+                mat.attach_host_strip(hs)
         if device is not None:
             from ..kernels.device import DeviceStream, stream_compatible
 

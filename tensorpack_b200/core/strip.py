@@ -21,6 +21,9 @@ import numpy as np
 from .. import _lib
 from . import layout
 
+# Version of the strip stream layout (step records, descriptors, batch
+# records).  A stream saved by another version is rebuilt on load.
+STRIP_FORMAT_VERSION = 1
 BATCH_BYTES = 4096   # largest batch record (one shared-memory slot of the kernel)
 BATCH_STEPS = 64     # most steps per batch record
 MAX_M = 4            # tokens per strip-kernel call
@@ -124,3 +127,39 @@ def check(hs: HostStripStream) -> None:
     _lib.check(lib.mtc_strip_check(hs.stream.ctypes.data, hs.stream.nbytes, hs.batch_off.ctypes.data,
                                    hs.strip_batch.ctypes.data, hs.n_batches, hs.n_strips, hs.tk,
                                    hs.max_batch_bytes, hs.flags), "strip stream")
+
+
+def export_host(hs: HostStripStream) -> tuple:
+    """(metadata, name -> array) of a host strip stream, for the on-disk
+    format (tensorpack_b200.core.fileformat)."""
+    meta = {"version": STRIP_FORMAT_VERSION, "K": hs.K, "N": hs.N, "tk": hs.tk, "tn": hs.tn, "exp2": hs.exp2,
+            "flags": int(hs.flags), "max_batch_bytes": int(hs.max_batch_bytes)}
+    return meta, {"stream": hs.stream, "batch_off": hs.batch_off, "strip_batch": hs.strip_batch}
+
+
+def import_host(mat, meta: dict, arrs: dict) -> "HostStripStream | None":
+    """A saved strip stream for ``mat``, validated record by record, or None
+    when it was written by another layout version or for another matrix
+    (the caller then builds it again).  Raises ValueError on a stream that
+    claims this version but fails validation."""
+    K, N = (int(v) for v in mat.shape)
+    try:
+        ok = (int(meta["version"]) == STRIP_FORMAT_VERSION and int(meta["K"]) == K and int(meta["N"]) == N
+              and int(meta["tk"]) == -(-K // layout.TILE) and int(meta["tn"]) == -(-N // layout.TILE)
+              and int(meta["exp2"]) == strip_exp2(mat.leaf_set))
+    except (KeyError, TypeError, ValueError):
+        return None
+    if not ok:
+        return None
+    try:
+        stream = np.ascontiguousarray(arrs["stream"], dtype=np.uint8)
+        batch_off = np.ascontiguousarray(arrs["batch_off"], dtype=np.uint32)
+        strip_batch = np.ascontiguousarray(arrs["strip_batch"], dtype=np.uint32)
+        hs = HostStripStream(K, N, int(meta["tk"]), int(meta["tn"]), int(meta["exp2"]), stream, batch_off,
+                             strip_batch, int(meta["max_batch_bytes"]), int(meta["flags"]))
+    except (KeyError, TypeError, ValueError) as e:
+        raise ValueError(f"saved strip stream: {e}") from None
+    if hs.n_strips != 4 * hs.tn or hs.n_batches < hs.n_strips:
+        raise ValueError("saved strip stream: table sizes do not match the matrix")
+    check(hs)
+    return hs

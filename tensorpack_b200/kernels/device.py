@@ -332,7 +332,7 @@ class DeviceStream:
                                                            merge_modes=merge_modes), self.device)
             return other[key]
         if self._strip is None:
-            self._strip = DeviceStrip(_strip.build_host(self._mat), self.device)
+            self._strip = DeviceStrip(self._mat.host_strip(), self.device)
         return self._strip
 
     def decode_strip(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:

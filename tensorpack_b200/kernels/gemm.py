@@ -252,14 +252,36 @@ class MTCMatrix:
         """Use an already built device stream (e.g. uploaded from a file)."""
         self._device[str(ds.device)] = ds
 
+    def host_strip(self):
+        """The default strip stream of this matrix (the decode layout for
+        M <= 4) in host memory: built on first use, or the one loaded from a
+        file (tensorpack_b200.core.strip)."""
+        hs = getattr(self, "_host_strip", None)
+        if hs is None:
+            from ..core import strip as _strip
+
+            hs = _strip.build_host(self)
+            self._host_strip = hs
+        return hs
+
+    def attach_host_strip(self, hs) -> None:
+        """Use an already built default strip stream (e.g. read from a file)."""
+        from ..core import strip as _strip
+
+        if hs.flags != 0 or hs.max_batch_bytes > _strip.BATCH_BYTES:
+            raise ValueError("attach_host_strip: only the default strip form can be attached")
+        self._host_strip = hs
+
     # ------------------------------------------------------------------ files
-    def save(self, path, *, include_stream: bool = False, device=None) -> None:
+    def save(self, path, *, include_stream: bool = False, device=None, include_strip: bool = False) -> None:
         """Write this matrix to a versioned ``.mtcpk`` file
         (tensorpack_b200.core.fileformat); ``include_stream`` also stores the
-        device tile stream so that loading skips the repack."""
+        device tile stream so that loading skips the repack, and
+        ``include_strip`` the decode kernel's strip stream (built on the
+        host, no GPU needed)."""
         from ..core.fileformat import save_mtc
 
-        save_mtc(path, self, include_stream=include_stream, device=device)
+        save_mtc(path, self, include_stream=include_stream, device=device, include_strip=include_strip)
 
     @classmethod
     def load(cls, path, *, device=None, use_stream: bool = True, mmap: bool = False) -> "MTCMatrix":

@@ -253,3 +253,73 @@ def test_header_is_plain_json(golden_dir, tmp_path):
     assert e["kind"] == "fixed" and e["shape"] == list(m.shape) and e["accounted_bits"] == m.accounted_bits
     for rec in e["arrays"].values():
         assert rec["offset"] % 64 == 0 and rec["offset"] >= data_off
+
+
+def test_strip_stream_saved_and_reused(golden_dir, tmp_path):
+    """include_strip stores the decode layout (built on the host, no GPU);
+    loading validates it and attaches it, so the decode does not rebuild it."""
+    from tensorpack_b200.core import strip
+
+    m = qtp_matrix(golden_dir)[0]
+    p = tmp_path / "strip.mtcpk"
+    m.save(p, include_strip=True)
+    meta = F.read_header(p)["entries"]["matrix"]
+    assert meta["strip"]["version"] == strip.STRIP_FORMAT_VERSION
+    r = MTCMatrix.load(p)
+    same_host_layout(m, r)
+    hs, fresh = r.__dict__.get("_host_strip"), strip.build_host(r)
+    assert hs is not None, "the saved strip stream was not attached"
+    for k in ("stream", "batch_off", "strip_batch"):
+        assert np.array_equal(getattr(hs, k), getattr(fresh, k)), k
+    assert (hs.exp2, hs.max_batch_bytes, hs.flags) == (fresh.exp2, fresh.max_batch_bytes, fresh.flags)
+    # a file without the strip stream loads as before and builds it on demand
+    q = tmp_path / "plain.mtcpk"
+    m.save(q)
+    r2 = MTCMatrix.load(q)
+    assert r2.__dict__.get("_host_strip") is None
+    assert np.array_equal(r2.host_strip().stream, fresh.stream)
+
+
+def _save_with_strip(path, m, edit_meta=None, edit_arrays=None):
+    """save_mtc with the exported strip stream altered before it is written
+    (the file's checksums then match the altered bytes)."""
+    from tensorpack_b200.core import strip
+
+    orig = strip.export_host
+
+    def export(hs):
+        meta, arrs = orig(hs)
+        arrs = {k: v.copy() for k, v in arrs.items()}
+        if edit_meta:
+            edit_meta(meta)
+        if edit_arrays:
+            edit_arrays(arrs)
+        return meta, arrs
+
+    strip.export_host = export
+    try:
+        m.save(path, include_strip=True)
+    finally:
+        strip.export_host = orig
+
+
+def test_strip_stream_of_another_version_is_rebuilt(golden_dir, tmp_path):
+    m = qtp_matrix(golden_dir)[0]
+    p = tmp_path / "strip.mtcpk"
+    _save_with_strip(p, m, edit_meta=lambda meta: meta.update(version=meta["version"] + 1))
+    r = MTCMatrix.load(p)
+    assert r.__dict__.get("_host_strip") is None  # ignored, built again on first use
+
+
+def test_damaged_strip_stream_rejected(golden_dir, tmp_path):
+    """A strip record that matches its checksum but fails the validator (a
+    consistent-looking but wrong file) raises instead of being used."""
+    m = qtp_matrix(golden_dir)[0]
+    p = tmp_path / "strip.mtcpk"
+
+    def damage(arrs):
+        arrs["stream"][0] ^= 0x01  # the strip index of the first batch record
+
+    _save_with_strip(p, m, edit_arrays=damage)
+    with pytest.raises(ValueError, match="strip"):
+        MTCMatrix.load(p)
