@@ -372,3 +372,25 @@ def test_shape_not_multiple_of_eight(model, wide):
     deq = O.fixed_dequant(W, modes, np.where(modes == 0, 0, scales).astype(np.float32), 4)
     X = rng.standard_normal((2, 44)).astype(np.float32)
     _check(model, m, deq, X, wide=wide)
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_runs_of_full_steps(model, wide):
+    """A 1024-row LLM-like layer (oracle allocation, MTC-QT-P at 4.25 b/w)
+    gives runs of identical full steps in both forms; the kernel's counted
+    run loop is checked through the model."""
+    from tensorpack_b200.core import strip
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    W, h = inputs.llm_like(1024, 128, seed=3)
+    a = O.PermutedQuadtree(W, h, sizes=(32, 16, 8, 4)).select(4.25)
+    m = MTCMatrix.from_qt_allocation(W, a)
+    hs = strip.build_host(m, wide=wide)
+    runs = 0
+    for b in range(hs.n_batches):
+        o = int(hs.batch_off[b])
+        nst = int(hs.stream[o + 4:o + 8].view(np.uint32)[0])
+        runs += int(((hs.stream[o + 8:o + 8 + 4 * nst].view(np.uint32) >> 22) > 1).sum())
+    assert runs > 0
+    X = inputs.llm_activations(2, 1024, seed=4, outlier_seed=0)
+    _check(model, m, a.dequant, X, wide=wide)
