@@ -394,3 +394,21 @@ def test_runs_of_full_steps(model, wide):
     assert runs > 0
     X = inputs.llm_activations(2, 1024, seed=4, outlier_seed=0)
     _check(model, m, a.dequant, X, wide=wide)
+
+
+def test_strip_exp2_edge_cases():
+    """The pre-scale puts the largest |scale| of a live leaf in (1/2, 1];
+    matrices with no live scale use 0; extreme scales are clamped."""
+    from tensorpack_b200.core import layout, strip
+
+    def ls(modes, scales):
+        n = len(modes)
+        z = np.zeros(n, np.int64)
+        return layout.LeafSet(z, z, np.full(n, 4), np.asarray(modes, np.uint8), np.asarray(scales, np.float32), z)
+
+    assert strip.strip_exp2(ls([0, 0], [5.0, 7.0])) == 0            # P0 leaves only
+    assert strip.strip_exp2(ls([4, 4], [0.0, 0.0])) == 0            # zero scales only
+    for smax in (0.75, 1.0, 3.0, 1e-3, -40.0):
+        e = strip.strip_exp2(ls([4, 0, 8], [smax, 1e6, smax / 3]))  # the P0 leaf's scale is ignored
+        assert 0.5 < abs(smax) * 2.0 ** e <= 1.0, (smax, e)
+    assert strip.strip_exp2(ls([4], [1e-38])) == 100                # clamped
