@@ -324,6 +324,11 @@ MTC_API int mtc_strip_partition(const uint32_t* batch_off, const uint32_t* strip
                                 int32_t target_ctas, int32_t max_batches, int32_t max_ctas, uint32_t* cta_part,
                                 int32_t* n_cta, uint32_t* max_cta_batches);
 
+/* 1 when mtc_strip_decode can run this stream at M tokens (the gathered
+ * activations, M x K fp16, and the batch slots fit shared memory), else 0.
+ * Host-only query, no CUDA call. */
+MTC_API int mtc_strip_fits(const mtc_strip_desc* s, int32_t M);
+
 /* Decode GEMM over the strip stream for M <= 4: Y[:, col_perm] =
  * X[:, row_perm] @ Wp (replaces mtc_gemm, gemm.py:541-574, and the
  * gather/GEMM/scatter of permutation.py:15-21).  X is M x K fp32, Y is

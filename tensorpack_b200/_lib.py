@@ -101,6 +101,7 @@ SIGNATURES = {
     "mtc_strip_check": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32]),
     "mtc_strip_partition": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, ctypes.POINTER(c_i32),
                                     ctypes.POINTER(c_u32)]),
+    "mtc_strip_fits": (c_i32, [ctypes.POINTER(StripDesc), c_i32]),
     "mtc_strip_decode": (c_i32, [ctypes.POINTER(StripDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, _EP, c_p]),
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),
     "mtc_gemm_prefill": (c_i32, [ctypes.POINTER(StreamDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64,

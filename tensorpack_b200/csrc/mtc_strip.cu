@@ -488,6 +488,14 @@ bool make_plan(const mtc_strip_desc* s, int M, bool wide, Plan* pl) {
 
 using namespace mtc;
 
+extern "C" int mtc_strip_fits(const mtc_strip_desc* s, int32_t M) {
+  if (!s || M < 1 || M > strip::kMaxM) return 0;
+  const bool wide = (s->flags & MTC_STRIP_WIDE) != 0;
+  const int per = wide ? 2 : strip::kMaxM;
+  Plan pl;
+  return make_plan(s, M < per ? M : per, wide, &pl) ? 1 : 0;
+}
+
 extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t M, int64_t ldx,
                                 const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
                                 uint32_t* status, const mtc_epilogue* ep, void* stream) {

@@ -335,6 +335,15 @@ class DeviceStream:
             self._strip = DeviceStrip(self._mat.host_strip(), self.device)
         return self._strip
 
+    def strip_fits(self, M: int) -> bool:
+        """Whether the strip kernel can run this matrix at M tokens (its
+        gathered activations and batch slots fit shared memory; K up to
+        about 24K at M = 3..4, about 100K at M = 1)."""
+        fits = self.__dict__.setdefault("_strip_fits", {})
+        if M not in fits:
+            fits[M] = bool(_lib.load().mtc_strip_fits(ctypes.byref(self.strip().desc), M))
+        return fits[M]
+
     def decode_strip(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
         """Y[:M] = X @ W for M <= 4 (mma.sync kernel over the strip stream);
         ``ep`` from ``epilogue()`` fuses a bias and activation."""
@@ -393,10 +402,11 @@ class DeviceStream:
 
     def matmul(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
         """Y = X @ W (+ the fused epilogue ``ep``): the strip-stream decode for
-        M <= 4 (``decode_kernel = "tensor"`` selects the tcgen05 decode), the
-        tcgen05 decode for M <= 16, the tensor-core prefill kernel above."""
+        M <= 4 when it fits (``decode_kernel = "tensor"`` selects the tcgen05
+        decode), the tcgen05 decode for M <= 16, the tensor-core prefill
+        kernel above."""
         M = X.shape[0]
-        if M <= STRIP_MAX_M and self.decode_kernel == "strip":
+        if M <= STRIP_MAX_M and self.decode_kernel == "strip" and self.strip_fits(M):
             return self.decode_strip(X, Y, ep)
         if M <= DECODE_MAX_M:
             return self.decode(X, Y, ep)

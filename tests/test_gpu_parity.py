@@ -75,9 +75,11 @@ def run_gemm(m, X, dev):
 
 
 def uses_strip(ds, M):
+    """Whether DeviceStream.matmul runs the strip-stream decode for M tokens
+    (the same rule as matmul)."""
     from tensorpack_b200.kernels.device import STRIP_MAX_M
 
-    return M <= STRIP_MAX_M and ds.decode_kernel == "strip"
+    return M <= STRIP_MAX_M and ds.decode_kernel == "strip" and ds.strip_fits(M)
 
 
 def check_gemm(m, W_deq_orig, W_stored, X, dev):

@@ -412,3 +412,25 @@ def test_strip_exp2_edge_cases():
         e = strip.strip_exp2(ls([4, 0, 8], [smax, 1e6, smax / 3]))  # the P0 leaf's scale is ignored
         assert 0.5 < abs(smax) * 2.0 ** e <= 1.0, (smax, e)
     assert strip.strip_exp2(ls([4], [1e-38])) == 100                # clamped
+
+
+def test_strip_fits_shared_memory_limits():
+    """The host-side query mirrors the launch plan: the gathered activations
+    (M x K fp16) must fit next to the batch slots."""
+    import ctypes
+
+    from tensorpack_b200 import _lib
+
+    lib = _lib.load()
+    hs = _llm_host()
+    part, n, most = hs.partition(4)
+    d = hs.desc(16, 16, 16, part, n, most)
+    for M in (1, 2, 3, 4):
+        assert lib.mtc_strip_fits(ctypes.byref(d), M) == 1
+    assert lib.mtc_strip_fits(ctypes.byref(d), 0) == 0 and lib.mtc_strip_fits(ctypes.byref(d), 5) == 0
+    big = _lib.StripDesc.from_buffer_copy(d)
+    big.tk = 28672 // 32  # Llama-70B down_proj K
+    assert lib.mtc_strip_fits(ctypes.byref(big), 1) == 1
+    assert lib.mtc_strip_fits(ctypes.byref(big), 4) == 0   # 4 x 28672 fp16 rows do not fit with the slots
+    big.tk = 200000 // 32
+    assert lib.mtc_strip_fits(ctypes.byref(big), 1) == 0
