@@ -4,7 +4,7 @@
  * The reference (Sharexi/TensorPack, "MTC") is a Python + Numba package; its
  * hot path is the packed GEMM `mtc.kernels.gemm.mtc_gemm` over an `MTCMatrix`
  * (mtc/kernels/gemm.py:217-574).  This header is the native boundary a
- * Python caller binds with ctypes (see INTEGRATION.md): plain pointers, sizes
+ * Python caller binds with ctypes: plain pointers, sizes
  * and a CUDA stream handle passed as `void*`; no C++ or torch types.
  *
  * Conventions
@@ -18,8 +18,10 @@
  *    15-21); row_perm / col_perm may be NULL for an unpermuted matrix.
  *  - Calls enqueue work on `stream` and do not synchronise, except
  *    mtc_repack_plan which reads back one 8-byte total.
- *  - The library holds no global mutable state: concurrent calls on
- *    different streams with different buffers are independent.
+ *  - Apart from mtc_gemv_static, the library holds no global mutable state:
+ *    concurrent calls on different streams with different buffers are
+ *    independent.  mtc_gemv_static keeps its scratch in one array per device
+ *    built into the library, so its calls must not overlap on the GPU.
  */
 #ifndef MTC_B200_H
 #define MTC_B200_H
@@ -144,6 +146,21 @@ MTC_API int mtc_abi_version(void);
 MTC_API const char* mtc_last_error(void);
 MTC_API int mtc_device_sm_count(int device);
 
+/* Limit, in ns, of every bounded pipeline wait (mbarrier, ticket) in the
+ * kernels launched after this call by any thread of the process; 0 restores
+ * the default of 2 s.  A wait that runs out sets MTC_STATUS_TIMEOUT, the
+ * kernel drains its own copies in flight (bounded) and returns without
+ * writing its output.  No counterpart in the reference (it has no GPU
+ * pipeline): a diagnostic of this library, also used by its tests. */
+MTC_API int mtc_set_wait_limit_ns(uint64_t ns);
+
+/* Diagnostic for tests of the timeout path: the NEXT mtc_strip_decode call
+ * (this process, any thread) makes every warp's first batch expect `bytes`
+ * (a multiple of 16, at most 4096) more than it copies, so that wait can
+ * never complete and runs out at the wait limit; the call after it is
+ * unaffected.  0 cancels a pending hold.  No counterpart in the reference. */
+MTC_API int mtc_debug_withhold_bytes(uint32_t bytes);
+
 /* Byte copy by the copy engines (cudaMemcpyAsync, device to device) on
  * `stream`; dst or src may be a peer GPU's memory mapped into this process
  * (symmetric memory), in which case the bytes cross NVLink without using
@@ -259,9 +276,10 @@ MTC_API int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, int6
  * micro-blocks are sorted by precision into steps that one warp consumes
  * with straight-line code, and consecutive steps of a strip form batch
  * records that one bulk copy moves.  See tensorpack_b200/csrc/mtc_strip.cuh
- * for the byte layout.  All pointers but cta_part are device pointers for
- * mtc_strip_decode. */
-#define MTC_STRIP_MAX_CTA 480     /* most CTA ranges of one strip-kernel launch */
+ * for the byte layout.  The kernel runs a static schedule
+ * (mtc_strip_schedule) that deals strips to CTAs and cuts each CTA's batch
+ * records into one contiguous range per warp.  All pointers are device
+ * pointers for mtc_strip_decode. */
 #define MTC_STRIP_WIDE 1u         /* stream flag: group steps of 16 groups, each lane both column quartets
                                      of one group's k half (four MMAs per B fragment) */
 #define MTC_STRIP_MERGE_MODES 2u  /* build flag (mtc_strip_plan / _fill only): P2 items packed with the P3
@@ -271,17 +289,19 @@ typedef struct mtc_strip_desc {
   const uint8_t* stream;        /* batch records, 16-byte aligned */
   const uint32_t* batch_off;    /* [n_batches + 1] byte offset of each batch record (last = total) */
   const uint32_t* strip_batch;  /* [n_strips + 1] first batch of each strip (last = n_batches) */
-  const uint32_t* cta_part;     /* HOST, [2 (n_cta + 1)]: first strip and first batch of each CTA's range
-                                   (mtc_strip_partition); the end pair is (n_strips, n_batches) */
+  const uint32_t* work;         /* [2 n_batches] schedule: per batch record in warp order {byte offset,
+                                   (bytes / 16) | slot << 12 | flush << 31} (mtc_strip_schedule) */
+  const uint32_t* warp_work;    /* [n_cta n_warps + 1] first work item of each warp */
+  const uint32_t* red;          /* [3 n_strips] {strip, first slot, slot count}, grouped by CTA */
+  const uint32_t* cta_red;      /* [n_cta + 1] first `red` entry of each CTA */
   int32_t K, N;                 /* logical shape of W */
   int32_t tk, tn;               /* 32x32 tiles along K and N (padded up) */
   int32_t n_strips, n_batches;  /* n_strips = 4 tn */
   int32_t exp2;                 /* the stream's scales are scale * 2^exp2 */
   uint32_t max_batch_bytes;     /* largest batch record */
-  int32_t n_cta;                /* CTA ranges, 1..MTC_STRIP_MAX_CTA */
-  uint32_t max_cta_batches;     /* most batch records in one CTA range */
+  int32_t n_cta, n_warps;       /* schedule grid: CTAs (1..n_strips) x warps per CTA */
+  uint32_t max_cta_slots;       /* most partial-sum slots (strip segments) of one CTA */
   uint32_t flags;               /* MTC_STRIP_* flags the stream was built with */
-  int32_t pad_;
   uint64_t stream_bytes;
 } mtc_strip_desc;
 
@@ -314,18 +334,23 @@ MTC_API int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, const 
                             const uint32_t* strip_batch, int32_t n_batches, int32_t n_strips, int32_t tk,
                             uint32_t max_batch_bytes, uint32_t flags);
 
-/* Split a strip stream into CTA ranges for mtc_strip_decode (host pointers,
- * no CUDA call): contiguous ranges of whole strips balanced by record bytes
- * over `target_ctas` (normally the SM count), each holding at most
- * `max_batches` batch records unless a single strip has more.  Writes
- * cta_part (2 (n_cta + 1) words, room for max_ctas + 1 pairs), n_cta and the
- * largest range's batch count. */
-MTC_API int mtc_strip_partition(const uint32_t* batch_off, const uint32_t* strip_batch, int32_t n_strips,
-                                int32_t target_ctas, int32_t max_batches, int32_t max_ctas, uint32_t* cta_part,
-                                int32_t* n_cta, uint32_t* max_cta_batches);
+/* Static schedule of a strip stream for mtc_strip_decode on `n_cta` CTAs
+ * (1..n_strips, normally the SM count) of `n_warps` warps (host pointers, no
+ * CUDA call).  Strips go to CTAs by estimated decode cost (longest first,
+ * each to the least loaded CTA); each CTA's batch records, in strip order,
+ * are cut into n_warps contiguous ranges of equal estimated cost.  The part
+ * of a strip that one warp holds is a segment with its own partial-sum slot;
+ * the last work item of a segment carries the flush bit.  Outputs (host
+ * arrays sized by the caller): work [2 n_batches], warp_work
+ * [n_cta n_warps + 1], red [3 n_strips], cta_red [n_cta + 1] and the most
+ * slots of one CTA.  The stream must have passed mtc_strip_check. */
+MTC_API int mtc_strip_schedule(const uint8_t* stream, const uint32_t* batch_off, const uint32_t* strip_batch,
+                               int32_t n_strips, int32_t n_cta, int32_t n_warps, uint32_t flags, uint32_t* work,
+                               uint32_t* warp_work, uint32_t* red, uint32_t* cta_red, uint32_t* max_slots);
 
 /* 1 when mtc_strip_decode can run this stream at M tokens (the gathered
- * activations, M x K fp16, and the batch slots fit shared memory), else 0.
+ * activations, M x K fp16, the partial-sum slots and the batch slots of the
+ * schedule's warps fit shared memory), else 0.
  * Host-only query, no CUDA call. */
 MTC_API int mtc_strip_fits(const mtc_strip_desc* s, int32_t M);
 
@@ -334,10 +359,10 @@ MTC_API int mtc_strip_fits(const mtc_strip_desc* s, int32_t M);
  * gather/GEMM/scatter of permutation.py:15-21).  X is M x K fp32, Y is
  * M x N fp32.  Products are q * fp16(fp16(x) * fp16(scale * 2^exp2)) on
  * the tensor cores (mma.sync, fp32 accumulation); the fp32 path computes
- * q * (fp16(x) * scale * 2^exp2) in fp32.  One CTA per range of
- * `s->cta_part`; partial sums and tickets live in shared memory, so the
- * call takes no workspace and leaves no state behind.  `status` (nullable)
- * receives MTC_STATUS_* bits. */
+ * q * (fp16(x) * scale * 2^exp2) in fp32.  The launch is s->n_cta CTAs of
+ * s->n_warps warps running the descriptor's schedule; partial sums live in
+ * shared memory, so the call takes no workspace and leaves no state behind.
+ * `status` (nullable) receives MTC_STATUS_* bits. */
 MTC_API int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t M, int64_t ldx,
                              const int32_t* row_perm, const int32_t* col_perm, float* Y, int64_t ldy,
                              uint32_t* status, const mtc_epilogue* ep, void* stream);

@@ -18,22 +18,34 @@ __all__ = ["MTCMatrix", "mtc_gemm", "MemoryArena", "PrecisionMode", "install_mtc
 
 
 def install_mtc_alias():
-    """Make ``import mtc.kernels.gemm`` / ``mtc.nn.layers`` / ``mtc.core.types``
-    / ``mtc.core.arena`` resolve to this package (for unmodified callers)."""
+    """Make the reference's import paths resolve to this package, for
+    unmodified callers: ``mtc.kernels.gemm`` (MTCMatrix, mtc_gemm),
+    ``mtc.nn.layers`` (LinearMTCAdaptive, LinearFP32), ``mtc.core.types``,
+    ``mtc.core.arena``, and ``mtc.core.quadtree`` / ``mtc.core.permutation``
+    (QuadtreeRD, PermutedQuadtreeRD, qt_dequant, permuted_qt_dequant,
+    unpermute, index_bits: the GPU allocators and exact reconstructions).
+    Returns the ``mtc`` package object."""
     import types
 
-    from . import core, kernels, nn
-    from .core import arena, types as ctypes_mod
+    from . import quant
+    from .core import arena, types as types_mod
     from .kernels import gemm
     from .nn import layers
 
-    pkg = types.ModuleType("mtc")
-    pkg.__path__ = []
-    pkg.PrecisionMode = PrecisionMode
-    pkg.MemoryArena = MemoryArena
-    mods = {"mtc": pkg, "mtc.core": core, "mtc.core.types": ctypes_mod, "mtc.core.arena": arena,
+    def package(name, **children):
+        mod = types.ModuleType(name)
+        mod.__path__ = []
+        for k, v in children.items():
+            setattr(mod, k, v)
+        return mod
+
+    core = package("mtc.core", types=types_mod, arena=arena, quadtree=quant, permutation=quant)
+    kernels = package("mtc.kernels", gemm=gemm)
+    nn = package("mtc.nn", layers=layers)
+    pkg = package("mtc", core=core, kernels=kernels, nn=nn, PrecisionMode=PrecisionMode, MemoryArena=MemoryArena)
+    mods = {"mtc": pkg, "mtc.core": core, "mtc.core.types": types_mod, "mtc.core.arena": arena,
+            "mtc.core.quadtree": quant, "mtc.core.permutation": quant,
             "mtc.kernels": kernels, "mtc.kernels.gemm": gemm, "mtc.nn": nn, "mtc.nn.layers": layers}
     for name, mod in mods.items():
         sys.modules[name] = mod
-    pkg.core, pkg.kernels, pkg.nn = core, kernels, nn
     return pkg

@@ -49,20 +49,20 @@ assert ctypes.sizeof(StreamDesc) == 104
 
 
 class StripDesc(ctypes.Structure):
-    """struct mtc_strip_desc (cta_part is a host pointer)."""
+    """struct mtc_strip_desc (all pointers on the device)."""
 
     _fields_ = [
-        ("stream", c_p), ("batch_off", c_p), ("strip_batch", c_p), ("cta_part", c_p),
+        ("stream", c_p), ("batch_off", c_p), ("strip_batch", c_p),
+        ("work", c_p), ("warp_work", c_p), ("red", c_p), ("cta_red", c_p),
         ("K", c_i32), ("N", c_i32), ("tk", c_i32), ("tn", c_i32),
         ("n_strips", c_i32), ("n_batches", c_i32), ("exp2", c_i32), ("max_batch_bytes", c_u32),
-        ("n_cta", c_i32), ("max_cta_batches", c_u32), ("flags", c_u32), ("pad_", c_i32), ("stream_bytes", c_u64),
+        ("n_cta", c_i32), ("n_warps", c_i32), ("max_cta_slots", c_u32), ("flags", c_u32), ("stream_bytes", c_u64),
     ]
 
 
-assert ctypes.sizeof(StripDesc) == 88
+assert ctypes.sizeof(StripDesc) == 112
 STRIP_WIDE = 1
 STRIP_MERGE_MODES = 2
-STRIP_MAX_CTA = 480
 
 
 class Epilogue(ctypes.Structure):
@@ -82,6 +82,8 @@ SIGNATURES = {
     "mtc_last_error": (ctypes.c_char_p, []),
     "mtc_device_sm_count": (c_i32, [c_i32]),
     "mtc_copy_async": (c_i32, [c_p, c_p, c_size, c_p]),
+    "mtc_set_wait_limit_ns": (c_i32, [c_u64]),
+    "mtc_debug_withhold_bytes": (c_i32, [c_u32]),
     "mtc_repack_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_p,
                                 ctypes.POINTER(c_u64), c_p]),
     "mtc_repack_fill": (c_i32, [c_p, c_u64, c_p, c_p, ctypes.POINTER(StreamDesc), c_p, c_p, c_p]),
@@ -99,8 +101,8 @@ SIGNATURES = {
     "mtc_strip_plan": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_u32, ctypes.POINTER(c_u64)]),
     "mtc_strip_fill": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32, c_u32, c_p, c_p, c_p]),
     "mtc_strip_check": (c_i32, [c_p, c_u64, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_u32]),
-    "mtc_strip_partition": (c_i32, [c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_p, ctypes.POINTER(c_i32),
-                                    ctypes.POINTER(c_u32)]),
+    "mtc_strip_schedule": (c_i32, [c_p, c_p, c_p, c_i32, c_i32, c_i32, c_u32, c_p, c_p, c_p, c_p,
+                                   ctypes.POINTER(c_u32)]),
     "mtc_strip_fits": (c_i32, [ctypes.POINTER(StripDesc), c_i32]),
     "mtc_strip_decode": (c_i32, [ctypes.POINTER(StripDesc), c_p, c_i32, c_i64, c_p, c_p, c_p, c_i64, c_p, _EP, c_p]),
     "mtc_prefill_workspace_bytes": (c_size, [ctypes.POINTER(StreamDesc), c_i32, c_i32]),

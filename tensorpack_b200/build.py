@@ -3,13 +3,16 @@
     python -m tensorpack_b200.build [--force]
 
 Objects go to ``tensorpack_b200/_build/``; the shared library is written next
-to this file so it travels with the package.  A rebuild happens when any
-source or header is newer than the library.
+to this file so it travels with the package.  The library carries a SHA-256
+of its sources, headers and compiler flags (a marker string in its read-only
+data); a rebuild happens when that hash differs from the sources on disk, so
+a stale prebuilt library shipped next to newer sources is never used.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -50,11 +53,36 @@ def _deps():
     return out
 
 
+HASH_MARKER = b"MTC_SOURCE_HASH="
+
+
+def source_hash() -> str:
+    """SHA-256 over the compiler flags and every source and header (by name
+    and content), in a fixed order."""
+    h = hashlib.sha256()
+    h.update(" ".join(ARCH + FLAGS[:-1]).encode())
+    for p in sorted(_deps(), key=os.path.basename):
+        h.update(os.path.basename(p).encode() + b"\0")
+        with open(p, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+def library_hash(path: str = LIB):
+    """The source hash recorded in a built library, or None."""
+    try:
+        with open(path, "rb") as f:
+            data = f.read()
+    except OSError:
+        return None
+    i = data.find(HASH_MARKER)
+    if i < 0:
+        return None
+    return data[i + len(HASH_MARKER):i + len(HASH_MARKER) + 64].decode("ascii", errors="replace")
+
+
 def needs_build() -> bool:
-    if not os.path.exists(LIB):
-        return True
-    t = os.path.getmtime(LIB)
-    return any(os.path.getmtime(p) > t for p in _deps())
+    return library_hash(LIB) != source_hash()
 
 
 def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB, build_dir: str = BUILD) -> str:
@@ -63,10 +91,13 @@ def build(force: bool = False, verbose: bool = False, defines=(), out: str = LIB
         return LIB
     os.makedirs(build_dir, exist_ok=True)
     cc = nvcc()
+    digest = source_hash()
 
     def compile_one(src):
         obj = os.path.join(build_dir, os.path.basename(src)[:-3] + ".o")
         cmd = [cc, *ARCH, *FLAGS, *("-D" + d for d in defines), "-c", src, "-o", obj]
+        if os.path.basename(src) == "mtc_abi.cu":
+            cmd.insert(-4, f"-DMTC_SOURCE_HASH=\"{digest}\"")
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -27,7 +27,8 @@ STRIP_FORMAT_VERSION = 1
 BATCH_BYTES = 4096   # largest batch record (one shared-memory slot of the kernel)
 BATCH_STEPS = 64     # most steps per batch record
 MAX_M = 4            # tokens per strip-kernel call
-CTA_BATCHES = 128    # most batch records per CTA range (shared-memory partial sums)
+WARPS = 16           # warps per CTA of the decode kernel's schedule (M = 2..4)
+WARPS_M1 = 24        # ... and for M = 1 (fewer registers per token: more warps fit)
 
 
 def strip_exp2(ls: layout.LeafSet) -> int:
@@ -66,36 +67,57 @@ class HostStripStream:
     def n_batches(self) -> int:
         return int(self.batch_off.shape[0] - 1)
 
-    def partition(self, target_ctas: int, max_batches: int = CTA_BATCHES):
-        """CTA ranges for the decode kernel: (cta_part uint32 [2 (n + 1)], n,
-        largest range's batch count)."""
+    def schedule(self, n_cta: int, n_warps: int = WARPS) -> "StripSchedule":
+        """The decode kernel's static schedule on ``n_cta`` CTAs (capped at the
+        strip count) of ``n_warps`` warps, built on the host."""
         lib = _lib.load()
-        part = np.zeros(2 * (_lib.STRIP_MAX_CTA + 1), dtype=np.uint32)
-        n = ctypes.c_int32()
-        most = ctypes.c_uint32()
-        _lib.check(lib.mtc_strip_partition(self.batch_off.ctypes.data, self.strip_batch.ctypes.data, self.n_strips,
-                                           int(target_ctas), int(max_batches), _lib.STRIP_MAX_CTA,
-                                           part.ctypes.data, ctypes.byref(n), ctypes.byref(most)), "strip partition")
-        return part[:2 * (n.value + 1)].copy(), n.value, most.value
+        n_cta = max(1, min(int(n_cta), self.n_strips))
+        work = np.zeros(2 * self.n_batches, dtype=np.uint32)
+        warp_work = np.zeros(n_cta * n_warps + 1, dtype=np.uint32)
+        red = np.zeros(3 * self.n_strips, dtype=np.uint32)
+        cta_red = np.zeros(n_cta + 1, dtype=np.uint32)
+        slots = ctypes.c_uint32()
+        _lib.check(lib.mtc_strip_schedule(self.stream.ctypes.data, self.batch_off.ctypes.data,
+                                          self.strip_batch.ctypes.data, self.n_strips, n_cta, int(n_warps),
+                                          int(self.flags), work.ctypes.data, warp_work.ctypes.data, red.ctypes.data,
+                                          cta_red.ctypes.data, ctypes.byref(slots)), "strip schedule")
+        return StripSchedule(n_cta, int(n_warps), work, warp_work, red, cta_red, slots.value)
 
-    def desc(self, stream_ptr, batch_off_ptr, strip_batch_ptr, cta_part: np.ndarray, n_cta: int,
-             max_cta_batches: int) -> _lib.StripDesc:
-        """The C descriptor with the device pointers of an uploaded copy and
-        a CTA partition (``cta_part`` must stay alive while it is used)."""
+    def desc(self, stream_ptr, batch_off_ptr, strip_batch_ptr, sched: "StripSchedule", sched_ptrs) -> _lib.StripDesc:
+        """The C descriptor with the device pointers of an uploaded copy of
+        the stream and of ``sched``'s arrays (work, warp_work, red, cta_red)."""
+        work, warp_work, red, cta_red = sched_ptrs
         return _lib.StripDesc(
-            stream=stream_ptr, batch_off=batch_off_ptr, strip_batch=strip_batch_ptr, cta_part=cta_part.ctypes.data,
-            K=self.K, N=self.N, tk=self.tk, tn=self.tn, n_strips=self.n_strips, n_batches=self.n_batches,
-            exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, n_cta=n_cta, max_cta_batches=max_cta_batches,
-            flags=self.flags, stream_bytes=int(self.stream.nbytes))
+            stream=stream_ptr, batch_off=batch_off_ptr, strip_batch=strip_batch_ptr, work=work, warp_work=warp_work,
+            red=red, cta_red=cta_red, K=self.K, N=self.N, tk=self.tk, tn=self.tn, n_strips=self.n_strips,
+            n_batches=self.n_batches, exp2=self.exp2, max_batch_bytes=self.max_batch_bytes, n_cta=sched.n_cta,
+            n_warps=sched.n_warps, max_cta_slots=sched.max_slots, flags=self.flags,
+            stream_bytes=int(self.stream.nbytes))
+
+
+@dataclass
+class StripSchedule:
+    """Static schedule of the strip decode kernel (mtc_strip_schedule): work
+    items {offset, (bytes / 16) | slot << 12 | flush << 31} in warp order,
+    the first item of each warp, and per CTA the strips with their
+    partial-sum slot ranges."""
+
+    n_cta: int
+    n_warps: int
+    work: np.ndarray       # uint32 [2 n_batches]
+    warp_work: np.ndarray  # uint32 [n_cta n_warps + 1]
+    red: np.ndarray        # uint32 [3 n_strips]
+    cta_red: np.ndarray    # uint32 [n_cta + 1]
+    max_slots: int
 
 
 def build_host(mat, batch_bytes: int = BATCH_BYTES, batch_steps: int = BATCH_STEPS,
-               wide: bool = False, merge_modes: bool = False) -> HostStripStream:
+               wide: bool = False, merge_modes: bool = True) -> HostStripStream:
     """Build the strip stream of an MTCMatrix on the host (no GPU needed).
     ``wide`` packs group steps of 16 groups with two micro-blocks per lane
-    (MTC_STRIP_WIDE); ``merge_modes`` packs P2 items with the P3 decoder and
-    P6 items with the P8 one (exact, fewer step kinds).  Both are checked on
-    the CPU model of the kernel only so far and are off by default."""
+    (MTC_STRIP_WIDE, measured slower on the B200, kept for comparison);
+    ``merge_modes`` (default) packs P2 items with the P3 decoder and P6 items
+    with the P8 one: exact, and fewer step kinds and partial steps."""
     flags = (_lib.STRIP_WIDE if wide else 0) | (_lib.STRIP_MERGE_MODES if merge_modes else 0)
     lib = _lib.load()
     K, N = (int(v) for v in mat.shape)
@@ -146,7 +168,10 @@ def import_host(mat, meta: dict, arrs: dict) -> "HostStripStream | None":
     try:
         ok = (int(meta["version"]) == STRIP_FORMAT_VERSION and int(meta["K"]) == K and int(meta["N"]) == N
               and int(meta["tk"]) == -(-K // layout.TILE) and int(meta["tn"]) == -(-N // layout.TILE)
-              and int(meta["exp2"]) == strip_exp2(mat.leaf_set))
+              and int(meta["exp2"]) == strip_exp2(mat.leaf_set)
+              # only the default form is attached to a matrix; another form
+              # (wide steps, larger batch records) is rebuilt in the default one
+              and int(meta.get("flags", 0)) == 0 and int(meta.get("max_batch_bytes", 0)) <= BATCH_BYTES)
     except (KeyError, TypeError, ValueError):
         return None
     if not ok:

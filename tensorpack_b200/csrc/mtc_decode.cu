@@ -556,7 +556,7 @@ extern "C" int mtc_decode(const mtc_stream_desc* s, const float* X, int32_t M, i
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
-  p.timeout_ns = 2000000000ull;
+  p.timeout_ns = wait_limit_ns();
   p.ep = Epi{epa.bias, epa.act};
   MTC_CHECK_CUDA(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem),
                  "mtc_decode: smem attribute");

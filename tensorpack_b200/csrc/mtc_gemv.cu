@@ -323,7 +323,7 @@ extern "C" int mtc_gemv(const mtc_stream_desc* s, const float* X, int32_t M, int
   p.x_stride = pl.x_stride;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
-  p.timeout_ns = 2000000000ull;
+  p.timeout_ns = wait_limit_ns();
   cudaStream_t st = as_stream(stream);
   // The opt-in to large dynamic shared memory is a per-device attribute:
   // set it on every call, so every device a process uses gets it.

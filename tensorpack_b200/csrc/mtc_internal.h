@@ -66,6 +66,12 @@ inline int read_epilogue(const mtc_epilogue* ep, EpiArg* out, const char* who) {
   return MTC_OK;
 }
 
+// Limit of every bounded pipeline wait of the next launches, in ns (2 s
+// unless mtc_set_wait_limit_ns changed it), and the diagnostic hold of
+// mtc_debug_withhold_bytes, taken (and cleared) by the next strip launch.
+unsigned long long wait_limit_ns();
+uint32_t take_withheld_bytes();
+
 // Shared launch helpers (mtc_prefill.cu): the X row gather into fp16 Xp and
 // the TMA descriptor of Xp used by the prefill and decode kernels.
 int launch_gather_x(const float* X, long long ldx, int K, int Kp, const int32_t* row_perm, int M, __half* Xp,

@@ -902,7 +902,7 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   p.ring_bytes = pl.ring_bytes;
   p.pow2e = ldexpf(1.0f, s->exp2);
   p.inv_pow2e = ldexpf(1.0f, -s->exp2);
-  p.timeout_ns = 2000000000ull;
+  p.timeout_ns = wait_limit_ns();
   p.ep = Epi{epa.bias, epa.act};
   const bool with_ep = epa.bias || epa.act;
   auto kernel = with_ep ? prefill_kernel<true> : prefill_kernel<false>;

@@ -497,45 +497,147 @@ extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, con
   return MTC_OK;
 }
 
-// CTA partition of a strip stream for the decode kernel: contiguous ranges of
-// whole strips, balanced by record bytes over `target_ctas` CTAs, each range
-// holding at most `max_batches` batch records (or one strip, if a single
-// strip has more).  Writes (first strip, first batch) of every range and the
-// end pair into cta_part (2 (n_cta + 1) words, host), n_cta and the largest
-// range's batch count.
-extern "C" int mtc_strip_partition(const uint32_t* batch_off, const uint32_t* strip_batch, int32_t n_strips,
-                                   int32_t target_ctas, int32_t max_batches, int32_t max_ctas, uint32_t* cta_part,
-                                   int32_t* n_cta_out, uint32_t* max_cta_batches_out) {
-  clear_error();
-  MTC_REQUIRE(batch_off && strip_batch && cta_part && n_cta_out && max_cta_batches_out,
-              "mtc_strip_partition: null pointer argument");
-  MTC_REQUIRE(n_strips >= 1 && target_ctas >= 1 && max_batches >= 1 && max_ctas >= 1,
-              "mtc_strip_partition: bad sizes");
-  auto sbytes = [&](int s) { return (uint64_t)batch_off[strip_batch[s + 1]] - batch_off[strip_batch[s]]; };
-  auto sbat = [&](int s) { return strip_batch[s + 1] - strip_batch[s]; };
-  const uint64_t total = (uint64_t)batch_off[strip_batch[n_strips]];
-  uint64_t done = 0;
-  uint32_t most = 0;
-  int c = 0, s = 0;
-  cta_part[0] = 0;
-  cta_part[1] = 0;
-  while (s < n_strips) {
-    MTC_REQUIRE(c < max_ctas, "mtc_strip_partition: more than %d CTA ranges needed", max_ctas);
-    const uint64_t target = (total - done) / (uint64_t)std::max(1, target_ctas - c);
-    uint64_t bytes = 0;
-    uint32_t nb = 0;
-    do {
-      bytes += sbytes(s);
-      nb += sbat(s);
-      ++s;
-    } while (s < n_strips && nb + sbat(s) <= (uint32_t)max_batches && bytes + sbytes(s) / 2 <= target);
-    done += bytes;
-    most = std::max(most, nb);
-    ++c;
-    cta_part[2 * c] = (uint32_t)s;
-    cta_part[2 * c + 1] = strip_batch[s];
+// Static schedule of a strip stream for the decode kernel.
+//
+// Cost model, in units of about one warp instruction at full issue, fitted
+// to per-batch clock counts of the kernel on the Llama-3-8B gate layer: a
+// step costs its decode by class (more for the micro-block layout and for
+// classes with a secondary plane), every dispatch (the head of a run of full
+// steps, or a partial step) adds the latency of reading and branching on its
+// descriptor, a generic step runs the fp32 path, and every batch record adds
+// its header and loop.  Only ratios matter: the schedule balances estimated
+// warp time, not bytes.
+__host__ inline int sched_step_cost(uint32_t d, bool wide) {
+  const int kind = desc_kind(d);
+  if (kind == kGeneric) return 170;
+  static const int group_cost[6] = {36, 40, 36, 50, 46, 40};  // P2, P3, P4, P5, P6, P8
+  static const int micro_cost[6] = {40, 46, 39, 61, 50, 45};
+  int body = kind < kU2 ? group_cost[kind] : micro_cost[kind - kU2];
+  if (wide && kind < kU2) body = body * 3 / 2;  // two micro-blocks per lane, one x load
+  return body;
+}
+constexpr int kSchedBatchCost = 48;
+constexpr int kSchedDispatchCost = 66;
+
+namespace {
+int schedule_impl(const uint8_t* stream, const uint32_t* batch_off, const uint32_t* strip_batch, int n_strips,
+                  int n_cta, int n_warps, bool wide, uint32_t* work, uint32_t* warp_work, uint32_t* red,
+                  uint32_t* cta_red, uint32_t* max_slots_out) {
+  const int n_batches = (int)strip_batch[n_strips];
+  // estimated cost of every batch record
+  std::vector<uint64_t> bcost(n_batches);
+  for (int b = 0; b < n_batches; ++b) {
+    const uint8_t* rec = stream + batch_off[b];
+    const uint32_t nst = ldu32(rec + 4);
+    uint64_t c = kSchedBatchCost;
+    for (uint32_t i = 0; i < nst;) {
+      const uint32_t d = ldu32(rec + 8 + 4 * i);
+      const uint32_t run = (uint32_t)std::max(1, desc_run(d));
+      c += kSchedDispatchCost + (uint64_t)run * sched_step_cost(d, wide);
+      i += run;
+    }
+    bcost[b] = c;
   }
-  *n_cta_out = c;
-  *max_cta_batches_out = most;
+  // strips to CTAs: longest first, each to the least loaded CTA
+  std::vector<uint64_t> scost(n_strips, 0);
+  for (int s = 0; s < n_strips; ++s)
+    for (uint32_t b = strip_batch[s]; b < strip_batch[s + 1]; ++b) scost[s] += bcost[b];
+  std::vector<int> order(n_strips);
+  for (int s = 0; s < n_strips; ++s) order[s] = s;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return scost[a] > scost[b]; });
+  std::vector<uint64_t> load(n_cta, 0);
+  std::vector<std::vector<int>> cta_strips(n_cta);
+  for (int s : order) {
+    int best = 0;
+    for (int c = 1; c < n_cta; ++c)
+      if (load[c] < load[best]) best = c;
+    load[best] += scost[s];
+    cta_strips[best].push_back(s);
+  }
+  uint32_t wi = 0, ri = 0, max_slots = 0;
+  for (int c = 0; c < n_cta; ++c) {
+    std::vector<int>& st = cta_strips[c];
+    std::sort(st.begin(), st.end());
+    std::vector<uint32_t> seq;  // batches of this CTA in order
+    for (int s : st)
+      for (uint32_t b = strip_batch[s]; b < strip_batch[s + 1]; ++b) seq.push_back(b);
+    const uint64_t total = load[c];
+    // cut seq into n_warps contiguous ranges at the batch boundary nearest each target
+    std::vector<size_t> cut(n_warps + 1, seq.size());
+    cut[0] = 0;
+    {
+      uint64_t acc = 0;
+      size_t i = 0;
+      for (int w = 1; w < n_warps; ++w) {
+        const uint64_t target = total * (uint64_t)w / (uint64_t)n_warps;
+        while (i < seq.size() && acc + bcost[seq[i]] <= target) acc += bcost[seq[i++]];
+        if (i < seq.size() && target - acc > acc + bcost[seq[i]] - target) acc += bcost[seq[i++]];
+        cut[w] = i;
+      }
+    }
+    // work items and flush slots: a segment is one warp's run of one strip
+    uint32_t slot = 0;
+    std::vector<uint32_t> strip_first(st.size(), 0), strip_cnt(st.size(), 0);
+    size_t sidx = 0;  // index into st of the strip at seq position
+    std::vector<int> strip_at(seq.size());
+    {
+      size_t k = 0;
+      for (size_t j = 0; j < st.size(); ++j)
+        for (uint32_t b = strip_batch[st[j]]; b < strip_batch[st[j] + 1]; ++b) strip_at[k++] = (int)j;
+    }
+    (void)sidx;
+    for (int w = 0; w < n_warps; ++w) {
+      warp_work[c * n_warps + w] = wi;
+      for (size_t i = cut[w]; i < cut[w + 1]; ++i) {
+        const uint32_t b = seq[i];
+        const int j = strip_at[i];
+        const bool first_of_seg = i == cut[w] || strip_at[i - 1] != j;
+        const bool last_of_seg = i + 1 == cut[w + 1] || strip_at[i + 1] != j;
+        if (first_of_seg) {
+          if (strip_cnt[j] == 0) strip_first[j] = slot;
+          ++strip_cnt[j];
+        }
+        const uint32_t bytes = batch_off[b + 1] - batch_off[b];
+        work[2 * wi] = batch_off[b];
+        work[2 * wi + 1] = (bytes >> 4) | (slot << 12) | (last_of_seg ? 0x80000000u : 0u);
+        ++wi;
+        if (last_of_seg) ++slot;
+      }
+    }
+    cta_red[c] = ri;
+    for (size_t j = 0; j < st.size(); ++j) {
+      red[3 * ri] = (uint32_t)st[j];
+      red[3 * ri + 1] = strip_first[j];
+      red[3 * ri + 2] = strip_cnt[j];
+      ++ri;
+    }
+    max_slots = std::max(max_slots, slot);
+  }
+  warp_work[n_cta * n_warps] = wi;
+  cta_red[n_cta] = ri;
+  *max_slots_out = max_slots;
   return MTC_OK;
+}
+}  // namespace
+
+extern "C" int mtc_strip_schedule(const uint8_t* stream, const uint32_t* batch_off, const uint32_t* strip_batch,
+                                  int32_t n_strips, int32_t n_cta, int32_t n_warps, uint32_t flags, uint32_t* work,
+                                  uint32_t* warp_work, uint32_t* red, uint32_t* cta_red, uint32_t* max_slots) {
+  clear_error();
+  MTC_REQUIRE(stream && batch_off && strip_batch && work && warp_work && red && cta_red && max_slots,
+              "mtc_strip_schedule: null pointer argument");
+  MTC_REQUIRE(n_strips >= 1 && n_cta >= 1 && n_cta <= n_strips && n_warps >= 1 && n_warps <= 32,
+              "mtc_strip_schedule: bad sizes (%d strips, %d CTAs, %d warps)", n_strips, n_cta, n_warps);
+  MTC_REQUIRE((flags & ~kWide) == 0, "mtc_strip_schedule: unknown stream flags 0x%x", flags);
+  for (int s = 0; s < n_strips; ++s)
+    MTC_REQUIRE(strip_batch[s + 1] > strip_batch[s], "mtc_strip_schedule: strip %d has no batch record", s);
+  const uint32_t n_batches = strip_batch[n_strips];
+  for (uint32_t b = 0; b < n_batches; ++b) {
+    const uint32_t bytes = batch_off[b + 1] - batch_off[b];
+    MTC_REQUIRE(batch_off[b + 1] > batch_off[b] && (bytes & 15u) == 0 && bytes <= 65520u && (batch_off[b] & 15u) == 0,
+                "mtc_strip_schedule: batch %u has a bad offset or size", b);
+  }
+  MTC_REQUIRE(n_batches < (1u << 19), "mtc_strip_schedule: %u batch records exceed the slot field", n_batches);
+  return schedule_impl(stream, batch_off, strip_batch, n_strips, n_cta, n_warps, (flags & kWide) != 0, work,
+                       warp_work, red, cta_red, max_slots);
 }

@@ -341,7 +341,7 @@ class DeviceStream:
         about 24K at M = 3..4, about 100K at M = 1)."""
         fits = self.__dict__.setdefault("_strip_fits", {})
         if M not in fits:
-            fits[M] = bool(_lib.load().mtc_strip_fits(ctypes.byref(self.strip().desc), M))
+            fits[M] = bool(_lib.load().mtc_strip_fits(ctypes.byref(self.strip().desc_for(M)), M))
         return fits[M]
 
     def decode_strip(self, X: torch.Tensor, Y: torch.Tensor, ep: Optional[_lib.Epilogue] = None) -> torch.Tensor:
@@ -349,7 +349,7 @@ class DeviceStream:
         ``ep`` from ``epilogue()`` fuses a bias and activation."""
         lib = _lib.load()
         st = self.strip()
-        _lib.check(lib.mtc_strip_decode(ctypes.byref(st.desc), X.data_ptr(), X.shape[0], X.stride(0),
+        _lib.check(lib.mtc_strip_decode(ctypes.byref(st.desc_for(X.shape[0])), X.data_ptr(), X.shape[0], X.stride(0),
                                         _ptr(self.row_perm), _ptr(self.col_perm), Y.data_ptr(), Y.stride(0),
                                         self.status.data_ptr(), _ep(ep), _stream(self.device)), "strip decode")
         return Y
@@ -436,22 +436,39 @@ class DeviceStream:
 class DeviceStrip:
     """The strip stream of one matrix on one device: batch records, batch
     offsets and per-strip batch ranges (uploaded from a HostStripStream),
-    the CTA partition for this device's SM count, and the C descriptor."""
+    the kernel's static schedules for this device's SM count (one with more
+    warps for M = 1, one for M = 2..4), and their C descriptors."""
 
-    def __init__(self, hs, device):
+    def __init__(self, hs, device, n_warps: Optional[int] = None):
+        from ..core import strip as _strip
+
         dev = torch.device(device)
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
+        sms = max(int(_lib.load().mtc_device_sm_count(dev.index)), 1)
+        warps = (n_warps, n_warps) if n_warps else (_strip.WARPS_M1, _strip.WARPS)
         with torch.cuda.device(dev):
             self.stream = torch.from_numpy(hs.stream).to(dev)
             self.batch_off = torch.from_numpy(hs.batch_off.view(np.int32)).to(dev)
             self.strip_batch = torch.from_numpy(hs.strip_batch.view(np.int32)).to(dev)
-        sms = int(_lib.load().mtc_device_sm_count(dev.index))
-        self.cta_part, self.n_cta, self.max_cta_batches = hs.partition(max(sms, 1))
         self.host = hs
         self.device = dev
-        self.desc = hs.desc(self.stream.data_ptr(), self.batch_off.data_ptr(), self.strip_batch.data_ptr(),
-                            self.cta_part, self.n_cta, self.max_cta_batches)
+        self._descs, self._keep = [], []
+        for nw in dict.fromkeys(warps):  # distinct warp counts, in order
+            sched = hs.schedule(sms, nw)
+            with torch.cuda.device(dev):
+                arrays = [torch.from_numpy(a.view(np.int32)).to(dev) for a in
+                          (sched.work, sched.warp_work, sched.red, sched.cta_red)]
+            self._keep.append((sched, arrays))
+            self._descs.append(hs.desc(self.stream.data_ptr(), self.batch_off.data_ptr(), self.strip_batch.data_ptr(),
+                                       sched, [a.data_ptr() for a in arrays]))
+        self.sched = self._keep[-1][0]
+        self.desc = self._descs[-1]      # M = 2..4 (and any M)
+        self.desc_m1 = self._descs[0]    # M = 1
+
+    def desc_for(self, M: int) -> _lib.StripDesc:
+        """The descriptor whose schedule serves M tokens."""
+        return self.desc_m1 if M == 1 else self.desc
 
     @property
     def stream_bytes(self) -> int:

@@ -1,4 +1,5 @@
-"""Quantized linear layer on the packed MTC GEMM (drop-in for mtc.nn)."""
-from .layers import LinearMTCAdaptive
+"""Quantized linear layer on the packed MTC GEMM (drop-in for mtc.nn), and
+the full-precision layer that callers compare it with."""
+from .layers import LinearFP32, LinearMTCAdaptive
 
-__all__ = ["LinearMTCAdaptive"]
+__all__ = ["LinearMTCAdaptive", "LinearFP32"]

@@ -27,6 +27,27 @@ _NP_ACT = {
 }
 
 
+class LinearFP32:
+    """The reference's full-precision linear layer (mtc/nn/layers.py:67-85),
+    inference part: seeded uniform(-1/sqrt(in), 1/sqrt(in)) weights,
+    ``forward(X) = X @ W + b``.  Kept so that callers which compare the
+    quantized layer against it run unchanged; it is not a packed path (numpy
+    in, numpy out, as in the reference)."""
+
+    def __init__(self, in_features: int, out_features: int, seed: int = 42):
+        rng = np.random.RandomState(seed)
+        bound = 1.0 / np.sqrt(in_features)
+        self.W = rng.uniform(-bound, bound, size=(in_features, out_features)).astype(np.float32)
+        self.b = np.zeros(out_features, dtype=np.float32)
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.W.nbytes + self.b.nbytes
+
+    def forward(self, X: np.ndarray) -> np.ndarray:
+        return np.asarray(X, np.float32) @ self.W + self.b
+
+
 class LinearMTCAdaptive(torch.nn.Module):
     """``activation`` (None, "relu", "silu", "gelu_tanh") is applied after the
     bias, fused into the GEMM's output pass on the GPU."""

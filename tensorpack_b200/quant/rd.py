@@ -45,18 +45,30 @@ def alpha_grid(mode: int) -> np.ndarray:
 
 @dataclass
 class Allocation:
-    """QTAllocation fields (mtc/core/quadtree.py:55-61); grids are numpy."""
+    """QTAllocation fields (mtc/core/quadtree.py:55-61); grids are numpy.
+    ``dequant`` (the exact reconstruction, quadtree.py:157-171) is computed
+    on first access by the GPU dequant kernel from the matrix the allocation
+    was made for."""
     sizes: Tuple[int, ...]
     leaf: Dict[int, np.ndarray]
     modes: Dict[int, np.ndarray]
     scales: Dict[int, np.ndarray]
     total_bits: int
     shape: Tuple[int, int]
-    dequant: Optional[np.ndarray] = None
+    source: Optional[np.ndarray] = field(default=None, repr=False)  # W the allocation was made for
+    _dequant: Optional[np.ndarray] = field(default=None, repr=False)
 
     @property
     def bits_per_element(self) -> float:
         return self.total_bits / (self.shape[0] * self.shape[1])
+
+    @property
+    def dequant(self) -> np.ndarray:
+        if self._dequant is None:
+            if self.source is None:
+                raise ValueError("this allocation does not hold its matrix; use qt_dequant(W, ...)")
+            self._dequant = _gpu_dequant(self.source, self)
+        return self._dequant
 
     def leaf_area_fraction(self) -> Dict[int, float]:
         n = self.shape[0] * self.shape[1]
@@ -65,17 +77,58 @@ class Allocation:
 
 @dataclass
 class PermutedAllocation:
-    """PermutedQTAllocation fields (mtc/core/permutation.py:54-67)."""
+    """PermutedQTAllocation fields (mtc/core/permutation.py:54-67); ``dequant``
+    is in the original channel order (permutation.py:76-79)."""
     inner: Allocation
     row_perm: np.ndarray
     col_perm: np.ndarray
     total_bits: int
-    dequant: Optional[np.ndarray] = None
+    source: Optional[np.ndarray] = field(default=None, repr=False)
+    _dequant: Optional[np.ndarray] = field(default=None, repr=False)
 
     @property
     def bits_per_element(self) -> float:
         K, N = self.inner.shape
         return self.total_bits / (K * N)
+
+    @property
+    def dequant(self) -> np.ndarray:
+        if self._dequant is None:
+            if self.source is None:
+                raise ValueError("this allocation does not hold its matrix; use permuted_qt_dequant(W, ...)")
+            self._dequant = _gpu_dequant(self.source, self)
+        return self._dequant
+
+
+def _gpu_dequant(W: np.ndarray, alloc) -> np.ndarray:
+    from ..kernels.gemm import MTCMatrix
+
+    return MTCMatrix.from_qt_allocation(np.asarray(W, np.float32), alloc).to_array()
+
+
+def qt_dequant(W, sizes, leaf, modes, scales) -> np.ndarray:
+    """Exact reconstruction of an MTC-QT allocation of W (the reference's
+    qt_dequant, mtc/core/quadtree.py:157-171), computed by the GPU dequant
+    kernel: q = clip(rint(w / s)) per leaf, then q * s in fp32."""
+    W = np.asarray(W, np.float32)
+    a = Allocation(tuple(int(s) for s in sizes), leaf, modes, scales, 0, W.shape)
+    return _gpu_dequant(W, a)
+
+
+def unpermute(Wp, row_perm, col_perm) -> np.ndarray:
+    """W with W[ix_(pr, pc)] = Wp (mtc/core/permutation.py:70-73)."""
+    Wp = np.asarray(Wp)
+    out = np.empty_like(Wp)
+    out[np.ix_(np.asarray(row_perm), np.asarray(col_perm))] = Wp
+    return out
+
+
+def permuted_qt_dequant(W, row_perm, col_perm, sizes, leaf, modes, scales) -> np.ndarray:
+    """Exact reconstruction of an MTC-QT-P allocation in the original channel
+    order (mtc/core/permutation.py:76-79), on the GPU."""
+    W = np.asarray(W, np.float32)
+    inner = Allocation(tuple(int(s) for s in sizes), leaf, modes, scales, 0, W.shape)
+    return _gpu_dequant(W, PermutedAllocation(inner, np.asarray(row_perm), np.asarray(col_perm), 0))
 
 
 class _Level:
@@ -101,6 +154,7 @@ class QuadtreeRD:
         self.device = torch.device(device if device is not None else "cuda")
         Wt = W if isinstance(W, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(W, dtype=np.float32))
         self.W = Wt.to(self.device, torch.float32).contiguous()
+        self.W_host = W if isinstance(W, np.ndarray) else None
         self.sizes = tuple(sorted(sizes, reverse=True))
         for a, b in zip(self.sizes, self.sizes[1:]):
             assert a == 2 * b, "quadtree levels must halve: e.g. (32, 16, 8)"
@@ -152,26 +206,32 @@ class QuadtreeRD:
     def select(self, bits_per_element: float) -> Allocation:
         budget = bits_per_element * self.shape[0] * self.shape[1]
         Dmax = max(float(c.D.max()) for c in self.levels.values())
-        ref = max(Dmax, 1e-30) / (2 * self.sizes[-1] ** 2)
-        lo_l, hi_l = np.log(ref * 1e-16), np.log(ref * 1e6)
-        best = self._solve(float(np.exp(hi_l)))
-        if float(best[0].sum()) > budget:
-            raise ValueError(f"Budget {bits_per_element} b/elem below the minimum "
-                             f"{float(best[0].sum()) / (self.shape[0] * self.shape[1]):.3f}")
+        scale_ref = max(Dmax, 1e-30) / (2 * self.sizes[-1] ** 2)
+        # bisection on log(lambda) between scale_ref * 1e-16 and scale_ref * 1e6,
+        # 60 halvings, keeping the cheapest solution that fits the budget
+        # (the same bracket and step count as the reference, for identical
+        # allocations: mtc/core/quadtree.py:126-140)
+        log_lo, log_hi = np.log(scale_ref * 1e-16), np.log(scale_ref * 1e6)
+        fit = self._solve(float(np.exp(log_hi)))
+        if float(fit[0].sum()) > budget:
+            raise ValueError(f"{bits_per_element} bits per element is below what this matrix needs "
+                             f"({float(fit[0].sum()) / (self.shape[0] * self.shape[1]):.3f} at the coarsest "
+                             f"allocation)")
         for _ in range(60):
-            mid = 0.5 * (lo_l + hi_l)
-            sol = self._solve(float(np.exp(mid)))
-            if float(sol[0].sum()) <= budget:
-                best, hi_l = sol, mid
+            lam_log = 0.5 * (log_lo + log_hi)
+            trial = self._solve(float(np.exp(lam_log)))
+            if float(trial[0].sum()) <= budget:
+                fit, log_hi = trial, lam_log
             else:
-                lo_l = mid
-        R, keep, idx = best
-        active = {self.sizes[0]: torch.ones_like(keep[self.sizes[0]])}
+                log_lo = lam_log
+        R, keep, idx = fit
+        # a node is a leaf when every ancestor was split and it is kept
+        reach = {self.sizes[0]: torch.ones_like(keep[self.sizes[0]])}
         leaf = {}
-        for s, s_next in zip(self.sizes, self.sizes[1:] + (None,)):
-            leaf[s] = active[s] & keep[s]
-            if s_next is not None:
-                active[s_next] = _up4(active[s] & ~keep[s])
+        for lvl, s in enumerate(self.sizes):
+            leaf[s] = reach[s] & keep[s]
+            if lvl + 1 < len(self.sizes):
+                reach[self.sizes[lvl + 1]] = _up4(reach[s] & ~keep[s])
         modes, scales = {}, {}
         mode_tab = torch.tensor(self.modes, dtype=torch.uint8, device=self.device)
         for s in self.sizes:
@@ -181,7 +241,7 @@ class QuadtreeRD:
             modes[s] = torch.where(leaf[s], mg, torch.zeros_like(mg)).cpu().numpy()
             scales[s] = torch.where(leaf[s], sg, torch.zeros_like(sg)).cpu().numpy()
         return Allocation(self.sizes, {s: leaf[s].cpu().numpy() for s in self.sizes}, modes, scales,
-                          int(float(R.sum())), self.shape)
+                          int(float(R.sum())), self.shape, source=self.W_host)
 
 
 def channel_orders(W: np.ndarray, importance, rows=True, cols=True):
@@ -213,4 +273,10 @@ class PermutedQuadtreeRD:
 
     def select(self, bits_per_element: float) -> PermutedAllocation:
         inner = self.qt.select(bits_per_element - self.perm_bits / self.W.size)
-        return PermutedAllocation(inner, self.pr, self.pc, inner.total_bits + self.perm_bits)
+        return PermutedAllocation(inner, self.pr, self.pc, inner.total_bits + self.perm_bits, source=self.W)
+
+
+def qt_allocate(W, bits_per_element: float, importance=None, sizes: Sequence[int] = (32, 16, 8),
+                modes: Sequence[int] = DEFAULT_MODES, device=None) -> Allocation:
+    """One-call MTC-QT allocation (mtc/core/quadtree.py:174-181), on the GPU."""
+    return QuadtreeRD(W, importance, sizes, modes, device=device).select(bits_per_element)

@@ -133,3 +133,15 @@ def forced_mode_allocation(K, N, seed=0, sizes=(32, 16, 8, 4), p_split=0.6):
         for j in range(N // root):
             visit(0, i, j)
     return W, tuple(sizes), leaf, modes, scales
+
+
+def gptq_layer(K=256, N=256, T=1024, seed=0):
+    """A layer with correlated, unevenly scaled input channels and its
+    calibration activations (the shape of the GPTQ tests' layer,
+    tests/test_gptq.py:13-18): W ~ N(0, 0.05^2), X = N(0,1) @ (I + G/sqrt(K))
+    with per-channel log-normal scales."""
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    mix = rng.standard_normal((K, K)) / np.sqrt(K) + np.eye(K)
+    X = (rng.standard_normal((T, K)) @ mix * np.exp(rng.standard_normal(K) * 0.5)).astype(np.float32)
+    return W, X

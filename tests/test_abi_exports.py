@@ -50,3 +50,18 @@ def test_invalid_arguments_fail_without_gpu(lib):
     rc = lib.mtc_gemv(None, None, 1, 1, None, None, None, 1, 0, None, 0, None, None, None)
     assert rc == _lib.MTC_ERR_INVALID
     assert b"null" in lib.mtc_last_error()
+
+
+def test_library_records_its_source_hash(lib):
+    """The built library carries the hash of the sources it was built from,
+    so a stale prebuilt library next to changed sources is rebuilt."""
+    assert build.library_hash() == build.source_hash()
+    assert not build.needs_build()
+
+
+def test_wait_limit_and_hold_arguments(lib):
+    """The timeout diagnostics validate their arguments without a GPU."""
+    assert lib.mtc_debug_withhold_bytes(8) == _lib.MTC_ERR_INVALID
+    assert lib.mtc_debug_withhold_bytes(8192) == _lib.MTC_ERR_INVALID
+    assert lib.mtc_debug_withhold_bytes(0) == 0
+    assert lib.mtc_set_wait_limit_ns(0) == 0

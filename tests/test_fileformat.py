@@ -311,6 +311,23 @@ def test_strip_stream_of_another_version_is_rebuilt(golden_dir, tmp_path):
     assert r.__dict__.get("_host_strip") is None  # ignored, built again on first use
 
 
+def test_strip_stream_of_another_form_is_rebuilt(golden_dir, tmp_path):
+    """A saved wide stream, or one with larger batch records, is not the
+    default form: the file loads and the default stream is built again on
+    first use instead of failing."""
+    from tensorpack_b200 import _lib
+    from tensorpack_b200.core import strip
+
+    m = qtp_matrix(golden_dir)[0]
+    for name, edit in (("wide", lambda meta: meta.update(flags=_lib.STRIP_WIDE)),
+                       ("big", lambda meta: meta.update(max_batch_bytes=2 * strip.BATCH_BYTES))):
+        p = tmp_path / f"{name}.mtcpk"
+        _save_with_strip(p, m, edit_meta=edit)
+        r = MTCMatrix.load(p)
+        assert r.__dict__.get("_host_strip") is None, name
+        assert np.array_equal(r.host_strip().stream, strip.build_host(r).stream)
+
+
 def test_damaged_strip_stream_rejected(golden_dir, tmp_path):
     """A strip record that matches its checksum but fails the validator (a
     consistent-looking but wrong file) raises instead of being used."""

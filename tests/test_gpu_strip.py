@@ -165,3 +165,58 @@ def test_strip_gate_shape_matches_tensor_decode(dev):
         ds.check_status()
         e = O.relative_frobenius_error(Yt.cpu().numpy().astype(np.float64), Ys.cpu().numpy())
         assert e < 1e-3, (M, e)
+
+
+def run_form(m, X, dev, wide=False, merge_modes=False, batch_bytes=None):
+    """The decode through a non-default strip form of the same matrix."""
+    import ctypes
+
+    import torch
+
+    from tensorpack_b200 import _lib
+
+    ds = m.device_stream(dev)
+    sp = ds.strip(wide=wide, merge_modes=merge_modes, batch_bytes=batch_bytes)
+    Xd = torch.from_numpy(np.ascontiguousarray(X, dtype=np.float32)).to(dev)
+    Y = torch.full((X.shape[0], m.shape[1]), float("nan"), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.mtc_strip_decode(ctypes.byref(sp.desc_for(X.shape[0])), Xd.data_ptr(), X.shape[0], Xd.stride(0),
+                                    None if ds.row_perm is None else ds.row_perm.data_ptr(),
+                                    None if ds.col_perm is None else ds.col_perm.data_ptr(), Y.data_ptr(),
+                                    Y.stride(0), ds.status.data_ptr(), None,
+                                    torch.cuda.current_stream(dev).cuda_stream), "strip decode")
+    torch.cuda.synchronize()
+    ds.check_status()
+    return Y.cpu().numpy(), sp.host.exp2
+
+
+@pytest.mark.parametrize("form", ["wide", "merge", "wide+merge", "small-batches"])
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_strip_forms_match_emulation(dev, form, M):
+    """The wide group steps, the merged decoder classes and 2 KB batch
+    records give the same products as the default form: within 1e-5 of the
+    exact emulation and 2e-3 of the reference dequant, on the forced
+    all-modes fixture (every mode at every leaf edge) and the permuted
+    LLM-like layer."""
+    from tensorpack_b200.kernels.gemm import MTCMatrix
+
+    kw = {"wide": {"wide": True}, "merge": {"merge_modes": True}, "wide+merge": {"wide": True, "merge_modes": True},
+          "small-batches": {"batch_bytes": 2048}}[form]
+    m, deq = forced()
+    X = np.random.default_rng(M + 30).standard_normal((M, 256)).astype(np.float32)
+    for mat, d, x in [(m, deq, X)]:
+        Y, e2 = run_form(mat, x, dev, **kw)
+        emul, _ = emulated_product(mat, d, x, e2)
+        assert O.relative_frobenius_error(emul, Y) < TOL_EMUL
+        assert O.relative_frobenius_error(x.astype(np.float64) @ d.astype(np.float64), Y) < TOL_REF
+    g, inner = _qt(os.path.join(os.path.dirname(__file__), "golden"), "llm_like_256x512.npz", "b4.25_inner_")
+    W, _ = inputs.llm_like(256, 512, seed=1)
+    pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
+    m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
+    stored = O.quadtree_dequant(W[pr][:, pc], inner.sizes, inner.leaf, inner.modes, inner.scales)
+    deq = O.unpermute(stored, pr, pc)
+    X = inputs.llm_activations(M, 256, seed=M + 3, outlier_seed=1)
+    Y, e2 = run_form(m, X, dev, **kw)
+    emul, _ = emulated_product(m, deq, X, e2)
+    assert O.relative_frobenius_error(emul, Y) < TOL_EMUL
+    assert O.relative_frobenius_error(X.astype(np.float64) @ deq.astype(np.float64), Y) < TOL_REF

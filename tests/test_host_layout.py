@@ -148,3 +148,32 @@ def test_unsupported_level_rejected():
                              {64: np.ones((1, 1), np.float32), 32: np.zeros((2, 2), np.float32)}, None, 0)
     with pytest.raises(ValueError):
         MTCMatrix.from_qt_allocation(np.zeros((64, 64), np.float32), a)
+
+
+def gptq_fixture(golden_dir):
+    """GPTQ codes on an MTC-QT-P grid, made by the reference
+    (tests/golden/make_gptq_fixture.py): allocation, stored-order codes and
+    the SHA-256 of the reference's dequantised GPTQ result."""
+    g = load(golden_dir, "gptq_qtp_256.npz")
+    sizes = tuple(int(s) for s in g["sizes"])
+    inner = O.QuadtreeAllocation(sizes, {s: g[f"leaf_{s}"] for s in sizes}, {s: g[f"modes_{s}"] for s in sizes},
+                                 {s: g[f"scales_{s}"] for s in sizes}, None, 0)
+    a = O.PermutedAllocation(inner, g["row_perm"], g["col_perm"], None, int(g["total_bits"]))
+    W, X = inputs.gptq_layer(256, 256, seed=0)
+    return g, a, W, X
+
+
+def test_gptq_codes_pack_to_the_reference_result(golden_dir):
+    """Explicit (non-RTN) codes are packed as given: decoding the arena and
+    undoing the permutation reproduces the reference's GPTQ output bit for
+    bit (mtc/baselines/gptq.py:39-138 inside qt_element_grid)."""
+    import hashlib
+
+    g, a, W, _ = gptq_fixture(golden_dir)
+    assert int(g["codes_differ_from_rtn"]) > 1000
+    m = MTCMatrix.from_qt_allocation(W, a, codes=g["codes_stored"])
+    Q = O.unpermute(decode_arena(m), g["row_perm"], g["col_perm"])
+    assert hashlib.sha256(np.ascontiguousarray(Q).tobytes()).hexdigest() == str(g["Q_sha"])
+    # the RTN packing of the same grid is a different matrix
+    rtn = O.unpermute(decode_arena(MTCMatrix.from_qt_allocation(W, a)), g["row_perm"], g["col_perm"])
+    assert not np.array_equal(rtn, Q)

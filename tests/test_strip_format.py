@@ -191,10 +191,12 @@ def test_stream_bytes_near_accounted(golden_dir):
     assert ratio < 1.25, ratio
 
 
-@pytest.mark.parametrize("target", [1, 5, 13, 64, 148, 400])
-def test_cta_partition_covers_and_balances(golden_dir, target):
-    """Ranges of whole strips cover the stream in order, respect the batch
-    cap, and no range exceeds the mean by more than one strip."""
+@pytest.mark.parametrize("n_cta,n_warps", [(1, 1), (5, 16), (13, 4), (64, 16), (148, 16), (400, 24)])
+def test_schedule_covers_and_balances(golden_dir, n_cta, n_warps):
+    """The static schedule hands every batch record to exactly one warp,
+    each warp's items are one strip after another, the flush bit closes
+    every segment with its own slot, and each CTA's reduction table lists
+    its strips with the slot ranges of their segments in order."""
     from tensorpack_b200.core import strip
     from tensorpack_b200.kernels.gemm import MTCMatrix
 
@@ -203,22 +205,51 @@ def test_cta_partition_covers_and_balances(golden_dir, target):
     pr, pc = g["b4.25_row_perm"], g["b4.25_col_perm"]
     m = MTCMatrix.from_qt_allocation(W, O.PermutedAllocation(inner, pr, pc, None, int(g["b4.25_total_bits"])))
     hs = strip.build_host(m, batch_bytes=2048)
-    for cap in (strip.CTA_BATCHES, 3):
-        part, n, most = hs.partition(target, max_batches=cap)
-        s_, b_ = part[0::2].astype(np.int64), part[1::2].astype(np.int64)
-        assert len(s_) == n + 1 and s_[0] == 0 and b_[0] == 0
-        assert s_[-1] == hs.n_strips and b_[-1] == hs.n_batches
-        assert (np.diff(s_) >= 1).all() and np.array_equal(b_, hs.strip_batch[s_].astype(np.int64))
-        nb = np.diff(b_)
-        assert most == nb.max()
-        single = np.diff(s_) == 1
-        assert ((nb <= cap) | single).all()
-        if cap == strip.CTA_BATCHES:
-            assert n <= target
-            off = hs.batch_off.astype(np.int64)
-            cta_bytes = off[b_[1:]] - off[b_[:-1]]
-            strip_bytes = np.diff(off[hs.strip_batch.astype(np.int64)])
-            assert cta_bytes.max() <= off[-1] / n + strip_bytes.max()
+    sc = hs.schedule(n_cta, n_warps)
+    n_cta = min(n_cta, hs.n_strips)
+    assert sc.n_cta == n_cta and sc.warp_work.size == n_cta * n_warps + 1
+    assert sc.warp_work[0] == 0 and sc.warp_work[-1] == hs.n_batches and (np.diff(sc.warp_work.astype(np.int64)) >= 0).all()
+    off = sc.work[0::2].astype(np.int64)
+    w1 = sc.work[1::2].astype(np.int64)
+    nbytes, slot, flush = (w1 & 0xFFF) << 4, (w1 >> 12) & 0x7FFFF, w1 >> 31
+    bo = hs.batch_off.astype(np.int64)
+    batch_of = {int(o): b for b, o in enumerate(bo[:-1])}
+    batches = np.array([batch_of[int(o)] for o in off])
+    assert np.array_equal(np.sort(batches), np.arange(hs.n_batches))       # every record exactly once
+    assert np.array_equal(nbytes, bo[batches + 1] - bo[batches])
+    strip_of = np.searchsorted(hs.strip_batch.astype(np.int64), batches, side="right") - 1
+    assert sc.cta_red[0] == 0 and sc.cta_red[-1] == hs.n_strips
+    seen = np.zeros(hs.n_strips, np.int64)
+    for c in range(n_cta):
+        items = range(int(sc.warp_work[c * n_warps]), int(sc.warp_work[(c + 1) * n_warps]))
+        red = sc.red.reshape(-1, 3)[sc.cta_red[c]:sc.cta_red[c + 1]]
+        seen[red[:, 0]] += 1
+        expect = {}
+        for w in range(n_warps):
+            lo, hi = int(sc.warp_work[c * n_warps + w]), int(sc.warp_work[c * n_warps + w + 1])
+            for i in range(lo, hi):
+                last = i + 1 == hi or strip_of[i + 1] != strip_of[i]
+                assert flush[i] == (1 if last else 0)
+                if last:
+                    expect.setdefault(int(strip_of[i]), []).append(int(slot[i]))
+                if i > lo and strip_of[i] == strip_of[i - 1]:
+                    assert slot[i] == slot[i - 1] and batches[i] == batches[i - 1] + 1
+        got = {int(s): list(range(int(f), int(f) + int(n))) for s, f, n in red}
+        assert got == expect
+        slots = [x for v in expect.values() for x in v]
+        assert sorted(slots) == list(range(len(slots))) and len(slots) <= sc.max_slots
+        assert set(int(s) for s in strip_of[list(items)]) == set(got)
+    assert (seen == 1).all()
+
+
+def test_schedule_rejects_bad_sizes():
+    from tensorpack_b200.core import strip
+
+    hs = _llm_host()
+    with pytest.raises(ValueError, match="bad sizes"):
+        hs.schedule(1, 0)
+    with pytest.raises(ValueError, match="bad sizes"):
+        hs.schedule(1, 33)
 
 
 def _llm_host(batch_bytes=2048):
@@ -269,15 +300,15 @@ def test_validator_rejects_damaged_streams(damage):
 
 
 def test_decode_rejects_bad_arguments_without_a_gpu():
-    """Argument and partition checks come before any CUDA call."""
+    """Argument and schedule checks come before any CUDA call."""
     import ctypes
 
     from tensorpack_b200 import _lib
 
     lib = _lib.load()
     hs = _llm_host()
-    part, n, most = hs.partition(4)
-    d = hs.desc(16, 16, 16, part, n, most)  # fake device pointers: nothing is launched
+    sc = hs.schedule(4)
+    d = hs.desc(16, 16, 16, sc, [16, 16, 16, 16])  # fake device pointers: nothing is launched
     X = Y = 16
 
     def call(desc, M=1, ldx=256, ldy=512):
@@ -288,13 +319,16 @@ def test_decode_rejects_bad_arguments_without_a_gpu():
     assert call(d, ldx=255) == _lib.MTC_ERR_INVALID
     bad = _lib.StripDesc.from_buffer_copy(d)
     bad.n_cta = 0
-    assert call(bad) == _lib.MTC_ERR_INVALID
-    short = part.copy()
-    short[-2] -= 1  # ranges no longer reach the last strip
-    bad = hs.desc(16, 16, 16, short, n, most)
-    assert call(bad) == _lib.MTC_ERR_INVALID and b"partition" in lib.mtc_last_error()
-    bad = hs.desc(16, 16, 16, part, n, 1)  # a range with more batches than max_cta_batches
-    assert call(bad) == _lib.MTC_ERR_INVALID
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"schedule" in lib.mtc_last_error()
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.n_warps = 40
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"schedule" in lib.mtc_last_error()
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.max_cta_slots = 0
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"max_cta_slots" in lib.mtc_last_error()
+    bad = _lib.StripDesc.from_buffer_copy(d)
+    bad.work = None
+    assert call(bad) == _lib.MTC_ERR_INVALID and b"null" in lib.mtc_last_error()
     bad = _lib.StripDesc.from_buffer_copy(d)
     bad.stream = 8  # not 16-byte aligned
     assert call(bad) == _lib.MTC_ERR_INVALID
@@ -423,8 +457,7 @@ def test_strip_fits_shared_memory_limits():
 
     lib = _lib.load()
     hs = _llm_host()
-    part, n, most = hs.partition(4)
-    d = hs.desc(16, 16, 16, part, n, most)
+    d = hs.desc(16, 16, 16, hs.schedule(4), [16, 16, 16, 16])
     for M in (1, 2, 3, 4):
         assert lib.mtc_strip_fits(ctypes.byref(d), M) == 1
     assert lib.mtc_strip_fits(ctypes.byref(d), 0) == 0 and lib.mtc_strip_fits(ctypes.byref(d), 5) == 0
