@@ -51,6 +51,7 @@ struct StripParams {
   Epi ep;
   unsigned long long timeout_ns;
   uint32_t withhold;      // diagnostic: bytes expected but never copied on each warp's first batch
+  int staged;             // X rows and pr arrive by bulk copy and are permuted in shared memory
   int nw, ns, max_slots;  // warps, slots per warp, partial-sum slots per CTA
   uint32_t slot_bytes;
   uint32_t off_x, off_scr, off_part, off_slots;  // shared-memory layout
@@ -280,7 +281,7 @@ __device__ __forceinline__ void flush(Acc<MT, WIDE>& A, int lane, float* scr, fl
 }
 
 template <int MT, bool WIDE>
-__global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const StripParams p) {
+__global__ void __launch_bounds__(MT == 1 ? (WIDE ? 768 : 1024) : 512, 1) strip_kernel(const StripParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nw = p.nw, ns = p.ns;
@@ -289,8 +290,12 @@ __global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const Str
   uint16_t* x16 = reinterpret_cast<uint16_t*>(smem + p.off_x);
   float* scr = reinterpret_cast<float*>(smem + p.off_scr) + warp * (MT * (WIDE ? 104 : 40));
   float* part = reinterpret_cast<float*>(smem + p.off_part);  // [max_slots][MT][8]
-  uint8_t* slots = smem + p.off_slots + (size_t)warp * ns * p.slot_bytes;
+  // slot k of warp w at off_slots + (k nw + w) slot_bytes: slot 1 of every
+  // warp is one contiguous region, the staging area of the activations
+  uint8_t* slots = smem + p.off_slots + (size_t)warp * p.slot_bytes;
+  const size_t slot_stride = (size_t)nw * p.slot_bytes;
   __shared__ int cta_abort;
+  __shared__ __align__(8) uint64_t xbar;
 
   const uint32_t w0 = __ldg(p.warp_work + c * nw + warp), w1 = __ldg(p.warp_work + c * nw + warp + 1);
   // lane 0 keeps the work entries of the slots: word 1 of item w0 + k in slot k
@@ -308,10 +313,23 @@ __global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const Str
     // `extra` > 0 only under mtc_debug_withhold_bytes: the phase then never
     // completes and the bounded wait on it runs out
     mbar_expect_tx(&bar[s], bytes + extra);
-    bulk_g2s(slots + (size_t)s * p.slot_bytes, p.stream + off, bytes, &bar[s]);
+    bulk_g2s(slots + (size_t)s * slot_stride, p.stream + off, bytes, &bar[s]);
     issued |= 1u << s;
   };
   if (tid == 0) cta_abort = 0;
+  float* xs = reinterpret_cast<float*>(smem + p.off_slots + slot_stride);  // staging: the slot-1 region
+  const int32_t* prs = reinterpret_cast<const int32_t*>(xs + (size_t)p.M * p.K);
+  if (p.staged && tid == 0) {
+    // X rows and pr go out before any weight copy: they are L2 hits and
+    // must not queue behind the first batches of every SM
+    const uint32_t row = (uint32_t)p.K * 4u;
+    mbar_init(&xbar, 1);
+    fence_barrier_init();
+    mbar_expect_tx(&xbar, row * (uint32_t)(p.M + (p.pr ? 1 : 0)));
+    for (int m = 0; m < p.M; ++m) bulk_g2s(xs + (size_t)m * p.K, p.X + (long long)m * p.ldx, row, &xbar);
+    if (p.pr) bulk_g2s(const_cast<int32_t*>(prs), p.pr, row, &xbar);
+  }
+  __syncthreads();
   uint32_t off0[kMaxSlots];
   if (lane == 0) {
 #pragma unroll
@@ -328,6 +346,39 @@ __global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const Str
     if (w0 < w1) issue(0, off0[0], ent[0], p.withhold);
   }
 
+  if (p.staged) {
+    // the activations were staged by bulk copy into the slot-1 region (not
+    // yet in use); the permutation runs in shared memory, so 148 CTAs do not
+    // each pull the scattered sectors of X[:, pr] from L2
+    if (tid == 0) {
+      if (!mbar_wait(&xbar, 0u, p.timeout_ns)) {
+        atomicOr(p.status, MTC_STATUS_TIMEOUT);
+        cta_abort = 1;
+        (void)mbar_wait(&xbar, 0u, 10000000ull);  // let the copy land before the CTA exits
+      }
+    }
+    __syncthreads();
+    if (!cta_abort) {
+      uint32_t xbad = 0;
+      for (int k = tid; k < p.kpad; k += blockDim.x) {
+        const int src = k < p.K ? (p.pr ? prs[k] : k) : -1;
+        const bool ok = src >= 0 && src < p.K;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const float v = (m < p.M && ok) ? xs[(size_t)m * p.K + src] : 0.0f;
+          if (!(fabsf(v) <= 65504.0f)) xbad = 1;
+          x16[(size_t)m * p.kpad + k] = f2h(v);
+        }
+      }
+      if (xbad) atomicOr(p.status, MTC_STATUS_X_RANGE);
+    }
+    __syncthreads();  // the staging area is read: slot 1 may be filled
+    if (lane == 0 && !cta_abort) {
+#pragma unroll
+      for (int k = 1; k < kMaxSlots; ++k)
+        if (k < ns && w0 + k < w1) issue(k, off0[k], ent[k], 0u);
+    }
+  } else {
   // X[:, pr] as fp16 for every token row (zero beyond M and K).  A thread's
   // source indices, then its activations, are loaded for all of its columns
   // of a pass before anything is stored, and the remaining weight copies are
@@ -383,13 +434,14 @@ __global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const Str
     if (xbad) atomicOr(p.status, MTC_STATUS_X_RANGE);
   }
   __syncthreads();
+  }
 
   Acc<MT, WIDE> A;
   A.zero();
   uint32_t parity = 0;
   int slot = 0;
-  bool abort = false;
-  for (uint32_t i = w0; i < w1; ++i) {
+  bool abort = cta_abort != 0;
+  for (uint32_t i = w0; i < w1 && !abort; ++i) {
     // the slot's next item, fetched now and used after this batch
     uint32_t noff = 0, nent = 0;
     const uint32_t ni = i + (uint32_t)ns;
@@ -414,7 +466,7 @@ __global__ void __launch_bounds__(MT == 1 ? 768 : 512, 1) strip_kernel(const Str
     }
     e1 = __shfl_sync(0xffffffffu, e1, 0);
     parity ^= 1u << slot;
-    const uint8_t* base = slots + (size_t)slot * p.slot_bytes;
+    const uint8_t* base = slots + (size_t)slot * slot_stride;
     // records are validated on the host before upload; this check keeps a
     // damaged record from reading beyond its slot
     if (strip::pad16(8 + 4 * (int)ldu32(base + 4)) > (int)((e1 & 0xFFFu) << 4)) {
@@ -475,7 +527,7 @@ struct Plan {
 bool make_plan(const mtc_strip_desc* s, int M, bool wide, Plan* pl) {
   if (M < 1 || M > (wide ? 2 : kMaxM)) return false;
   pl->mt = M == 1 ? 1 : M == 2 ? 2 : 4;
-  const int max_nw = pl->mt == 1 ? 24 : 16;
+  const int max_nw = pl->mt == 1 ? (wide ? 24 : 32) : 16;
   if (s->n_warps < 1 || s->n_warps > max_nw) return false;
   pl->nw = s->n_warps;
   pl->slot_bytes = (s->max_batch_bytes + 127u) & ~127u;
@@ -567,6 +619,12 @@ extern "C" int mtc_strip_decode(const mtc_strip_desc* s, const float* X, int32_t
     p.ep = Epi{e.bias, e.act};
     p.timeout_ns = wait_limit_ns();
     p.withhold = m0 == 0 ? take_withheld_bytes() : 0u;
+    // activations by bulk copy when rows and permutation are 16-byte
+    // aligned and they fit the slot-1 region of every warp
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(p.X), pa = reinterpret_cast<uintptr_t>(row_perm);
+    const size_t stage = (size_t)(Mi + (row_perm ? 1 : 0)) * (size_t)s->K * 4;
+    p.staged = (xa & 15) == 0 && (ldx & 3) == 0 && (pa & 15) == 0 && (s->K & 3) == 0 &&
+               stage <= (size_t)pl.nw * pl.slot_bytes && stage < (1u << 20);
     p.nw = pl.nw;
     p.ns = pl.ns;
     p.max_slots = (int)s->max_cta_slots;

@@ -510,14 +510,51 @@ extern "C" int mtc_strip_check(const uint8_t* stream, uint64_t stream_bytes, con
 __host__ inline int sched_step_cost(uint32_t d, bool wide) {
   const int kind = desc_kind(d);
   if (kind == kGeneric) return 170;
-  static const int group_cost[6] = {36, 40, 36, 50, 46, 40};  // P2, P3, P4, P5, P6, P8
-  static const int micro_cost[6] = {40, 46, 39, 61, 50, 45};
+  static const int group_cost[6] = {30, 50, 28, 42, 42, 30};  // P2, P3, P4, P5, P6, P8
+  static const int micro_cost[6] = {32, 40, 32, 40, 40, 32};
   int body = kind < kU2 ? group_cost[kind] : micro_cost[kind - kU2];
   if (wide && kind < kU2) body = body * 3 / 2;  // two micro-blocks per lane, one x load
   return body;
 }
-constexpr int kSchedBatchCost = 48;
-constexpr int kSchedDispatchCost = 66;
+constexpr int kSchedBatchCost = 50;
+constexpr int kSchedDispatchCost = 83;
+
+// Cut costs c[0..n) into `parts` contiguous ranges whose largest sum is as
+// small as possible (binary search on that sum, greedy fill); cut[w] is the
+// first element of range w, cut[parts] = n.
+__host__ inline void optimal_cuts(const std::vector<uint64_t>& c, int parts, std::vector<size_t>* cut) {
+  const size_t n = c.size();
+  uint64_t lo = 0, hi = 0;
+  for (uint64_t v : c) lo = std::max(lo, v), hi += v;
+  auto fits = [&](uint64_t cap) {
+    int used = 1;
+    uint64_t acc = 0;
+    for (uint64_t v : c) {
+      if (acc + v > cap) {
+        ++used;
+        acc = 0;
+      }
+      acc += v;
+    }
+    return used <= parts;
+  };
+  while (lo < hi) {
+    const uint64_t mid = lo + (hi - lo) / 2;
+    if (fits(mid)) hi = mid;
+    else lo = mid + 1;
+  }
+  cut->assign(parts + 1, n);
+  (*cut)[0] = 0;
+  int w = 1;
+  uint64_t acc = 0;
+  for (size_t i = 0; i < n && w < parts; ++i) {
+    if (acc + c[i] > lo) {
+      (*cut)[w++] = i;
+      acc = 0;
+    }
+    acc += c[i];
+  }
+}
 
 namespace {
 int schedule_impl(const uint8_t* stream, const uint32_t* batch_off, const uint32_t* strip_batch, int n_strips,
@@ -561,20 +598,11 @@ int schedule_impl(const uint8_t* stream, const uint32_t* batch_off, const uint32
     std::vector<uint32_t> seq;  // batches of this CTA in order
     for (int s : st)
       for (uint32_t b = strip_batch[s]; b < strip_batch[s + 1]; ++b) seq.push_back(b);
-    const uint64_t total = load[c];
-    // cut seq into n_warps contiguous ranges at the batch boundary nearest each target
-    std::vector<size_t> cut(n_warps + 1, seq.size());
-    cut[0] = 0;
-    {
-      uint64_t acc = 0;
-      size_t i = 0;
-      for (int w = 1; w < n_warps; ++w) {
-        const uint64_t target = total * (uint64_t)w / (uint64_t)n_warps;
-        while (i < seq.size() && acc + bcost[seq[i]] <= target) acc += bcost[seq[i++]];
-        if (i < seq.size() && target - acc > acc + bcost[seq[i]] - target) acc += bcost[seq[i++]];
-        cut[w] = i;
-      }
-    }
+    // cut seq into n_warps contiguous ranges, the costliest as cheap as possible
+    std::vector<uint64_t> sc(seq.size());
+    for (size_t i = 0; i < seq.size(); ++i) sc[i] = bcost[seq[i]];
+    std::vector<size_t> cut;
+    optimal_cuts(sc, n_warps, &cut);
     // work items and flush slots: a segment is one warp's run of one strip
     uint32_t slot = 0;
     std::vector<uint32_t> strip_first(st.size(), 0), strip_cnt(st.size(), 0);
