@@ -514,13 +514,15 @@ def main():
             gemm_step()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         barrier()
-        with ClockSampler(local_rank) as clocks:
-            for i in range(args.steps):
-                flush.zero_()
-                ev[i][0].record(stream)
-                gemm_step()
-                ev[i][1].record(stream)
-            barrier()
+        # clocks sampled every millisecond over both timed prefill loops
+        # (the step and the kernel alone)
+        clocks = ClockSampler(local_rank, period_s=0.001).__enter__()
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            gemm_step()
+            ev[i][1].record(stream)
+        barrier()
         step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps)
         value = flops / (step_ms * 1e-3) / 1e12
         for ds in streams:
@@ -536,6 +538,7 @@ def main():
                 ds.prefill_gemm(Mp, Y[j])
                 kev[i][j][1].record(stream)
         barrier()
+        clocks.__exit__(None, None, None)
         kern_ms = max_over_ranks(sum(a.elapsed_time(b) for row in kev for a, b in row) / args.steps)
         achieved = local_flops / (kern_ms * 1e-3) / 1e12
         if args.only == "prefill":

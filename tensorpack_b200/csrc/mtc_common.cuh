@@ -645,6 +645,15 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// Programmatic dependent launch (kernels launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization): the next kernel in the
+// stream may start once every CTA of this one has called launch_dependents;
+// griddep_wait blocks until the previous kernel has completed and its memory
+// is visible.  Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

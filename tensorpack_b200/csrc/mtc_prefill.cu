@@ -72,6 +72,13 @@ struct PrefillParams {
   long long ldy;
   uint32_t* status;
   int n_bands, n_tiles, nkb;
+  // Split tail: tiles [t_main, n_tiles) (the last, partial wave) are cut
+  // along K into `split` pieces each; piece j (cluster j < n_pieces) covers
+  // k blocks [s nkb / split, (s + 1) nkb / split) of tile t_main + j / split,
+  // s = j % split, and leaves its partial sums in part[j] (CBM x BN fp32,
+  // row-major), which prefill_tail_reduce adds up.  n_pieces = 0: no split.
+  int t_main, split, n_pieces;
+  float* part;
   int SA, SB;         // A-tile and W-tile pipeline depths
   int vec2;           // Y rows 8-byte aligned: float2 stores
   uint32_t ring_bytes;
@@ -82,6 +89,34 @@ struct PrefillParams {
 
 __device__ __forceinline__ void flag(uint32_t* st, uint32_t bits) {
   if (st) atomicOr(st, bits);
+}
+
+// The work of one cluster, in the order every role walks it: its whole tiles
+// t = cid, cid + G, ... below t_main, then at most one tail piece.
+struct Item {
+  int tile, kb0, kb1, piece;  // piece < 0: a whole tile
+};
+__device__ __forceinline__ int regular_items(const PrefillParams& p, int cid, int G) {
+  return cid < p.t_main ? (p.t_main - 1 - cid) / G + 1 : 0;
+}
+__device__ __forceinline__ int item_count(const PrefillParams& p, int cid, int G) {
+  return regular_items(p, cid, G) + (cid < p.n_pieces ? 1 : 0);
+}
+__device__ __forceinline__ Item item_of(const PrefillParams& p, int cid, int G, int i) {
+  Item w;
+  if (i < regular_items(p, cid, G)) {
+    w.tile = cid + i * G;
+    w.kb0 = 0;
+    w.kb1 = p.nkb;
+    w.piece = -1;
+  } else {
+    const int sp = cid % p.split;
+    w.tile = p.t_main + cid / p.split;
+    w.kb0 = sp * p.nkb / p.split;
+    w.kb1 = (sp + 1) * p.nkb / p.split;
+    w.piece = cid;
+  }
+  return w;
 }
 
 
@@ -155,9 +190,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // from the odd one); the bytes count on the even CTA's barrier.
     if (lane == 0) {
       uint32_t it = 0;
-      for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters) {
-        const int mblk = tile / p.n_bands;
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+      const int n_items = item_count(p, cid, n_clusters);
+      for (int ii = 0; ii < n_items && !flags[0]; ++ii) {
+        const Item w = item_of(p, cid, n_clusters, ii);
+        const int mblk = w.tile / p.n_bands;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int sa = it % p.SA;
           if (it >= (uint32_t)p.SA && !mbar_wait(&empty_a[sa], ((it / p.SA) & 1) ^ 1, p.timeout_ns)) {
             flags[0] = 1;
@@ -177,17 +214,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // offset) of 32 sub-stages at a time into shared memory, one chunk ahead
     // of lane 0, which issues the bulk copies; so lane 0 never waits on a
     // global load.
-    const int n_my_tiles = cid < p.n_tiles ? (p.n_tiles - 1 - cid) / n_clusters + 1 : 0;
+    // chunks of kMetaChunk sub-stages: ceil(nkb / kMetaChunk) per whole
+    // tile, then those of the tail piece
+    const int n_reg = regular_items(p, cid, n_clusters);
     const int chunks_per_tile = (p.nkb + kMetaChunk - 1) / kMetaChunk;
-    const int n_chunks = n_my_tiles * chunks_per_tile;
+    const Item tail = item_of(p, cid, n_clusters, n_reg);  // meaningful when cid < n_pieces
+    const int tail_chunks = cid < p.n_pieces ? (tail.kb1 - tail.kb0 + kMetaChunk - 1) / kMetaChunk : 0;
+    const int n_chunks = n_reg * chunks_per_tile + tail_chunks;
+    // chunk q -> its item and k-block range [kb0, kb1)
+    auto chunk_of = [&](int q, int& tile, int& kb0, int& kb1) {
+      if (q < n_reg * chunks_per_tile) {
+        tile = cid + (q / chunks_per_tile) * n_clusters;
+        kb0 = (q % chunks_per_tile) * kMetaChunk;
+        kb1 = min(p.nkb, kb0 + kMetaChunk);
+      } else {
+        tile = tail.tile;
+        kb0 = tail.kb0 + (q - n_reg * chunks_per_tile) * kMetaChunk;
+        kb1 = min(tail.kb1, kb0 + kMetaChunk);
+      }
+    };
     uint4 nxt0, nxt1;
     auto load_chunk = [&](int q) {
-      const int tile = cid + (q / chunks_per_tile) * n_clusters;
+      int tile = 0, kc0 = 0, kc1 = 0;
+      if (q < n_chunks) chunk_of(q, tile, kc0, kc1);
       const int band = tile % p.n_bands;
-      const int kb = (q % chunks_per_tile) * kMetaChunk + lane;
+      const int kb = kc0 + lane;
       nxt0 = make_uint4(0u, 0u, 0u, 0u);
       nxt1 = make_uint4(0u, 0u, 0u, 0u);
-      if (q < n_chunks && kb < p.nkb) {
+      if (q < n_chunks && kb < kc1) {
         const size_t sub = (size_t)(2 * band + (int)rank) * p.nkb + kb;
         nxt0 = *reinterpret_cast<const uint4*>(s.stage_ranges + 4 * sub);
         nxt1 = make_uint4(s.stage_counts[sub], s.stage_offsets[sub], 0u, 0u);
@@ -208,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int q = 0; q < n_chunks; ++q) {
       load_chunk(q + 1);                              // in flight while lane 0 issues chunk q
       if (lane == 0) {
-        const int kb0 = (q % chunks_per_tile) * kMetaChunk;
-        const int kb1 = min(p.nkb, kb0 + kMetaChunk);
+        int ctile, kb0, kb1;
+        chunk_of(q, ctile, kb0, kb1);
         for (int kb = kb0; kb < kb1 && !flags[0]; ++kb, ++it) {
           // The sub-stage goes to the byte ring as one contiguous piece:
           // descriptors (128 B) | work list | row-0 records | row-1 records.
@@ -275,13 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(256, BN);
       uint32_t it = 0, tcount = 0;
-      for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters, ++tcount) {
+      const int n_items = item_count(p, cid, n_clusters);
+      for (int ii = 0; ii < n_items && !flags[0]; ++ii, ++tcount) {
+        const Item w = item_of(p, cid, n_clusters, ii);
         if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1, p.timeout_ns)) {
           flags[0] = 1;
           break;
         }
         tc::fence_after();
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int sa = it % p.SA, sb = it % p.SB;
           if (!mbar_wait(&full_a[sa], (it / p.SA) & 1, p.timeout_ns) ||
               !mbar_wait(&full_b[sb], (it / p.SB) & 1, p.timeout_ns)) {
@@ -294,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bd = tc::smem_desc_k_sw128(b0 + 32 * j);
-            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > w.kb0 || j > 0) ? 1u : 0u;
             tc::mma_f16_ss_pair(tmem, tc::smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
             tc::mma_f16_ss_pair(tmem + 256, tc::smem_desc_k_sw128(a0 + kAHalf + 32 * j), bd, idesc, acc);
           }
@@ -317,8 +373,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int dw = (warp - kDeqWarp0) % kDeqWarps;
     const uint32_t full_b_remote = tc::mapa(full_b, 0);
     uint32_t it = 0;
-    for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters) {
-      for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+    const int n_items = item_count(p, cid, n_clusters);
+    for (int ii = 0; ii < n_items && !flags[0]; ++ii) {
+      const Item w = item_of(p, cid, n_clusters, ii);
+      for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
         if ((int)(it % kDeqGroups) != grp) continue;  // the other group's stage
         const int sb = it % p.SB, ps = it % kRingSlots;
         bool ok = mbar_wait(&pfull[ps], (it / kRingSlots) & 1, p.timeout_ns);
@@ -345,8 +403,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (half = accumulator).
     const uint32_t acc_empty_remote = tc::mapa(acc_empty, 0);
     uint32_t tcount = 0;
-    for (int tile = cid; tile < p.n_tiles && !flags[0]; tile += n_clusters, ++tcount) {
-      const int mblk = tile / p.n_bands, band = tile % p.n_bands;
+    const int n_items = item_count(p, cid, n_clusters);
+    for (int ii = 0; ii < n_items && !flags[0]; ++ii, ++tcount) {
+      const Item w = item_of(p, cid, n_clusters, ii);
+      const int mblk = w.tile / p.n_bands, band = w.tile % p.n_bands;
+      // a tail piece writes its partial sums (CBM x BN, row-major) instead
+      const bool piece = w.piece >= 0;
+      float* const ybase = piece ? p.part + (size_t)w.piece * CBM * BN - ((long long)mblk * CBM * BN + band * BN)
+                                 : p.Y;
+      const long long ld = piece ? BN : p.ldy;
       if (!mbar_wait(acc_full, tcount & 1, p.timeout_ns)) {
         flags[0] = 1;
         break;
@@ -374,17 +439,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int hr = 0; hr < 2; ++hr) {
               const int m = m0 + 8 * hr;
               if (m >= p.M) continue;
-              float* y = p.Y + (long long)m * p.ldy;
+              float* y = ybase + (long long)m * ld;
 #pragma unroll
               for (int r = 0; r < RW; ++r) {
                 const int n = nb + 8 * r;
                 float a = __uint_as_float(v[4 * r + 2 * hr]) * p.inv_pow2e;
                 float b = __uint_as_float(v[4 * r + 2 * hr + 1]) * p.inv_pow2e;
                 if constexpr (EPI) {
-                  if (n < s.N) a = epi_apply(p.ep, a, n);
-                  if (n + 1 < s.N) b = epi_apply(p.ep, b, n + 1);
+                  if (!piece) {
+                    if (n < s.N) a = epi_apply(p.ep, a, n);
+                    if (n + 1 < s.N) b = epi_apply(p.ep, b, n + 1);
+                  }
                 }
-                if (p.vec2 && n + 1 < s.N) {
+                if ((p.vec2 || piece) && n + 1 < s.N) {
                   *reinterpret_cast<float2*>(y + n) = make_float2(a, b);
                 } else {
                   if (n < s.N) y[n] = a;
@@ -412,6 +479,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) {
     tc::fence_after();
     tc::tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// The split tail's partial sums: for the n_tail tiles t_main.., output
+// Y[m][n] = epilogue(sum over s of part[t split + s][m - m0][n - n0]), the
+// pieces added in order (deterministic).  One thread per four columns.
+__global__ void __launch_bounds__(256) prefill_tail_reduce(const float* __restrict__ part, int t_main, int split,
+                                                           int n_tail, int n_bands, int M, int N,
+                                                           float* __restrict__ Y, long long ldy, int vec4, Epi ep) {
+  constexpr int C4 = BN / 4;
+  const long long total = (long long)n_tail * CBM * C4;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c4 = (int)(idx % C4), r = (int)((idx / C4) % CBM), t = (int)(idx / ((long long)C4 * CBM));
+    const int tile = t_main + t, mblk = tile / n_bands, band = tile % n_bands;
+    const int m = mblk * CBM + r, n = band * BN + 4 * c4;
+    if (m >= M || n >= N) continue;
+    const float4* src = reinterpret_cast<const float4*>(part + ((size_t)t * split * CBM + r) * BN) + c4;
+    float4 a = src[0];
+    for (int sp = 1; sp < split; ++sp) {
+      const float4 b = src[(size_t)sp * CBM * C4];
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (n + i < N) v[i] = epi_apply(ep, v[i], n + i);
+    float* y = Y + (long long)m * ldy + n;
+    if (vec4 && n + 3 < N) {
+      *reinterpret_cast<float4*>(y) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (int i = 0; i < 4 && n + i < N; ++i) y[i] = v[i];
+    }
   }
 }
 
@@ -655,6 +755,7 @@ struct PrefillPlan {
   int Kp, Np, nkb, n_mblk, n_bands, n_tiles, SA, SB;
   uint32_t ring_bytes;
   size_t smem, xp_bytes, yp_bytes;
+  size_t part_bytes;  // partial sums of a split tail: one CBM x BN fp32 block per CTA pair of this device
 };
 
 // Compile-time overrides of the pipeline depths (tuning builds only).
@@ -701,6 +802,15 @@ bool plan_prefill(const mtc_stream_desc* s, int M, bool permuted, PrefillPlan* p
   pl->smem = used + ring;
   pl->xp_bytes = ((size_t)M * pl->Kp * 2 + 255) & ~(size_t)255;
   pl->yp_bytes = permuted ? (size_t)M * pl->Np * 4 : 0;
+  pl->part_bytes = 0;
+  int dev = 0, sms = 0;
+  if (pl->nkb >= 4) {
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms >= 4)
+      pl->part_bytes = (size_t)(sms / 2) * CBM * BN * 4;
+    else
+      (void)cudaGetLastError();  // no device here: no split tail, and no error left behind
+  }
   return true;
 }
 
@@ -791,7 +901,7 @@ using namespace mtc;
 extern "C" size_t mtc_prefill_workspace_bytes(const mtc_stream_desc* s, int32_t M, int32_t permuted) {
   PrefillPlan pl;
   if (!s || M <= 0 || !plan_prefill(s, M, permuted != 0, &pl)) return 0;
-  return pl.xp_bytes + pl.yp_bytes;
+  return pl.xp_bytes + pl.yp_bytes + pl.part_bytes;
 }
 
 namespace {
@@ -926,10 +1036,42 @@ extern "C" int mtc_prefill_gemm(const mtc_stream_desc* s, int32_t M, float* Y, i
   MTC_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg),
                  "mtc_prefill_gemm: cluster occupancy");
   MTC_REQUIRE(max_clusters >= 1, "mtc_prefill_gemm: no CTA pair of %zu bytes of shared memory fits", pl.smem);
-  int clusters = pl.n_tiles < max_clusters ? pl.n_tiles : max_clusters;
-  if (s->max_sms >= 2 && clusters > (int)(s->max_sms / 2)) clusters = (int)(s->max_sms / 2);
+  int P = max_clusters;
+  if (s->max_sms >= 2 && P > (int)(s->max_sms / 2)) P = (int)(s->max_sms / 2);
+  // Wave quantisation: the tiles beyond the last whole wave of P pairs
+  // would leave most pairs idle for a whole tile time.  When they fill at
+  // most half a wave they are cut along K into pieces spread over the pairs
+  // (at least two k blocks each), and prefill_tail_reduce adds the pieces.
+  const int R = pl.n_tiles >= P ? pl.n_tiles % P : pl.n_tiles;
+  int S = R > 0 ? P / R : 0;
+  if (S > pl.nkb / 2) S = pl.nkb / 2;
+  if (S > 16) S = 16;
+  const size_t avail = ws_bytes - pl.xp_bytes - pl.yp_bytes;
+  const size_t piece_bytes = (size_t)CBM * BN * 4;
+  if (S >= 2 && (size_t)R * S * piece_bytes <= avail) {
+    p.t_main = pl.n_tiles - R;
+    p.split = S;
+    p.n_pieces = R * S;
+    p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pl.xp_bytes + pl.yp_bytes);
+  } else {
+    p.t_main = pl.n_tiles;
+    p.split = 1;
+    p.n_pieces = 0;
+    p.part = nullptr;
+  }
+  int clusters = p.t_main > 0 ? (p.t_main < P ? p.t_main : P) : 0;
+  if (p.n_pieces > clusters) clusters = p.n_pieces;
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   MTC_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, tmap, p), "mtc_prefill_gemm: launch");
   MTC_CHECK_LAUNCH("mtc_prefill_gemm");
+  if (p.n_pieces > 0) {
+    const int n_tail = p.n_pieces / p.split;
+    const long long threads = (long long)n_tail * CBM * (BN / 4);
+    const int grid = (int)((threads + 255) / 256);
+    const int vec4 = ((p.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15) == 0) ? 1 : 0;
+    prefill_tail_reduce<<<grid, 256, 0, st>>>(p.part, p.t_main, p.split, n_tail, p.n_bands, M, s->N, p.Y, p.ldy,
+                                              vec4, with_ep ? p.ep : Epi{nullptr, 0});
+    MTC_CHECK_LAUNCH("mtc_prefill_gemm: tail reduce");
+  }
   return MTC_OK;
 }

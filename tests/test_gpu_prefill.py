@@ -170,8 +170,10 @@ def test_prefill_many_tiles(dev, K, N, M, permuted):
 def test_host_gemm_pipeline(dev, M, chunk):
     """HostGemm: pinned host X in, host Y out, row chunks overlapped.  Rows
     are independent in the GEMM, so chunks of the prefill kernel give the
-    whole-matrix call's values exactly; a chunk of <= 16 rows goes to the
-    decode kernel (another summation order), held to the tolerance."""
+    whole-matrix call's values up to the summation order: both sum the same
+    fp16 operands, but a tail of tiles cut along K is cut by the tile count
+    of the call (TOL_F16); a chunk of <= 16 rows goes to the decode kernel
+    (another summation order), held to the tolerance."""
     import torch
 
     from tensorpack_b200.kernels.gemm import HostGemm
@@ -187,6 +189,6 @@ def test_host_gemm_pipeline(dev, M, chunk):
     assert O.relative_frobenius_error(ref, Yh.numpy()) < TOL_REF
     whole = prefill(m, X, dev) if M > 16 else None
     if whole is not None and (M % chunk == 0 or M % chunk > 16):
-        np.testing.assert_array_equal(Yh.numpy(), whole)
+        assert O.relative_frobenius_error(whole.astype(np.float64), Yh.numpy()) < TOL_F16
     with pytest.raises(ValueError):
         hg(torch.zeros(4, 255))

@@ -7,9 +7,12 @@ Y[:, pc] with mtc_permute_rows; the exchange goes through NCCL or through
 copy-engine copies into the peers' symmetric-memory buffers.  Every rank
 must hold the full product:
 within the GEMM tolerance of the oracle's fp64 product of the exact dequant.
-The prefill result must also be bit-identical to the unsharded single-GPU
-result (each output tile sums the same k stages in the same order); the
-decode splits K by the number of bands, so only the tolerance applies there.
+The prefill result must also match the unsharded single-GPU result to
+within the accumulation-order bound TOL_F16: each output tile sums the same
+operands, but when the last wave of tiles is cut along K the cut depends on
+the tile count, which differs between a slice and the whole matrix (the
+decode splits K by the number of bands, so there too only the tolerance
+applies).
 Needs two GPUs; skipped otherwise.
 """
 
@@ -72,8 +75,8 @@ def _worker(rank, world, port, golden_dir, out_q, transport):
             full.check_status()
             ref = X.double().cpu().numpy() @ ref_w
             err = O.relative_frobenius_error(ref, Y.cpu().numpy())
-            same = bool(torch.equal(Y, Y1))
-            res.append((M, err, same))
+            diff = float((Y.double() - Y1.double()).norm() / Y1.double().norm())
+            res.append((M, err, diff))
         out_q.put((rank, res, list(sh.plan.cuts)))
     finally:
         dist.destroy_process_group()
@@ -84,7 +87,7 @@ def test_sharded_gemm_on_two_gpus(golden_dir, transport):
     import torch
     import torch.multiprocessing as mp
 
-    from test_gpu_parity import TOL_REF
+    from test_gpu_parity import TOL_F16, TOL_REF
 
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -104,7 +107,7 @@ def test_sharded_gemm_on_two_gpus(golden_dir, transport):
     out = sorted(q.get(timeout=10) for _ in range(world))
     for rank, res, cuts in out:
         assert len(cuts) == world + 1 and cuts[0] == 0 and cuts[-1] == 1024
-        for M, err, same in res:
+        for M, err, diff in res:
             assert err < TOL_REF, (rank, M, err)
             if M > 16:
-                assert same, (rank, M)
+                assert diff < TOL_F16, (rank, M, diff)
